@@ -1,0 +1,394 @@
+#!/usr/bin/env python
+"""Decode-attention benchmark for the B200 attention operator.
+
+A step is one decode step of the whole layer stack's attention op: for every layer, the fused
+append (QK-norm + RoPE + fp16 store of the new K/V) and decode attention over the resident
+fp16 KV cache, for B independent sequences, one new token each.  Default workload: the
+Qwen3-4B shape of BASELINE config 2 (36 layers, 32 q / 8 kv heads, head_dim 128, KV length
+4096, batch 64).  Inputs are seeded synthetic N(0,1) tensors (there is no dataset).
+
+value   = KV bytes read per step (fp16, all layers, all sequences, all ranks) / step time, GB/s,
+          with inputs resident in HBM; CUDA events on the launching stream, max over ranks.
+e2e     = the same metric through the public host API with the step's q/k/v inputs copied from
+          pinned host memory and the attention outputs copied back inside the timed region.
+N > 1   = weak scaling: every rank runs the full per-GPU batch, no communication on the path.
+
+--impl reference times the reference's CPU attention (the C restatement of attentionCpu in
+oracle/, the reference itself being TypeScript with no JavaScript runtime on the box) on the
+host cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # BASELINE config 2 at batch 64 (the north-star target shape).
+    "qwen3-4b": dict(layers=36, Hq=32, Hkv=8, D=128, L=4096, base=1e6, qk_norm=True, batch=64, scale=None,
+                     softcap=0.0, window_even=0, ff=None),
+    # BASELINE config 4.
+    "gemma2-2b": dict(layers=26, Hq=8, Hkv=4, D=256, L=8192, base=1e4, qk_norm=False, batch=32, scale=1 / 16,
+                      softcap=50.0, window_even=4096, ff=None),
+    # BASELINE config 5 on one GPU (the long-context shape; sequence sharding is the multi-GPU form).
+    "llama3.2-1b-long": dict(layers=16, Hq=32, Hkv=8, D=64, L=131072, base=5e5, qk_norm=False, batch=8, scale=None,
+                             softcap=0.0, window_even=0, ff=(32.0, 1.0, 4.0, 8192)),
+}
+
+
+def kv_bytes_per_step(c, batch):
+    """Algorithmic KV bytes one step reads: per layer and sequence, K and V rows of the attended
+    range (the window on windowed layers), Hkv x D fp16 each."""
+    total = 0
+    for layer in range(c["layers"]):
+        keys = c["L"]
+        if c["window_even"] and layer % 2 == 0:
+            keys = min(keys, c["window_even"])
+        total += batch * keys * c["Hkv"] * c["D"] * 2 * 2
+    return total
+
+
+def load_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return float(json.load(fh)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def read_traffic(workload):
+    """dram bytes per decode launch from the committed ncu summary, if one exists."""
+    path = os.path.join(ROOT, "profiles", f"decode_{workload}.md")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip().split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu_index)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=5)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference_sample(c, batch, target_s, threads=0, seed=7):
+    """Time the CPU attention (oracle restatement of attentionCpu) on a bounded sample of the
+    workload: whole (layer, sequence) decode units at the configured KV length, repeated over a
+    pool of 8 sequences until about target_s seconds of work.  Returns (GB/s, threads, desc)."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(seed)
+    keys = c["L"]
+    per_seq = keys * c["Hkv"] * c["D"] * 4 * 2
+    pool = max(1, min(batch, 8, (1 << 30) // per_seq))
+    k = rng.standard_normal(pool * keys * c["Hkv"] * c["D"], dtype=np.float32)
+    v = rng.standard_normal(pool * keys * c["Hkv"] * c["D"], dtype=np.float32)
+    q = rng.standard_normal(pool * c["Hq"] * c["D"], dtype=np.float32)
+    past = [keys - 1] * pool
+    stride = keys * c["Hkv"] * c["D"]
+    t0 = time.perf_counter()
+    _, used = O.attention_batch(q, k, v, pool, stride, 1, c["Hq"], c["Hkv"], c["D"], past, c["scale"], c["softcap"],
+                                0, threads)
+    first = time.perf_counter() - t0
+    reps = max(1, int(target_s / max(first, 1e-3)))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.attention_batch(q, k, v, pool, stride, 1, c["Hq"], c["Hkv"], c["D"], past, c["scale"], c["softcap"], 0,
+                          threads)
+    dt = time.perf_counter() - t0
+    units = reps * pool
+    gbs = units * keys * c["Hkv"] * c["D"] * 4 / dt / 1e9  # fp16 K+V bytes of those units
+    desc = (f"{units} (layer, sequence) decode units at KV length {keys} ({c['Hq']}q/{c['Hkv']}kv, D {c['D']}), "
+            f"JS-faithful double arithmetic over f32 K/V, {used} threads, {dt:.1f} s; bytes counted as the fp16 "
+            f"KV of those units")
+    return gbs, used, desc
+
+
+def run_reference(args, c, workload):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    per_step_s = 2.0
+    vals = []
+    for i in range(args.warmup + args.steps):
+        gbs, used, desc = cpu_reference_sample(c, args.batch, per_step_s, threads=0, seed=100 + i)
+        if i >= args.warmup:
+            vals.append(gbs)
+    value = sum(vals) / len(vals)
+    tok_s = value * 1e9 / (kv_bytes_per_step(c, 1))
+    line = {
+        "metric": "decode-attn KV-read GB/s", "value": round(value, 4), "unit": "GB/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(kv_bytes_per_step(c, args.batch) / (value * 1e9) * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": workload, "global_batch": args.batch * args.gpus, "kv_len": c["L"],
+                   "layers": c["layers"], "parallelism": "cpu"},
+        "tokens_per_s": round(tok_s, 3),
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": used, "kind": "port", "sample": desc},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=list(CONFIGS), default="qwen3-4b")
+    ap.add_argument("--batch", type=int, default=None, help="sequences per GPU")
+    ap.add_argument("--layers", type=int, default=None, help="override the layer count (tests only)")
+    ap.add_argument("--kv-len", type=int, default=None, help="override the KV length (tests only)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    c = dict(CONFIGS[args.workload])
+    if args.layers:
+        c["layers"] = args.layers
+    if args.kv_len:
+        c["L"] = args.kv_len
+    args.batch = args.batch or c["batch"]
+    args.warmup = max(args.warmup, 3)
+    workload = args.workload
+    if args.impl == "reference":
+        return run_reference(args, c, workload)
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from brimkern_b200.engine import AttentionEngine, AttnConfig, KvCache, RopeTable, llama3_rope_factors
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B, Lkv, layers = args.batch, c["L"], c["layers"]
+    Hq, Hkv, D = c["Hq"], c["Hkv"], c["D"]
+
+    eng = AttentionEngine(local)
+    ff = llama3_rope_factors(D, c["base"], *c["ff"]) if c["ff"] else None
+    rope = RopeTable(eng.ctx, D, c["base"], ff, Lkv)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+    qn = kn = None
+    if c["qk_norm"]:
+        qn = (1 + 0.02 * torch.randn(D, generator=gen, device=dev)).float()
+        kn = (1 + 0.02 * torch.randn(D, generator=gen, device=dev)).float()
+    cfgs = []
+    for layer in range(layers):
+        window = c["window_even"] if (c["window_even"] and layer % 2 == 0) else 0
+        cfgs.append(AttnConfig(Hq, Hkv, D, scale=c["scale"], softcap=c["softcap"], window=window, q_norm=qn,
+                               k_norm=kn, rope=rope))
+    kv = KvCache(eng.ctx, layers, B, Hkv, D, Lkv)
+    tmp_k = torch.empty((Lkv, Hkv, D), dtype=torch.float32, device=dev)
+    tmp_v = torch.empty_like(tmp_k)
+    for layer in range(layers):
+        for b in range(B):
+            tmp_k.normal_(generator=gen)
+            tmp_v.normal_(generator=gen)
+            kv.write_rows(layer, b, 0, tmp_k, tmp_v)
+    del tmp_k, tmp_v
+    past = [Lkv - 1] * B  # KV length Lkv including the token appended each step
+    q_in = torch.randn((layers, B, 1, Hq, D), generator=gen, device=dev)
+    k_in = torch.randn((layers, B, 1, Hkv, D), generator=gen, device=dev)
+    v_in = torch.randn((layers, B, 1, Hkv, D), generator=gen, device=dev)
+    q_work = torch.empty((B, 1, Hq, D), dtype=torch.float32, device=dev)
+    out = torch.empty((layers, B, 1, Hq, D), dtype=torch.float32, device=dev)
+    eng.ctx.reserve(64 << 20)
+    stream = torch.cuda.current_stream()
+
+    def step(ev=None, qi=q_in, ki=k_in, vi=v_in, oo=out):
+        for layer in range(layers):
+            eng.appendKv(kv, layer, cfgs[layer], qi[layer], ki[layer], vi[layer], q_work, past)
+            if ev is not None:
+                ev[layer][0].record(stream)
+            eng.recAttention(kv, layer, cfgs[layer], q_work, oo[layer], past)
+            if ev is not None:
+                ev[layer][1].record(stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    eng.ctx.check()
+    barrier()
+    torch.cuda.synchronize()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+    phys = int(vis[local]) if len(vis) > local and vis[local].strip().isdigit() else local
+    sampler = ClockSampler(phys)
+    sampler.start()
+    time.sleep(0.3)
+    n0 = eng.ctx.launches
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    layer_ev = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(layers)]
+                for _ in range(args.steps)]
+    start.record(stream)
+    for s in range(args.steps):
+        step(layer_ev[s])
+    stop.record(stream)
+    torch.cuda.synchronize()
+    launches = eng.ctx.launches - n0
+    clocks = sampler.stop()
+    eng.ctx.check()
+    barrier()
+    ms_total = start.elapsed_time(stop)
+    attn_ms = [layer_ev[s][l][0].elapsed_time(layer_ev[s][l][1]) for s in range(args.steps) for l in range(layers)]
+    if world > 1:
+        t = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    bytes_step = kv_bytes_per_step(c, B)
+    value = world * bytes_step / (ms_step * 1e-3) / 1e9
+    tok_s = world * B / (ms_step * 1e-3)
+
+    # Roofline of the decode attention launches (decode kernel + its split combine).
+    peak, peak_kind = load_peak()
+    attn_avg_ms = sum(attn_ms) / len(attn_ms)
+    bytes_launch = bytes_step / layers
+    achieved = bytes_launch / (attn_avg_ms * 1e-3) / 1e9
+    traffic = read_traffic(workload)
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                "kernel": "decode_attn_kernel (+ combine_kernel)", "bytes_per_launch": bytes_launch,
+                "avg_launch_ms": round(attn_avg_ms, 5), "frac_of_8TBs": round(achieved / 8000.0, 4)}
+
+    # End to end through the host API: pinned host inputs -> device, step, outputs -> host.
+    e2e = None
+    if not args.no_e2e:
+        hq = q_in.cpu().pin_memory()
+        hk = k_in.cpu().pin_memory()
+        hv = v_in.cpu().pin_memory()
+        hout = torch.empty(out.shape, dtype=torch.float32, pin_memory=True)
+        dq, dk, dv, do = torch.empty_like(q_in), torch.empty_like(k_in), torch.empty_like(v_in), torch.empty_like(out)
+
+        def e2e_step():
+            dq.copy_(hq, non_blocking=True)
+            dk.copy_(hk, non_blocking=True)
+            dv.copy_(hv, non_blocking=True)
+            step(None, dq, dk, dv, do)
+            hout.copy_(do, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e_step = e_ms / args.steps
+        e2e = {"value": round(world * bytes_step / (e_step * 1e-3) / 1e9, 2), "unit": "GB/s",
+               "h2d_bytes_per_step": int((hq.numel() + hk.numel() + hv.numel()) * 4),
+               "d2h_bytes_per_step": int(hout.numel() * 4), "ms_per_step": round(e_step, 4),
+               "tokens_per_s": round(world * B / (e_step * 1e-3), 1)}
+        eng.ctx.check()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        gbs, used, desc = cpu_reference_sample(c, B, 10.0)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": used, "kind": "port", "sample": desc}
+
+    if rank == 0:
+        line = {
+            "metric": "decode-attn KV-read GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 KV / f32 accumulate", "data": "synthetic",
+            "config": {"workload": workload, "global_batch": B * world, "batch_per_gpu": B, "kv_len": Lkv,
+                       "layers": layers, "heads": f"{Hq}q/{Hkv}kv", "head_dim": D,
+                       "parallelism": f"batch-sharded x{world} (no communication)",
+                       "l2": f"no flush: each step streams {bytes_step / 1e9:.1f} GB of KV > 126 MB L2"},
+            "tokens_per_s": round(tok_s, 1),
+            "frac_of_measured_hbm": round(value / world / peak, 4),
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

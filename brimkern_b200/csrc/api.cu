@@ -1,0 +1,619 @@
+// C-ABI implementation of libbrk_attn (declared in include/brk_attn.h): contexts, RoPE tables,
+// the KV cache manager and the dispatch of the attention kernels.  Host code only.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return fail(BRK_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+#define BRK_CUDA(call)                                         \
+    do {                                                       \
+        cudaError_t e_ = (call);                               \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call);    \
+    } while (0)
+
+// Makes `device` current for the scope of a call and restores the caller's device afterwards.
+struct DeviceGuard {
+    int prev = -1;
+    bool changed = false;
+    explicit DeviceGuard(int device) {
+        if (cudaGetDevice(&prev) == cudaSuccess && prev != device) {
+            changed = cudaSetDevice(device) == cudaSuccess;
+        }
+    }
+    ~DeviceGuard() {
+        if (changed) cudaSetDevice(prev);
+    }
+};
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D map over a cache buffer viewed as [rows][head_dim] fp16, box = [box_rows][64] with the
+// 128-byte swizzle that the kernels' shared-memory addressing assumes.
+int make_cache_map(CUtensorMap *m, const __half *base, uint64_t rows, int head_dim, int box_rows) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return fail(BRK_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)head_dim * sizeof(__half)};
+    cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1u, 1u};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(BRK_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return BRK_OK;
+}
+
+bool supported_head_dim(int d) { return d == 64 || d == 128 || d == 256; }
+
+size_t kv_elems(const brk_kv_desc &d, int cap) {
+    return (size_t)d.n_layers * d.batch * d.n_kv_heads * (size_t)cap * d.head_dim;
+}
+
+int kv_build_maps(brk_kv *kv) {
+    const uint64_t rows = (uint64_t)kv->desc.n_layers * kv->desc.batch * kv->desc.n_kv_heads * kv->cap;
+    int rc;
+    if ((rc = make_cache_map(&kv->tm_dec_k, kv->k, rows, kv->desc.head_dim, brk::decode_stage_keys(kv->desc.head_dim))))
+        return rc;
+    if ((rc = make_cache_map(&kv->tm_dec_v, kv->v, rows, kv->desc.head_dim, brk::decode_stage_keys(kv->desc.head_dim))))
+        return rc;
+    if ((rc = make_cache_map(&kv->tm_pre_k, kv->k, rows, kv->desc.head_dim, brk::prefill_tile_keys()))) return rc;
+    if ((rc = make_cache_map(&kv->tm_pre_v, kv->v, rows, kv->desc.head_dim, brk::prefill_tile_keys()))) return rc;
+    return BRK_OK;
+}
+
+// Shape checks shared by every attention entry point.
+int check_call(const brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
+               const int32_t *past_len) {
+    if (!ctx || !kv || !p || !past_len) return fail(BRK_ERR_INVALID, "null handle or argument");
+    if (kv->ctx != ctx) return fail(BRK_ERR_INVALID, "kv cache belongs to another context");
+    if (layer < 0 || layer >= kv->desc.n_layers)
+        return fail(BRK_ERR_INVALID, "layer %d outside [0, %d)", layer, kv->desc.n_layers);
+    if (batch != kv->desc.batch) return fail(BRK_ERR_INVALID, "batch %d != cache batch %d", batch, kv->desc.batch);
+    if (batch < 1 || batch > BRK_MAX_BATCH) return fail(BRK_ERR_INVALID, "batch %d outside [1, %d]", batch, BRK_MAX_BATCH);
+    if (n_tokens < 1) return fail(BRK_ERR_INVALID, "n_tokens %d < 1", n_tokens);
+    if (p->n_kv_heads != kv->desc.n_kv_heads || p->head_dim != kv->desc.head_dim)
+        return fail(BRK_ERR_INVALID, "params (%d kv heads, dim %d) do not match the cache (%d, %d)", p->n_kv_heads,
+                    p->head_dim, kv->desc.n_kv_heads, kv->desc.head_dim);
+    if (p->n_heads < 1 || p->n_kv_heads < 1 || p->n_heads % p->n_kv_heads)
+        return fail(BRK_ERR_INVALID, "n_heads %d is not a multiple of n_kv_heads %d", p->n_heads, p->n_kv_heads);
+    if (!supported_head_dim(p->head_dim)) return fail(BRK_ERR_UNSUPPORTED, "head_dim %d (64, 128 or 256)", p->head_dim);
+    if (p->kv_offset < 0) return fail(BRK_ERR_INVALID, "kv_offset %d < 0", p->kv_offset);
+    for (int b = 0; b < batch; ++b)
+        if (past_len[b] < p->kv_offset)
+            return fail(BRK_ERR_INVALID, "past_len[%d] = %d is before the cache's first position %d", b, past_len[b],
+                        p->kv_offset);
+    return BRK_OK;
+}
+
+float effective_scale(const brk_attn_params *p) {
+    return p->scale > 0.f ? p->scale : (float)(1.0 / std::sqrt((double)p->head_dim));
+}
+
+// Splits of the key range per (sequence, kv head, row tile): enough CTAs to fill the GPU's
+// concurrent slots without leaving a mostly-empty last wave; BRK_DECODE_SPLITS overrides.
+int choose_splits(const brk_ctx *ctx, int head_dim, int units, int span) {
+    const int tk = brk::decode_stage_keys(head_dim);
+    const int max_split = std::max(1, std::min(64, (span + tk - 1) / tk));
+    if (const char *env = getenv("BRK_DECODE_SPLITS")) {
+        int n = atoi(env);
+        if (n >= 1) return std::min(n, max_split);
+    }
+    const long long slots = (long long)ctx->num_sms * brk::decode_ctas_per_sm(head_dim);
+    double best = 1e30;
+    int best_n = 1;
+    for (int n = 1; n <= max_split; ++n) {
+        const long long ctas = (long long)units * n;
+        const long long waves = (ctas + slots - 1) / slots;
+        const int keys = ((span + n - 1) / n + tk - 1) / tk * tk;
+        double cost = (double)waves * (keys + 2 * tk);  // + fixed per-CTA cost in key units
+        if (n > 1) cost += 2 * tk;                      // the combine pass
+        if (cost < best - 1e-9) {
+            best = cost;
+            best_n = n;
+        }
+    }
+    return best_n;
+}
+
+// The decode path (final output or a partial), splitting the key range over CTAs.
+int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
+               const int32_t *past_len, const float *q, float *out, float *part_ml, float *part_o, bool clamp_rows,
+               cudaStream_t stream) {
+    const int D = p->head_dim, G = p->n_heads / p->n_kv_heads;
+    brk::DecodeArgs a;
+    memset(&a, 0, sizeof(a));
+    a.q = q;
+    a.err = ctx->d_err;
+    a.B = batch;
+    a.T = n_tokens;
+    a.Hq = p->n_heads;
+    a.Hkv = p->n_kv_heads;
+    a.G = G;
+    a.layer = layer;
+    a.cap = kv->cap;
+    a.mtiles = (n_tokens * G + 15) / 16;
+    a.kv_offset = p->kv_offset;
+    a.window = p->window > 0 ? p->window : 0;
+    a.scale = effective_scale(p);
+    a.scale_log2 = a.scale * 1.4426950408889634f;
+    a.softcap = p->softcap > 0.f ? p->softcap : 0.f;
+    int span = 1;
+    for (int b = 0; b < batch; ++b) {
+        a.past_len[b] = past_len[b];
+        int hi = past_len[b] + n_tokens - p->kv_offset;
+        if (hi > kv->cap) {
+            if (!clamp_rows)
+                return fail(BRK_ERR_CAPACITY, "sequence %d needs %d cache rows, capacity is %d (grow the cache)", b, hi,
+                            kv->cap);
+            hi = kv->cap;
+        }
+        int lo = a.window > 0 ? std::max(0, past_len[b] - a.window + 1 - p->kv_offset) : 0;
+        span = std::max(span, hi - lo);
+    }
+    const int units = batch * p->n_kv_heads * a.mtiles;
+    int nsplit = choose_splits(ctx, D, units, span);
+    const int tk = brk::decode_stage_keys(D);
+    a.keys_per_split = ((span + nsplit - 1) / nsplit + tk - 1) / tk * tk;
+    nsplit = (span + a.keys_per_split - 1) / a.keys_per_split;
+    a.nsplit = nsplit;
+    const int rows = batch * n_tokens * p->n_heads;
+
+    const bool direct = out != nullptr && nsplit == 1;
+    const bool direct_partial = out == nullptr && nsplit == 1;
+    if (direct) {
+        a.out = out;
+    } else if (direct_partial) {
+        a.part_ml = part_ml;
+        a.part_o = part_o;
+    } else {
+        const size_t need = (size_t)nsplit * rows * (2 + D) * sizeof(float);
+        if (need > ctx->ws_bytes) {
+            int rc = brk_ctx_reserve(ctx, need);
+            if (rc) return rc;
+        }
+        a.part_ml = static_cast<float *>(ctx->ws);
+        a.part_o = a.part_ml + (size_t)nsplit * rows * 2;
+    }
+    cudaError_t e = brk::launch_decode(D, kv->tm_dec_k, kv->tm_dec_v, a, nsplit, p->n_kv_heads * a.mtiles, batch, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
+    ++ctx->launches;
+    if (!direct && !direct_partial) {
+        brk::CombineArgs c;
+        c.part_ml = a.part_ml;
+        c.part_o = a.part_o;
+        c.out = out;
+        c.out_ml = out ? nullptr : part_ml;
+        c.out_o = out ? nullptr : part_o;
+        c.n_parts = nsplit;
+        c.rows = rows;
+        c.D = D;
+        e = brk::launch_combine(c, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
+        ++ctx->launches;
+    }
+    return BRK_OK;
+}
+
+}  // namespace
+
+namespace brk {
+int prefill_tile_keys() { return 128; }
+}  // namespace brk
+
+extern "C" {
+
+const char *brk_last_error(void) { return g_last_error.c_str(); }
+
+int brk_abi_version(void) { return BRK_ABI_VERSION; }
+
+int brk_ctx_create(int device, brk_ctx **out) {
+    if (!out) return fail(BRK_ERR_INVALID, "out is null");
+    *out = nullptr;
+    int n = 0;
+    BRK_CUDA(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) return fail(BRK_ERR_INVALID, "device %d outside [0, %d)", device, n);
+    DeviceGuard g(device);
+    cudaDeviceProp prop;
+    BRK_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10) return fail(BRK_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", device, prop.major, prop.minor);
+    brk_ctx *c = new brk_ctx();
+    c->device = device;
+    c->num_sms = prop.multiProcessorCount;
+    cudaError_t e = cudaMalloc(&c->d_err, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        delete c;
+        return cuda_fail(e, "context error word");
+    }
+    *out = c;
+    return BRK_OK;
+}
+
+int brk_ctx_destroy(brk_ctx *ctx) {
+    if (!ctx) return BRK_OK;
+    DeviceGuard g(ctx->device);
+    cudaDeviceSynchronize();
+    cudaFree(ctx->d_err);
+    cudaFree(ctx->ws);
+    delete ctx;
+    return BRK_OK;
+}
+
+int brk_ctx_check(brk_ctx *ctx, void *stream) {
+    if (!ctx) return fail(BRK_ERR_INVALID, "null context");
+    DeviceGuard g(ctx->device);
+    BRK_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+    int err = 0;
+    BRK_CUDA(cudaMemcpy(&err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err) {
+        BRK_CUDA(cudaMemset(ctx->d_err, 0, sizeof(int)));
+        return fail(BRK_ERR_DEVICE, "a kernel gave up on a bounded wait (code %d)", err);
+    }
+    return BRK_OK;
+}
+
+uint64_t brk_ctx_launches(const brk_ctx *ctx) { return ctx ? ctx->launches : 0; }
+
+int brk_ctx_reserve(brk_ctx *ctx, size_t bytes) {
+    if (!ctx) return fail(BRK_ERR_INVALID, "null context");
+    if (bytes <= ctx->ws_bytes) return BRK_OK;
+    DeviceGuard g(ctx->device);
+    BRK_CUDA(cudaDeviceSynchronize());  // queued kernels may still read the old workspace
+    cudaFree(ctx->ws);
+    ctx->ws = nullptr;
+    ctx->ws_bytes = 0;
+    BRK_CUDA(cudaMalloc(&ctx->ws, bytes));
+    ctx->ws_bytes = bytes;
+    return BRK_OK;
+}
+
+int brk_rope_create(brk_ctx *ctx, int head_dim, double base, const float *ff_host, int max_positions,
+                    brk_rope **out) {
+    if (!ctx || !out) return fail(BRK_ERR_INVALID, "null argument");
+    *out = nullptr;
+    if (head_dim < 2 || head_dim % 2) return fail(BRK_ERR_INVALID, "head_dim %d must be even", head_dim);
+    if (max_positions < 1) return fail(BRK_ERR_INVALID, "max_positions %d < 1", max_positions);
+    const int half = head_dim / 2;
+    // ropeCpu / ropeFactorsCpu (kernels.ts:3428-3460): freq = pos / (base ** (2i/D) [* ff[i]]).
+    std::vector<double> denom(half);
+    for (int i = 0; i < half; ++i) {
+        double dn = std::pow(base, (2.0 * i) / (double)head_dim);
+        if (ff_host) dn = dn * (double)ff_host[i];
+        denom[i] = dn;
+    }
+    std::vector<double2> table((size_t)max_positions * half);
+    for (int pos = 0; pos < max_positions; ++pos)
+        for (int i = 0; i < half; ++i) {
+            const double freq = (double)pos / denom[i];
+            table[(size_t)pos * half + i] = make_double2(std::cos(freq), std::sin(freq));
+        }
+    DeviceGuard g(ctx->device);
+    brk_rope *r = new brk_rope();
+    r->ctx = ctx;
+    r->head_dim = head_dim;
+    r->max_pos = max_positions;
+    cudaError_t e = cudaMalloc(&r->table, table.size() * sizeof(double2));
+    if (e == cudaSuccess) e = cudaMemcpy(r->table, table.data(), table.size() * sizeof(double2), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(r->table);
+        delete r;
+        return cuda_fail(e, "rope table");
+    }
+    *out = r;
+    return BRK_OK;
+}
+
+int brk_rope_destroy(brk_rope *rope) {
+    if (!rope) return BRK_OK;
+    DeviceGuard g(rope->ctx->device);
+    cudaFree(rope->table);
+    delete rope;
+    return BRK_OK;
+}
+
+int brk_rope_max_positions(const brk_rope *rope) { return rope ? rope->max_pos : 0; }
+
+int brk_llama3_rope_factors(int head_dim, double base, double factor, double low_freq_factor,
+                            double high_freq_factor, int original_context, float *ff_out) {
+    if (!ff_out || head_dim < 2 || head_dim % 2 || factor <= 0 || high_freq_factor <= low_freq_factor ||
+        original_context <= 0)
+        return fail(BRK_ERR_INVALID, "invalid llama3 rope scaling arguments");
+    // Published llama3 scaling: keep high frequencies, divide low frequencies by `factor`, and
+    // interpolate in between on orig_ctx / wavelength.  Stored as divisors of the frequency.
+    const double pi = 3.14159265358979323846;
+    const double low_wavelen = original_context / low_freq_factor;
+    const double high_wavelen = original_context / high_freq_factor;
+    for (int i = 0; i < head_dim / 2; ++i) {
+        const double freq = 1.0 / std::pow(base, (2.0 * i) / head_dim);
+        const double wavelen = 2.0 * pi / freq;
+        double scaled;
+        if (wavelen < high_wavelen) {
+            scaled = freq;
+        } else if (wavelen > low_wavelen) {
+            scaled = freq / factor;
+        } else {
+            const double smooth = (original_context / wavelen - low_freq_factor) / (high_freq_factor - low_freq_factor);
+            scaled = (1.0 - smooth) * freq / factor + smooth * freq;
+        }
+        ff_out[i] = (float)(freq / scaled);
+    }
+    return BRK_OK;
+}
+
+int brk_kv_create(brk_ctx *ctx, const brk_kv_desc *desc, brk_kv **out) {
+    if (!ctx || !desc || !out) return fail(BRK_ERR_INVALID, "null argument");
+    *out = nullptr;
+    const brk_kv_desc &d = *desc;
+    if (d.dtype != BRK_KV_F16) return fail(BRK_ERR_UNSUPPORTED, "kv dtype %d (only BRK_KV_F16)", d.dtype);
+    if (!supported_head_dim(d.head_dim)) return fail(BRK_ERR_UNSUPPORTED, "head_dim %d (64, 128 or 256)", d.head_dim);
+    if (d.n_layers < 1 || d.batch < 1 || d.batch > BRK_MAX_BATCH || d.n_kv_heads < 1 || d.capacity < 1)
+        return fail(BRK_ERR_INVALID, "invalid kv descriptor");
+    if ((long long)d.n_layers * d.batch * d.n_kv_heads * (long long)d.capacity >= (1ll << 31))
+        return fail(BRK_ERR_CAPACITY, "layers * batch * kv_heads * capacity must stay below 2^31 rows");
+    DeviceGuard g(ctx->device);
+    brk_kv *kv = new brk_kv();
+    kv->ctx = ctx;
+    kv->desc = d;
+    kv->cap = d.capacity;
+    const size_t bytes = kv_elems(d, kv->cap) * sizeof(__half);
+    cudaError_t e = cudaMalloc(&kv->k, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&kv->v, bytes);
+    if (e == cudaSuccess) e = cudaMemset(kv->k, 0, bytes);
+    if (e == cudaSuccess) e = cudaMemset(kv->v, 0, bytes);
+    if (e != cudaSuccess) {
+        cudaFree(kv->k);
+        cudaFree(kv->v);
+        delete kv;
+        return cuda_fail(e, "kv cache allocation");
+    }
+    int rc = kv_build_maps(kv);
+    if (rc) {
+        cudaFree(kv->k);
+        cudaFree(kv->v);
+        delete kv;
+        return rc;
+    }
+    *out = kv;
+    return BRK_OK;
+}
+
+int brk_kv_destroy(brk_kv *kv) {
+    if (!kv) return BRK_OK;
+    DeviceGuard g(kv->ctx->device);
+    cudaDeviceSynchronize();
+    cudaFree(kv->k);
+    cudaFree(kv->v);
+    delete kv;
+    return BRK_OK;
+}
+
+int brk_kv_capacity(const brk_kv *kv) { return kv ? kv->cap : 0; }
+
+int brk_kv_grow(brk_kv *kv, int rows, void *stream) {
+    if (!kv) return fail(BRK_ERR_INVALID, "null kv");
+    if (rows <= kv->cap) return BRK_OK;
+    const int cap = std::max(rows, std::max(kv->cap + 1024, 1024));  // ensureKv, kernels.ts:1785
+    const brk_kv_desc &d = kv->desc;
+    if ((long long)d.n_layers * d.batch * d.n_kv_heads * (long long)cap >= (1ll << 31))
+        return fail(BRK_ERR_CAPACITY, "growing to %d rows exceeds 2^31 cache rows", cap);
+    DeviceGuard g(kv->ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t bytes = kv_elems(d, cap) * sizeof(__half);
+    __half *nk = nullptr, *nv = nullptr;
+    cudaError_t e = cudaMalloc(&nk, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&nv, bytes);
+    if (e != cudaSuccess) {
+        cudaFree(nk);
+        cudaFree(nv);
+        return cuda_fail(e, "kv cache growth");
+    }
+    const size_t segs = (size_t)d.n_layers * d.batch * d.n_kv_heads;
+    const size_t old_pitch = (size_t)kv->cap * d.head_dim * sizeof(__half);
+    const size_t new_pitch = (size_t)cap * d.head_dim * sizeof(__half);
+    BRK_CUDA(cudaMemsetAsync(nk, 0, bytes, s));
+    BRK_CUDA(cudaMemsetAsync(nv, 0, bytes, s));
+    BRK_CUDA(cudaMemcpy2DAsync(nk, new_pitch, kv->k, old_pitch, old_pitch, segs, cudaMemcpyDeviceToDevice, s));
+    BRK_CUDA(cudaMemcpy2DAsync(nv, new_pitch, kv->v, old_pitch, old_pitch, segs, cudaMemcpyDeviceToDevice, s));
+    BRK_CUDA(cudaStreamSynchronize(s));
+    cudaFree(kv->k);
+    cudaFree(kv->v);
+    kv->k = nk;
+    kv->v = nv;
+    kv->cap = cap;
+    return kv_build_maps(kv);
+}
+
+int brk_kv_reset(brk_kv *kv, void *stream) {
+    if (!kv) return fail(BRK_ERR_INVALID, "null kv");
+    DeviceGuard g(kv->ctx->device);
+    const size_t bytes = kv_elems(kv->desc, kv->cap) * sizeof(__half);
+    BRK_CUDA(cudaMemsetAsync(kv->k, 0, bytes, static_cast<cudaStream_t>(stream)));
+    BRK_CUDA(cudaMemsetAsync(kv->v, 0, bytes, static_cast<cudaStream_t>(stream)));
+    return BRK_OK;
+}
+
+static int check_rows(const brk_kv *kv, int layer, int seq, int row0, int n_rows) {
+    if (!kv) return fail(BRK_ERR_INVALID, "null kv");
+    if (layer < 0 || layer >= kv->desc.n_layers || seq < 0 || seq >= kv->desc.batch)
+        return fail(BRK_ERR_INVALID, "layer %d / sequence %d out of range", layer, seq);
+    if (row0 < 0 || n_rows < 0 || (long long)row0 + n_rows > kv->cap)
+        return fail(BRK_ERR_CAPACITY, "rows [%d, %d) outside the capacity %d", row0, row0 + n_rows, kv->cap);
+    return BRK_OK;
+}
+
+int brk_kv_write_rows(brk_kv *kv, int layer, int seq, int row0, int n_rows, const float *k, const float *v,
+                      void *stream) {
+    int rc = check_rows(kv, layer, seq, row0, n_rows);
+    if (rc) return rc;
+    DeviceGuard g(kv->ctx->device);
+    const brk_kv_desc &d = kv->desc;
+    const size_t off = ((size_t)(layer * d.batch + seq) * d.n_kv_heads * kv->cap + row0) * d.head_dim;
+    cudaError_t e = brk::launch_kv_write_rows(kv->k + off, kv->v + off, k, v, n_rows, d.n_kv_heads, d.head_dim, kv->cap,
+                                              static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? BRK_OK : cuda_fail(e, "kv write");
+}
+
+int brk_kv_read_rows(const brk_kv *kv, int layer, int seq, int row0, int n_rows, uint16_t *k_out, uint16_t *v_out,
+                     void *stream) {
+    int rc = check_rows(kv, layer, seq, row0, n_rows);
+    if (rc) return rc;
+    DeviceGuard g(kv->ctx->device);
+    const brk_kv_desc &d = kv->desc;
+    const size_t off = ((size_t)(layer * d.batch + seq) * d.n_kv_heads * kv->cap + row0) * d.head_dim;
+    cudaError_t e = brk::launch_kv_read_rows(kv->k + off, kv->v + off, k_out, v_out, n_rows, d.n_kv_heads, d.head_dim,
+                                             kv->cap, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? BRK_OK : cuda_fail(e, "kv read");
+}
+
+int brk_attn_append(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
+                    const int32_t *past_len, const float *q_in, const float *k_in, const float *v_in, float *q_out,
+                    void *stream) {
+    if ((q_in == nullptr) != (q_out == nullptr)) return fail(BRK_ERR_INVALID, "q_in and q_out go together");
+    if ((k_in == nullptr) != (v_in == nullptr)) return fail(BRK_ERR_INVALID, "k_in and v_in go together");
+    if (kv) {
+        int rc = check_call(ctx, kv, layer, p, batch, n_tokens, past_len);
+        if (rc) return rc;
+    } else {
+        // q-only prologue (norm + rotation of q, no cache): any even head_dim up to 1024.
+        if (!ctx || !p || !past_len) return fail(BRK_ERR_INVALID, "null handle or argument");
+        if (k_in) return fail(BRK_ERR_INVALID, "k_in / v_in need a kv cache");
+        if (p->head_dim < 2 || p->head_dim % 2 || p->head_dim > 1024 || p->n_heads < 1)
+            return fail(BRK_ERR_INVALID, "q-only append needs an even head_dim <= 1024 and n_heads >= 1");
+        if (batch < 1 || batch > BRK_MAX_BATCH || n_tokens < 1)
+            return fail(BRK_ERR_INVALID, "batch %d / n_tokens %d out of range", batch, n_tokens);
+        for (int b = 0; b < batch; ++b)
+            if (past_len[b] < 0) return fail(BRK_ERR_INVALID, "past_len[%d] < 0", b);
+    }
+    if (p->rope && (p->rope->head_dim != p->head_dim || p->rope->ctx != ctx))
+        return fail(BRK_ERR_INVALID, "rope table head_dim %d != %d", p->rope->head_dim, p->head_dim);
+    brk::AppendArgs a;
+    memset(&a, 0, sizeof(a));
+    for (int b = 0; b < batch; ++b) {
+        const int last = past_len[b] + n_tokens;
+        if (p->rope && last > p->rope->max_pos)
+            return fail(BRK_ERR_CAPACITY, "position %d beyond the rope table (%d positions)", last - 1, p->rope->max_pos);
+        if (k_in && last - p->kv_offset > kv->cap)
+            return fail(BRK_ERR_CAPACITY, "sequence %d appends up to row %d, capacity is %d (grow the cache)", b,
+                        last - p->kv_offset, kv->cap);
+        a.past_len[b] = past_len[b];
+    }
+    DeviceGuard g(ctx->device);
+    a.q_in = q_in;
+    a.k_in = k_in;
+    a.v_in = v_in;
+    a.q_out = q_out;
+    a.kc = kv ? kv->k : nullptr;
+    a.vc = kv ? kv->v : nullptr;
+    a.rope = p->rope ? p->rope->table : nullptr;
+    a.rope_max = p->rope ? p->rope->max_pos : 0;
+    a.q_norm = p->q_norm;
+    a.k_norm = p->k_norm;
+    a.eps = p->eps;
+    a.one_plus = p->norm_one_plus ? 1 : 0;
+    a.B = batch;
+    a.T = n_tokens;
+    a.Hq = p->n_heads;
+    a.Hkv = kv ? p->n_kv_heads : 0;
+    a.D = p->head_dim;
+    a.layer = layer;
+    a.cap = kv ? kv->cap : 0;
+    a.kv_offset = p->kv_offset;
+    cudaError_t e = brk::launch_append(a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "append kernel launch");
+    ++ctx->launches;
+    return BRK_OK;
+}
+
+int brk_attn_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
+                    const int32_t *past_len, const float *q, float *out, void *stream) {
+    int rc = check_call(ctx, kv, layer, p, batch, n_tokens, past_len);
+    if (rc) return rc;
+    if (!q || !out) return fail(BRK_ERR_INVALID, "null q or out");
+    DeviceGuard g(ctx->device);
+    return run_decode(ctx, kv, layer, p, batch, n_tokens, past_len, q, out, nullptr, nullptr, false,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int brk_attn_prefill(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
+                     const int32_t *past_len, const float *q, float *out, void *stream) {
+    int rc = check_call(ctx, kv, layer, p, batch, n_tokens, past_len);
+    if (rc) return rc;
+    (void)q;
+    (void)out;
+    (void)stream;
+    return fail(BRK_ERR_UNSUPPORTED, "the tensor-core prefill kernel is not built in this library version");
+}
+
+int brk_attn_forward(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
+                     const int32_t *past_len, const float *q, float *out, void *stream) {
+    return brk_attn_decode(ctx, kv, layer, p, batch, n_tokens, past_len, q, out, stream);
+}
+
+int brk_attn_decode_partial(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch,
+                            int n_tokens, const int32_t *past_len, const float *q, float *part_ml, float *part_o,
+                            void *stream) {
+    int rc = check_call(ctx, kv, layer, p, batch, n_tokens, past_len);
+    if (rc) return rc;
+    if (!q || !part_ml || !part_o) return fail(BRK_ERR_INVALID, "null q or partial buffers");
+    DeviceGuard g(ctx->device);
+    return run_decode(ctx, kv, layer, p, batch, n_tokens, past_len, q, nullptr, part_ml, part_o, true,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int brk_attn_combine(brk_ctx *ctx, int n_parts, int rows, int head_dim, const float *part_ml, const float *part_o,
+                     float *out, void *stream) {
+    if (!ctx || !part_ml || !part_o || !out) return fail(BRK_ERR_INVALID, "null argument");
+    if (n_parts < 1 || rows < 0 || head_dim < 1) return fail(BRK_ERR_INVALID, "invalid combine shape");
+    DeviceGuard g(ctx->device);
+    brk::CombineArgs c;
+    c.part_ml = part_ml;
+    c.part_o = part_o;
+    c.out = out;
+    c.out_ml = nullptr;
+    c.out_o = nullptr;
+    c.n_parts = n_parts;
+    c.rows = rows;
+    c.D = head_dim;
+    cudaError_t e = brk::launch_combine(c, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
+    ++ctx->launches;
+    return BRK_OK;
+}
+
+}  // extern "C"

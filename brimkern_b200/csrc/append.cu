@@ -1,0 +1,165 @@
+// KV append with the q/k prologue fused: per-head RMSNorm (QK-norm), NeoX RoPE, fp16 store.
+//
+// Replaces, for one layer, the reference's chain rmsnorm(q), rmsnorm(k) (kernels.ts:1707-1709,
+// shaders.ts:580-598) -> rope / rope_factors (kernels.ts:1710-1718, shaders.ts:1361-1408) ->
+// copyBufferToBuffer of K and V into the cache at row pastLen (kernels.ts:1727-1730).
+//
+// Bit-exactness: the reference's CPU functions (rmsnormCpu kernels.ts:3395, ropeCpu :3445,
+// ropeFactorsCpu :3428) compute in double and round to f32 on each Float32Array store.  This
+// kernel does the same in fp64 with explicitly rounded operations (no FMA contraction), the
+// sum of squares in the same sequential order, and cos/sin taken from a table the host built
+// with the same libm expression, so each stored f32 equals the oracle's; K and V are then
+// rounded f32 -> fp16 to nearest even.
+#include "common.cuh"
+#include "internal.h"
+
+namespace brk {
+
+namespace {
+
+constexpr int kRowsPerBlock = 4;  // one warp per head-vector row
+
+__global__ void __launch_bounds__(kRowsPerBlock * 32) append_kernel(const __grid_constant__ AppendArgs a) {
+    extern __shared__ float xs_all[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int D = a.D, half = D >> 1;
+    const int per_tok = a.Hq + 2 * a.Hkv;
+    const long long row = (long long)blockIdx.x * kRowsPerBlock + warp;
+    if (row >= (long long)a.B * a.T * per_tok) return;
+    const int bt = (int)(row / per_tok), kind = (int)(row % per_tok);
+    const int b = bt / a.T, t = bt % a.T;
+    const int pos = a.past_len[b] + t;
+
+    const float *src;
+    const float *gain = nullptr;
+    bool rotate = a.rope != nullptr;
+    float *qdst = nullptr;
+    __half *cdst = nullptr;
+    if (kind < a.Hq) {
+        if (!a.q_out) return;
+        src = a.q_in + ((size_t)bt * a.Hq + kind) * D;
+        gain = a.q_norm;
+        qdst = a.q_out + ((size_t)bt * a.Hq + kind) * D;
+    } else {
+        const bool is_k = kind < a.Hq + a.Hkv;
+        const int h = is_k ? kind - a.Hq : kind - a.Hq - a.Hkv;
+        const float *in = is_k ? a.k_in : a.v_in;
+        if (!in) return;
+        src = in + ((size_t)bt * a.Hkv + h) * D;
+        const size_t crow = ((size_t)(a.layer * a.B + b) * a.Hkv + h) * a.cap + (size_t)(pos - a.kv_offset);
+        cdst = (is_k ? a.kc : a.vc) + crow * D;
+        if (is_k) {
+            gain = a.k_norm;
+        } else {
+            rotate = false;  // V is neither normalised nor rotated
+        }
+    }
+
+    float *xs = xs_all + warp * D;
+    for (int d = lane; d < D; d += 32) xs[d] = src[d];
+    __syncwarp();
+
+    if (gain) {
+        // rmsnormCpu: ss = sum x^2 in order (double), inv = 1/sqrt(ss/dim + eps), y = f32(x*inv*g).
+        double inv = 0.0;
+        if (lane == 0) {
+            double ss = 0.0;
+            for (int d = 0; d < D; ++d) {
+                const double x = xs[d];
+                ss = __dadd_rn(ss, __dmul_rn(x, x));
+            }
+            inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)D), a.eps)));
+        }
+        inv = __shfl_sync(0xffffffffu, inv, 0);
+        __syncwarp();
+        for (int d = lane; d < D; d += 32) {
+            const double w = gain[d];
+            const double g = a.one_plus ? __dadd_rn(1.0, w) : w;
+            xs[d] = (float)__dmul_rn(__dmul_rn((double)xs[d], inv), g);
+        }
+        __syncwarp();
+    }
+
+    if (rotate) {
+        // ropeCpu: o_i = f32(x_i c - x_{i+D/2} s), o_{i+D/2} = f32(x_{i+D/2} c + x_i s).
+        const double2 *cs = a.rope + (size_t)pos * half;
+        for (int i = lane; i < half; i += 32) {
+            const double2 e = cs[i];
+            const double x0 = xs[i], x1 = xs[i + half];
+            const float o0 = (float)__dsub_rn(__dmul_rn(x0, e.x), __dmul_rn(x1, e.y));
+            const float o1 = (float)__dadd_rn(__dmul_rn(x1, e.x), __dmul_rn(x0, e.y));
+            if (qdst) {
+                qdst[i] = o0;
+                qdst[i + half] = o1;
+            } else {
+                cdst[i] = __float2half_rn(o0);
+                cdst[i + half] = __float2half_rn(o1);
+            }
+        }
+    } else {
+        for (int d = lane; d < D; d += 32) {
+            if (qdst)
+                qdst[d] = xs[d];
+            else
+                cdst[d] = __float2half_rn(xs[d]);
+        }
+    }
+}
+
+// Plain f32 -> fp16 row store into one (layer, sequence) segment: rows [row0, row0+n) of every
+// kv head.  kc/vc point at row row0 of kv head 0 of the segment; heads are `cap` rows apart.
+__global__ void kv_write_rows_kernel(__half *kc, __half *vc, const float *k, const float *v, int n_rows, int Hkv,
+                                     int D, int cap) {
+    const long long n = (long long)n_rows * Hkv * D;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const int d = (int)(i % D);
+        const int h = (int)((i / D) % Hkv);
+        const int r = (int)(i / ((long long)D * Hkv));
+        const size_t dst = ((size_t)h * cap + r) * D + d;
+        if (k) kc[dst] = __float2half_rn(k[i]);
+        if (v) vc[dst] = __float2half_rn(v[i]);
+    }
+}
+
+__global__ void kv_read_rows_kernel(const __half *kc, const __half *vc, uint16_t *k, uint16_t *v, int n_rows, int Hkv,
+                                    int D, int cap) {
+    const long long n = (long long)n_rows * Hkv * D;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const int d = (int)(i % D);
+        const int h = (int)((i / D) % Hkv);
+        const int r = (int)(i / ((long long)D * Hkv));
+        const size_t src = ((size_t)h * cap + r) * D + d;
+        if (k) k[i] = __half_as_ushort(kc[src]);
+        if (v) v[i] = __half_as_ushort(vc[src]);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_append(const AppendArgs &a, cudaStream_t s) {
+    const long long rows = (long long)a.B * a.T * (a.Hq + 2 * a.Hkv);
+    if (rows == 0) return cudaSuccess;
+    const unsigned grid = (unsigned)((rows + kRowsPerBlock - 1) / kRowsPerBlock);
+    append_kernel<<<grid, kRowsPerBlock * 32, kRowsPerBlock * a.D * sizeof(float), s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kv_write_rows(__half *kc, __half *vc, const float *k, const float *v, int n_rows, int Hkv, int D,
+                                 int cap, cudaStream_t s) {
+    const long long n = (long long)n_rows * Hkv * D;
+    if (n == 0) return cudaSuccess;
+    const unsigned grid = (unsigned)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    kv_write_rows_kernel<<<grid, 256, 0, s>>>(kc, vc, k, v, n_rows, Hkv, D, cap);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kv_read_rows(const __half *kc, const __half *vc, uint16_t *k, uint16_t *v, int n_rows, int Hkv,
+                                int D, int cap, cudaStream_t s) {
+    const long long n = (long long)n_rows * Hkv * D;
+    if (n == 0) return cudaSuccess;
+    const unsigned grid = (unsigned)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    kv_read_rows_kernel<<<grid, 256, 0, s>>>(kc, vc, k, v, n_rows, Hkv, D, cap);
+    return cudaGetLastError();
+}
+
+}  // namespace brk

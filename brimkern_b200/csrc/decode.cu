@@ -1,0 +1,420 @@
+// Decode attention over the resident fp16 KV cache (replaces attention_decode,
+// shaders.ts:1768-1851, and its dispatch in recAttention, kernels.ts:1626-1641).
+//
+// One CTA per (sequence, kv head, row tile, split).  The rows of a CTA are up to 16 (token,
+// q head) pairs of one kv head's query group, so every K/V byte read from HBM serves the whole
+// group (the reference re-reads K/V once per q head).  A producer warp streams the CTA's key
+// range through a ring of shared-memory stages with 2-D TMA loads (128-byte swizzled
+// [keys][64 x fp16] boxes, no multicast); four consumer warps each take 16 keys of every stage
+// and run QK^T and PV on the tensor cores (mma.m16n8k16, fp16 in, fp32 accumulate), keeping an
+// online softmax per warp with quad shuffles.  The warps merge their (max, sum, output) in
+// shared memory at the end; with split-KV the CTA writes a partial that brk_attn_combine merges.
+#include <math_constants.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace brk {
+
+namespace {
+
+constexpr int kKeysPerWarp = 16;
+constexpr int kConsumerWarps = 4;
+constexpr int kStageKeys = kKeysPerWarp * kConsumerWarps;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+template <int D>
+struct DecodeCfg;
+template <>
+struct DecodeCfg<64> {
+    static constexpr int kStages = 6, kMinBlocks = 2;
+};
+template <>
+struct DecodeCfg<128> {
+    static constexpr int kStages = 3, kMinBlocks = 2;
+};
+template <>
+struct DecodeCfg<256> {
+    static constexpr int kStages = 3, kMinBlocks = 1;
+};
+
+template <int D>
+struct DecodeLayout {
+    static constexpr int kBlocks = D / 64;                         // 128-byte column blocks per row
+    static constexpr uint32_t kBoxBytes = kStageKeys * 128;        // one [keys][64] fp16 box
+    static constexpr uint32_t kTileBytes = kBlocks * kBoxBytes;    // K (or V) of one stage
+    static constexpr uint32_t kStageBytes = 2 * kTileBytes;
+    static constexpr uint32_t kRingBytes = DecodeCfg<D>::kStages * kStageBytes;
+    static constexpr uint32_t kQBytes = kBlocks * 16 * 128;        // 16 rows of q, fp16, swizzled
+    static constexpr uint32_t kBarBytes = 2 * DecodeCfg<D>::kStages * 8;
+    static constexpr uint32_t kSmemBytes = 1024 + kRingBytes + kQBytes + kBarBytes;
+    static_assert(kConsumerWarps * 16 * D * 4 + 2 * kConsumerWarps * 16 * 4 <= kRingBytes,
+                  "merge buffers must fit in the ring");
+};
+
+template <int D>
+__global__ void __launch_bounds__((kConsumerWarps + 1) * 32, DecodeCfg<D>::kMinBlocks)
+    decode_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                       const __grid_constant__ DecodeArgs a) {
+    using L = DecodeLayout<D>;
+    constexpr int S = DecodeCfg<D>::kStages;
+    constexpr int KS = D / 16;   // k-steps of QK^T
+    constexpr int NTO = D / 8;   // n-tiles of the output
+    constexpr bool kQInRegs = D <= 128;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *ring = smem;
+    uint8_t *qs = ring + L::kRingBytes;
+    uint64_t *full = reinterpret_cast<uint64_t *>(qs + L::kQBytes);
+    uint64_t *empty = full + S;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int split = blockIdx.x;
+    const int kvh = blockIdx.y / a.mtiles, mt = blockIdx.y % a.mtiles;
+    const int b = blockIdx.z;
+    const int G = a.G, T = a.T;
+    const int nrows = T * G;
+    const int row0 = mt * 16;
+    const int past = a.past_len[b];
+
+    // Key range of this CTA, in cache rows.  Token t attends [pos_t - W + 1, pos_t] (W <= 0: from 0).
+    const int t_lo = row0 / G;
+    const int t_hi = min(row0 + 15, nrows - 1) / G;
+    int kv_hi = past + t_hi + 1 - a.kv_offset;
+    if (kv_hi > a.cap) kv_hi = a.cap;
+    int kv_lo = 0;
+    if (a.window > 0) kv_lo = max(0, past + t_lo - a.window + 1 - a.kv_offset);
+    const int k_begin = kv_lo + split * a.keys_per_split;
+    const int k_end = min(kv_hi, k_begin + a.keys_per_split);
+    const int ntiles = k_begin < k_end ? (k_end - k_begin + kStageKeys - 1) / kStageKeys : 0;
+    const int seg_row = ((a.layer * a.B + b) * a.Hkv + kvh) * a.cap;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        fence_barrier_init();
+    }
+    // Stage this CTA's 16 q rows as fp16 in the same swizzled layout as the K boxes.
+    for (int idx = threadIdx.x; idx < 16 * (D / 8); idx += blockDim.x) {
+        const int r = idx / (D / 8), ch = idx % (D / 8);
+        const int rr = row0 + r;
+        float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
+        if (rr < nrows) {
+            const int t = rr / G, h = kvh * G + rr % G;
+            const float *src = a.q + (((size_t)b * T + t) * a.Hq + h) * D + ch * 8;
+            x0 = *reinterpret_cast<const float4 *>(src);
+            x1 = *reinterpret_cast<const float4 *>(src + 4);
+        }
+        uint4 pk;
+        pk.x = pack_half2(x0.x, x0.y);
+        pk.y = pack_half2(x0.z, x0.w);
+        pk.z = pack_half2(x1.x, x1.y);
+        pk.w = pack_half2(x1.z, x1.w);
+        *reinterpret_cast<uint4 *>(qs + (ch >> 3) * 2048 + sw128(r, ch & 7)) = pk;
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ---- producer: one elected lane streams K/V tiles through the ring.
+        if (lane == 0 && ntiles > 0) {
+            tma_prefetch_desc(&tmk);
+            tma_prefetch_desc(&tmv);
+            int issued = 0;
+            for (int i = 0; i < ntiles; ++i) {
+                const int s = i % S;
+                if (i >= S && !mbar_wait(&empty[s], ((i / S) - 1) & 1, a.err, kErrSlotTimeout)) break;
+                mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+                uint8_t *st = ring + s * L::kStageBytes;
+                const int y = seg_row + k_begin + i * kStageKeys;
+#pragma unroll
+                for (int j = 0; j < L::kBlocks; ++j) tma_load_2d(st + j * L::kBoxBytes, &tmk, j * 64, y, &full[s]);
+#pragma unroll
+                for (int j = 0; j < L::kBlocks; ++j)
+                    tma_load_2d(st + L::kTileBytes + j * L::kBoxBytes, &tmv, j * 64, y, &full[s]);
+                issued = i + 1;
+            }
+            // Before leaving, make sure every copy this lane started has landed (bounded).
+            for (int i = issued > S ? issued - S : 0; i < issued; ++i)
+                mbar_wait(&full[i % S], (i / S) & 1, a.err, kErrTmaTimeout);
+        }
+        return;
+    }
+
+    // ---- consumers
+    const int qr = lane >> 2, qc = lane & 3;
+    uint32_t qf[kQInRegs ? KS : 1][4];
+    if constexpr (kQInRegs) {
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks)
+            ldsm_x4(smem_addr(qs + (ks >> 2) * 2048 + sw128(lane & 15, (ks & 3) * 2 + (lane >> 4))), qf[ks][0],
+                    qf[ks][1], qf[ks][2], qf[ks][3]);
+    }
+
+    // Causal / window limits of this lane's two rows (rows rA and rA + 8 of the tile).
+    const int rA = row0 + qr, rB = rA + 8;
+    const int hiA = rA < nrows ? past + rA / G - a.kv_offset : -1;
+    const int hiB = rB < nrows ? past + rB / G - a.kv_offset : -1;
+    const int loA = a.window > 0 ? past + rA / G - a.window + 1 - a.kv_offset : INT_MIN;
+    const int loB = a.window > 0 ? past + rB / G - a.window + 1 - a.kv_offset : INT_MIN;
+    const bool use_cap = a.softcap > 0.f;
+
+    float o[NTO][4];
+#pragma unroll
+    for (int n = 0; n < NTO; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m2[2] = {-CUDART_INF_F, -CUDART_INF_F};  // running max, log2 units
+    float lsum[2] = {0.f, 0.f};                    // this lane's share of the running sum
+
+    for (int i = 0; i < ntiles; ++i) {
+        const int s = i % S;
+        if (!mbar_wait(&full[s], (i / S) & 1, a.err, kErrTmaTimeout)) break;
+        uint8_t *kt = ring + s * L::kStageBytes;
+        uint8_t *vt = kt + L::kTileBytes;
+        const int key0 = k_begin + i * kStageKeys + warp * kKeysPerWarp;
+
+        // S = Q K^T for this warp's 16 keys (two n-tiles of 8 keys).
+        float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        const int krow = warp * kKeysPerWarp + ((lane >> 4) << 3) + (lane & 7);
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(smem_addr(kt + (ks >> 2) * L::kBoxBytes + sw128(krow, (ks & 3) * 2 + ((lane >> 3) & 1))), b0, b1,
+                    b2, b3);
+            uint32_t a0, a1, a2, a3;
+            if constexpr (kQInRegs) {
+                a0 = qf[ks][0], a1 = qf[ks][1], a2 = qf[ks][2], a3 = qf[ks][3];
+            } else {
+                ldsm_x4(smem_addr(qs + (ks >> 2) * 2048 + sw128(lane & 15, (ks & 3) * 2 + (lane >> 4))), a0, a1, a2,
+                        a3);
+            }
+            mma_16816(sacc[0], a0, a1, a2, a3, b0, b1);
+            mma_16816(sacc[1], a0, a1, a2, a3, b2, b3);
+        }
+
+        // Scores -> masked, scaled (log2 units), online softmax per row.
+        float mx[2] = {-CUDART_INF_F, -CUDART_INF_F};
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = key0 + nt * 8 + 2 * qc + (e & 1);
+                const int hi = e < 2 ? hiA : hiB, lo = e < 2 ? loA : loB;
+                float x = sacc[nt][e];
+                if (use_cap)
+                    x = a.softcap * tanhf(x * a.scale / a.softcap) * kLog2e;
+                else
+                    x = x * a.scale_log2;
+                x = (key >= lo && key <= hi && key < k_end) ? x : -CUDART_INF_F;
+                sacc[nt][e] = x;
+                mx[e >> 1] = fmaxf(mx[e >> 1], x);
+            }
+        float muse[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+            const float mnew = fmaxf(m2[r], mx[r]);
+            muse[r] = mnew == -CUDART_INF_F ? 0.f : mnew;
+            const float alpha = exp2f(m2[r] - muse[r]);
+            m2[r] = mnew;
+            lsum[r] *= alpha;
+#pragma unroll
+            for (int n = 0; n < NTO; ++n) {
+                o[n][2 * r] *= alpha;
+                o[n][2 * r + 1] *= alpha;
+            }
+        }
+        float p[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                p[nt][e] = exp2f(sacc[nt][e] - muse[e >> 1]);
+                lsum[e >> 1] += p[nt][e];
+            }
+        const uint32_t pa0 = pack_half2(p[0][0], p[0][1]);
+        const uint32_t pa1 = pack_half2(p[0][2], p[0][3]);
+        const uint32_t pa2 = pack_half2(p[1][0], p[1][1]);
+        const uint32_t pa3 = pack_half2(p[1][2], p[1][3]);
+
+        // Keys past the range end get zero V rows, so that 0 * (whatever the tile read) stays 0.
+        const bool tail = key0 + kKeysPerWarp > k_end;
+        if (tail) {
+            const int first = max(k_end - key0, 0);
+            for (int idx = lane; idx < (kKeysPerWarp - first) * (D / 8); idx += 32) {
+                const int rl = first + idx / (D / 8), ch = idx % (D / 8);
+                *reinterpret_cast<uint4 *>(vt + (ch >> 3) * L::kBoxBytes + sw128(warp * kKeysPerWarp + rl, ch & 7)) =
+                    make_uint4(0u, 0u, 0u, 0u);
+            }
+            __syncwarp();
+        }
+
+        // O += P V (16 keys), V fragments through ldmatrix.trans.
+        const int vrow = warp * kKeysPerWarp + (((lane >> 3) & 1) << 3) + (lane & 7);
+#pragma unroll
+        for (int np = 0; np < NTO / 2; ++np) {
+            const int chunk = np * 2 + (lane >> 4);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(smem_addr(vt + (chunk >> 3) * L::kBoxBytes + sw128(vrow, chunk & 7)), b0, b1, b2, b3);
+            mma_16816(o[2 * np], pa0, pa1, pa2, pa3, b0, b1);
+            mma_16816(o[2 * np + 1], pa0, pa1, pa2, pa3, b2, b3);
+        }
+        if (tail) fence_proxy_async_smem();  // generic writes before the next TMA into this slot
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    // ---- merge the four warps' (m, l, O) in shared memory (the ring is free now).
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], 1);
+        lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], 2);
+    }
+    named_barrier_sync(1, kConsumerWarps * 32);
+    float *cm = reinterpret_cast<float *>(ring);             // [warp][16]
+    float *cl = cm + kConsumerWarps * 16;                     // [warp][16]
+    float *co = cl + kConsumerWarps * 16;                     // [warp][16][D]
+    if (qc == 0) {
+        cm[warp * 16 + qr] = m2[0];
+        cm[warp * 16 + qr + 8] = m2[1];
+        cl[warp * 16 + qr] = lsum[0];
+        cl[warp * 16 + qr + 8] = lsum[1];
+    }
+#pragma unroll
+    for (int n = 0; n < NTO; ++n) {
+        const int d = n * 8 + 2 * qc;
+        *reinterpret_cast<float2 *>(co + (warp * 16 + qr) * D + d) = make_float2(o[n][0], o[n][1]);
+        *reinterpret_cast<float2 *>(co + (warp * 16 + qr + 8) * D + d) = make_float2(o[n][2], o[n][3]);
+    }
+    named_barrier_sync(1, kConsumerWarps * 32);
+
+    const int nvalid = min(16, nrows - row0);
+    const int rows_total = a.B * T * a.Hq;
+    for (int idx = threadIdx.x; idx < nvalid * D; idx += kConsumerWarps * 32) {
+        const int r = idx / D, d = idx % D;
+        float M = -CUDART_INF_F;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, cm[w * 16 + r]);
+        float Lsum = 0.f, O = 0.f;
+        if (M != -CUDART_INF_F) {
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) {
+                const float f = exp2f(cm[w * 16 + r] - M);
+                Lsum += cl[w * 16 + r] * f;
+                O += co[(w * 16 + r) * D + d] * f;
+            }
+        }
+        const int rr = row0 + r;
+        const int t = rr / G, h = kvh * G + rr % G;
+        const size_t R = ((size_t)b * T + t) * a.Hq + h;
+        if (a.out) {
+            a.out[R * D + d] = O / Lsum;
+        } else {
+            const size_t PR = (size_t)split * rows_total + R;
+            a.part_o[PR * D + d] = O;
+            if (d == 0) {
+                a.part_ml[PR * 2] = M == -CUDART_INF_F ? -CUDART_INF_F : M * kLn2;
+                a.part_ml[PR * 2 + 1] = Lsum;
+            }
+        }
+    }
+}
+
+// Log-sum-exp merge of partials: one warp per row.
+__global__ void combine_kernel(const __grid_constant__ CombineArgs a) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= a.rows) return;
+    float M = -CUDART_INF_F;
+    for (int p = 0; p < a.n_parts; ++p) M = fmaxf(M, a.part_ml[((size_t)p * a.rows + warp) * 2]);
+    // Partials with no key (m = -inf) carry weight 0; so does everything when no part has a key.
+    float Lsum = 0.f;
+    if (M != -CUDART_INF_F)
+        for (int p = 0; p < a.n_parts; ++p) {
+            const float m = a.part_ml[((size_t)p * a.rows + warp) * 2];
+            if (m != -CUDART_INF_F) Lsum += a.part_ml[((size_t)p * a.rows + warp) * 2 + 1] * expf(m - M);
+        }
+    for (int d = lane; d < a.D; d += 32) {
+        float O = 0.f;
+        if (M != -CUDART_INF_F)
+            for (int p = 0; p < a.n_parts; ++p) {
+                const float m = a.part_ml[((size_t)p * a.rows + warp) * 2];
+                if (m != -CUDART_INF_F) O += a.part_o[((size_t)p * a.rows + warp) * a.D + d] * expf(m - M);
+            }
+        if (a.out) {
+            a.out[(size_t)warp * a.D + d] = O / Lsum;
+        } else {
+            a.out_o[(size_t)warp * a.D + d] = O;
+            if (d == 0) {
+                a.out_ml[(size_t)warp * 2] = M;
+                a.out_ml[(size_t)warp * 2 + 1] = Lsum;
+            }
+        }
+    }
+}
+
+template <int D>
+cudaError_t launch_decode_t(const CUtensorMap &tmk, const CUtensorMap &tmv, const DecodeArgs &a, dim3 grid,
+                            cudaStream_t s) {
+    static unsigned long long configured = 0;  // one bit per device: the opt-in is per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64 || !(configured & (1ull << dev))) {
+        cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             DecodeLayout<D>::kSmemBytes);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) configured |= 1ull << dev;
+    }
+    decode_attn_kernel<D><<<grid, (kConsumerWarps + 1) * 32, DecodeLayout<D>::kSmemBytes, s>>>(tmk, tmv, a);
+    return cudaGetLastError();
+}
+
+template <int D>
+int ctas_per_sm_t() {
+    static int n = 0;
+    if (n == 0) {
+        cudaFuncSetAttribute(decode_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             DecodeLayout<D>::kSmemBytes);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_attn_kernel<D>, (kConsumerWarps + 1) * 32,
+                                                          DecodeLayout<D>::kSmemBytes) != cudaSuccess ||
+            n < 1)
+            n = 1;
+    }
+    return n;
+}
+
+}  // namespace
+
+int decode_stage_keys(int) { return kStageKeys; }
+
+int decode_ctas_per_sm(int head_dim) {
+    switch (head_dim) {
+        case 64: return ctas_per_sm_t<64>();
+        case 128: return ctas_per_sm_t<128>();
+        case 256: return ctas_per_sm_t<256>();
+        default: return 1;
+    }
+}
+
+cudaError_t launch_decode(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const DecodeArgs &a,
+                          int grid_x, int grid_y, int grid_z, cudaStream_t s) {
+    const dim3 grid(grid_x, grid_y, grid_z);
+    switch (head_dim) {
+        case 64: return launch_decode_t<64>(tmk, tmv, a, grid, s);
+        case 128: return launch_decode_t<128>(tmk, tmv, a, grid, s);
+        case 256: return launch_decode_t<256>(tmk, tmv, a, grid, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_combine(const CombineArgs &a, cudaStream_t s) {
+    if (a.rows == 0) return cudaSuccess;
+    const int threads = 256;
+    const long long blocks = ((long long)a.rows * 32 + threads - 1) / threads;
+    combine_kernel<<<(unsigned)blocks, threads, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace brk

@@ -1,0 +1,376 @@
+"""Host side of the attention operator: a mirror of the reference engine's attention / KV-cache
+surface (``WebGpuEngine`` in src/lib/webgpu/kernels.ts) over the C ABI of libbrk_attn.
+
+The reference host is TypeScript; no JavaScript runtime exists in this image, so the host layer
+is written in Python with the reference's method names and argument meanings:
+
+* readback twins used by selfValidate -- ``attention`` (kernels.ts:610), ``attentionDecode``
+  (:624), ``rope`` (:556), ``ropeFactors`` (:568), ``rmsnorm`` (:428): numpy in, numpy out;
+* the resident path -- ``ensureKv`` / ``setKvQuant`` / ``clearKvCache`` (:1760-1806), the
+  session check of ``runDecodeGpu`` (:1817-1825), ``recAttention`` (:1626) and the attention
+  slice of ``recordLayerKV`` (:1707-1731): device tensors in, device tensors out.
+
+PyTorch only provides device memory and streams here; every computation runs in the library's
+CUDA kernels.  Errors raise ``BrkError`` (the library has no fallback path).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from ._lib import BrkError, check
+
+_SUPPORTED_DIMS = (64, 128, 256)
+
+
+def _stream_ptr(stream: Optional[torch.cuda.Stream] = None) -> ctypes.c_void_p:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _positions(past_len, batch: int):
+    arr = (ctypes.c_int32 * batch)()
+    vals = [int(past_len)] * batch if np.isscalar(past_len) else [int(x) for x in past_len]
+    if len(vals) != batch:
+        raise BrkError(L.BRK_ERR_INVALID, f"past_len has {len(vals)} entries for batch {batch}")
+    for i, v in enumerate(vals):
+        arr[i] = v
+    return arr
+
+
+class Context:
+    """One library context per GPU (the engine instance of kernels.ts:100)."""
+
+    def __init__(self, device: int = 0):
+        self.device = int(device)
+        h = ctypes.c_void_p()
+        check(L.lib().brk_ctx_create(self.device, ctypes.byref(h)))
+        self.handle = h
+
+    def check(self, stream=None) -> None:
+        """Synchronise and raise if a kernel gave up on a bounded wait."""
+        check(L.lib().brk_ctx_check(self.handle, _stream_ptr(stream)))
+
+    @property
+    def launches(self) -> int:
+        """Kernels launched through this context so far."""
+        return int(L.lib().brk_ctx_launches(self.handle))
+
+    def reserve(self, nbytes: int) -> None:
+        check(L.lib().brk_ctx_reserve(self.handle, int(nbytes)))
+
+    def close(self) -> None:
+        if self.handle:
+            L.lib().brk_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class RopeTable:
+    """NeoX RoPE cos/sin table (rope / rope_factors, shaders.ts:1361-1408) for positions
+    [0, max_positions), built on the host in double exactly like ropeCpu."""
+
+    def __init__(self, ctx: Context, head_dim: int, base: float, ff: Optional[Sequence[float]] = None,
+                 max_positions: int = 4096):
+        self.ctx, self.head_dim, self.base = ctx, head_dim, float(base)
+        h = ctypes.c_void_p()
+        ffp = None
+        if ff is not None:
+            self._ff = np.ascontiguousarray(ff, dtype=np.float32)
+            ffp = self._ff.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        check(L.lib().brk_rope_create(ctx.handle, head_dim, self.base, ffp, int(max_positions), ctypes.byref(h)))
+        self.handle = h
+        self.max_positions = int(max_positions)
+
+    def close(self):
+        if self.handle:
+            L.lib().brk_rope_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def llama3_rope_factors(head_dim: int, base: float, factor: float, low_freq_factor: float,
+                        high_freq_factor: float, original_context: int) -> np.ndarray:
+    """Divisors ff[i] of the llama3 RoPE scaling (what rope_freqs.weight holds, model.ts:590)."""
+    ff = np.zeros(head_dim // 2, np.float32)
+    check(L.lib().brk_llama3_rope_factors(head_dim, float(base), float(factor), float(low_freq_factor),
+                                          float(high_freq_factor), int(original_context),
+                                          ff.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
+    return ff
+
+
+class KvCache:
+    """Persistent fp16 KV cache of ``n_layers`` layers x ``batch`` sequences (KvEntry,
+    kernels.ts:93), head-major in HBM."""
+
+    def __init__(self, ctx: Context, n_layers: int, batch: int, n_kv_heads: int, head_dim: int, capacity: int):
+        self.ctx = ctx
+        self.n_layers, self.batch, self.n_kv_heads, self.head_dim = n_layers, batch, n_kv_heads, head_dim
+        desc = L.KvDesc(n_layers, batch, n_kv_heads, head_dim, int(capacity), L.BRK_KV_F16)
+        h = ctypes.c_void_p()
+        check(L.lib().brk_kv_create(ctx.handle, ctypes.byref(desc), ctypes.byref(h)))
+        self.handle = h
+
+    @property
+    def capacity(self) -> int:
+        return L.lib().brk_kv_capacity(self.handle)
+
+    def grow(self, rows: int, stream=None) -> None:
+        """ensureKv growth rule: capacity -> max(rows, capacity + 1024, 1024) when rows > capacity."""
+        check(L.lib().brk_kv_grow(self.handle, int(rows), _stream_ptr(stream)))
+
+    def reset(self, stream=None) -> None:
+        check(L.lib().brk_kv_reset(self.handle, _stream_ptr(stream)))
+
+    def write_rows(self, layer: int, seq: int, row0: int, k: torch.Tensor, v: torch.Tensor, stream=None) -> None:
+        n = k.shape[0]
+        check(L.lib().brk_kv_write_rows(self.handle, layer, seq, row0, n, _ptr(k.contiguous()), _ptr(v.contiguous()),
+                                        _stream_ptr(stream)))
+
+    def read_rows(self, layer: int, seq: int, row0: int, n_rows: int, stream=None):
+        """Rows in the reference's token-major layout [n_rows, n_kv_heads, D] as float16 tensors."""
+        dev = torch.device("cuda", self.ctx.device)
+        k = torch.empty((n_rows, self.n_kv_heads, self.head_dim), dtype=torch.int16, device=dev)
+        v = torch.empty_like(k)
+        check(L.lib().brk_kv_read_rows(self.handle, layer, seq, row0, n_rows, _ptr(k), _ptr(v), _stream_ptr(stream)))
+        return k.view(torch.float16), v.view(torch.float16)
+
+    def close(self):
+        if self.handle:
+            L.lib().brk_kv_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+@dataclass
+class AttnConfig:
+    """LayerCfg's attention fields (kernels.ts:24-56) plus the extensions of this build."""
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    scale: Optional[float] = None       # attnScale; None -> 1/sqrt(head_dim)
+    softcap: float = 0.0                # attnLogitSoftcap
+    window: int = 0                     # sliding window (0 = global)
+    eps: float = 1e-6
+    one_plus: bool = False              # rmsGainOnePlus
+    q_norm: Optional[torch.Tensor] = None   # device [head_dim] f32
+    k_norm: Optional[torch.Tensor] = None
+    rope: Optional[RopeTable] = None
+    kv_offset: int = 0
+
+    def params(self) -> L.AttnParams:
+        return L.AttnParams(self.n_heads, self.n_kv_heads, self.head_dim,
+                            0.0 if self.scale is None else float(self.scale), float(self.softcap or 0.0),
+                            int(self.window or 0), int(self.kv_offset), int(bool(self.one_plus)), float(self.eps),
+                            _ptr(self.q_norm), _ptr(self.k_norm), self.rope.handle.value if self.rope else None)
+
+
+class AttentionEngine:
+    """Mirror of WebGpuEngine's attention / KV-cache methods (kernels.ts:556-704, 1626-1825)."""
+
+    def __init__(self, device: int = 0):
+        self.device = torch.device("cuda", device)
+        self.ctx = Context(device)
+        # ?attndecode=0 kill switch (kernels.ts:181-215) -> BRK_ATTN_DECODE=0.
+        self.attnDecodeOk = os.environ.get("BRK_ATTN_DECODE", "1") != "0"
+        self.kvGpu: Optional[KvCache] = None
+        self.kvSession = ""
+        self.kvQuant = False
+
+    # ---- plumbing ---------------------------------------------------------------------
+    def _dev(self, a) -> torch.Tensor:
+        return torch.as_tensor(np.ascontiguousarray(a, dtype=np.float32)).to(self.device)
+
+    @staticmethod
+    def _host(t: torch.Tensor) -> np.ndarray:
+        return t.detach().float().cpu().numpy().ravel()
+
+    # ---- readback twins (selfValidate surface) ------------------------------------------
+    def _attention_readback(self, q, k, v, nTokens, nHeads, nKvHeads, headDim, pastLen, scale, softcap, kernel,
+                            window=0):
+        kvLen = pastLen + nTokens
+        D = next((d for d in _SUPPORTED_DIMS if d >= headDim), None)
+        if D is None:
+            raise BrkError(L.BRK_ERR_UNSUPPORTED, f"head_dim {headDim} > 256")
+        sc = float(scale) if scale is not None else 1.0 / math.sqrt(headDim)
+
+        def pad(a, rows, heads):
+            a = np.asarray(a, np.float32).reshape(rows, heads, headDim)
+            if D == headDim:
+                return a
+            out = np.zeros((rows, heads, D), np.float32)
+            out[..., :headDim] = a  # zero lanes add nothing to q.k and produce unused outputs
+            return out
+
+        qd = self._dev(pad(q, nTokens, nHeads))
+        kd = self._dev(pad(k, kvLen, nKvHeads))
+        vd = self._dev(pad(v, kvLen, nKvHeads))
+        kv = KvCache(self.ctx, 1, 1, nKvHeads, D, kvLen)
+        kv.write_rows(0, 0, 0, kd, vd)
+        cfg = AttnConfig(nHeads, nKvHeads, D, scale=sc, softcap=softcap, window=window)
+        out = torch.empty((nTokens, nHeads, D), dtype=torch.float32, device=self.device)
+        self.recAttention(kv, 0, cfg, qd, out, pastLen, kernel=kernel)
+        self.ctx.check()
+        kv.close()
+        return out[..., :headDim].cpu().numpy().ravel()
+
+    def attention(self, q, k, v, nTokens, nHeads, nKvHeads, headDim, pastLen=0, scale=None, softcap=0.0):
+        """kernels.ts:610 — causal GQA attention; k/v [kvLen, nKvHeads, headDim] f32 (stored as fp16)."""
+        return self._attention_readback(q, k, v, nTokens, nHeads, nKvHeads, headDim, pastLen, scale, softcap, "auto")
+
+    def attentionDecode(self, q, k, v, nTokens, nHeads, nKvHeads, headDim, pastLen=0, scale=None, softcap=0.0):
+        """kernels.ts:624 — the same through the decode kernel."""
+        return self._attention_readback(q, k, v, nTokens, nHeads, nKvHeads, headDim, pastLen, scale, softcap,
+                                        "decode")
+
+    def _q_prologue(self, x, rows, headDim, nHeads, pastLen, rope, gain, eps, onePlus):
+        if rows % nHeads:
+            raise BrkError(L.BRK_ERR_INVALID, "rows must be a multiple of nHeads")
+        xd = self._dev(x)
+        out = torch.empty_like(xd)
+        cfg = AttnConfig(nHeads, 1, headDim, eps=eps, one_plus=onePlus, q_norm=gain, rope=rope)
+        p = cfg.params()
+        pos = _positions([pastLen], 1)
+        check(L.lib().brk_attn_append(self.ctx.handle, None, 0, ctypes.byref(p), 1, rows // nHeads, pos, _ptr(xd),
+                                      None, None, _ptr(out), _stream_ptr()))
+        self.ctx.check()
+        return self._host(out)
+
+    def rope(self, x, rows, headDim, nHeads, pastLen=0, base=10000.0):
+        """kernels.ts:556 — NeoX RoPE of x [rows = seq*nHeads, headDim] at pastLen + row/nHeads."""
+        table = RopeTable(self.ctx, headDim, base, None, pastLen + rows // nHeads)
+        return self._q_prologue(x, rows, headDim, nHeads, pastLen, table, None, 1e-6, False)
+
+    def ropeFactors(self, x, ff, rows, headDim, nHeads, pastLen=0, base=10000.0):
+        """kernels.ts:568 — RoPE with per-frequency divisors ff [headDim/2]."""
+        table = RopeTable(self.ctx, headDim, base, ff, pastLen + rows // nHeads)
+        return self._q_prologue(x, rows, headDim, nHeads, pastLen, table, None, 1e-6, False)
+
+    def rmsnorm(self, x, w, rows, dim, eps=1e-5, onePlus=False):
+        """kernels.ts:428 — RMSNorm of x [rows, dim] with gain w (per-head QK-norm when dim = headDim)."""
+        return self._q_prologue(x, rows, dim, 1, 0, None, self._dev(w), eps, onePlus)
+
+    # ---- KV manager (kernels.ts:1749-1806) ----------------------------------------------
+    def setKvQuant(self, q8: bool) -> None:
+        if q8:
+            raise BrkError(L.BRK_ERR_UNSUPPORTED, "int8 KV cache is not built in this version (fp16 only)")
+        if self.kvQuant != q8:
+            self.kvQuant = q8
+            self.resetKvGpu()
+
+    def resetKvGpu(self) -> None:
+        if self.kvGpu is not None:
+            self.kvGpu.close()
+        self.kvGpu = None
+        self.kvSession = ""
+
+    def clearKvCache(self) -> None:
+        self.resetKvGpu()
+
+    def ensureKv(self, n_layers: int, rows: int, batch: int, n_kv_heads: int, head_dim: int) -> KvCache:
+        """Cache holding >= rows rows for every layer; grows to max(rows, cap + 1024, 1024)."""
+        kv = self.kvGpu
+        if kv is not None and (kv.n_layers, kv.batch, kv.n_kv_heads, kv.head_dim) != (n_layers, batch, n_kv_heads,
+                                                                                      head_dim):
+            self.resetKvGpu()
+            kv = None
+        if kv is None:
+            kv = KvCache(self.ctx, n_layers, batch, n_kv_heads, head_dim, max(rows, 1024))
+            self.kvGpu = kv
+        elif kv.capacity < rows:
+            kv.grow(rows)
+        return kv
+
+    def session(self, session_id: str, past_len) -> None:
+        """runDecodeGpu's session rule (kernels.ts:1817-1825): a new session id or pastLen 0
+        resets the cache; pastLen > 0 on an unknown session means the cache is lost (raised)."""
+        first = int(past_len) if np.isscalar(past_len) else int(min(past_len))
+        if session_id != self.kvSession or first == 0:
+            if first > 0:
+                raise BrkError(L.BRK_ERR_INVALID,
+                               f'session "{session_id}" unknown with pastLen={first}: cache lost, restart at 0')
+            self.resetKvGpu()
+            self.kvSession = session_id
+
+    # ---- resident path ------------------------------------------------------------------
+    def recAttention(self, kv: KvCache, layer: int, cfg: AttnConfig, q: torch.Tensor, out: torch.Tensor, past_len,
+                     kernel: str = "auto", stream=None) -> torch.Tensor:
+        """recAttention (kernels.ts:1626): q [B, T, Hq, D] f32 (rotated) -> out [B, T, Hq, D] f32."""
+        B = kv.batch
+        T = q.numel() // (B * cfg.n_heads * cfg.head_dim)
+        p = cfg.params()
+        pos = _positions(past_len, B)
+        if kernel == "auto" and not self.attnDecodeOk:
+            kernel = "prefill"
+        fn = {"auto": L.lib().brk_attn_forward, "decode": L.lib().brk_attn_decode,
+              "prefill": L.lib().brk_attn_prefill}[kernel]
+        check(fn(self.ctx.handle, kv.handle, layer, ctypes.byref(p), B, T, pos, _ptr(q), _ptr(out), _stream_ptr(stream)))
+        return out
+
+    def appendKv(self, kv: KvCache, layer: int, cfg: AttnConfig, q_in: torch.Tensor, k_in: torch.Tensor,
+                 v_in: torch.Tensor, q_out: torch.Tensor, past_len, stream=None) -> torch.Tensor:
+        """QK-norm + RoPE of q and the new k, fp16 store of k and v at row pastLen
+        (kernels.ts:1707-1730)."""
+        B = kv.batch
+        T = q_in.numel() // (B * cfg.n_heads * cfg.head_dim)
+        p = cfg.params()
+        pos = _positions(past_len, B)
+        check(L.lib().brk_attn_append(self.ctx.handle, kv.handle, layer, ctypes.byref(p), B, T, pos, _ptr(q_in),
+                                      _ptr(k_in), _ptr(v_in), _ptr(q_out), _stream_ptr(stream)))
+        return q_out
+
+    def attentionLayer(self, kv: KvCache, layer: int, cfg: AttnConfig, q_in, k_in, v_in, past_len,
+                       q_work: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                       kernel: str = "auto", stream=None) -> torch.Tensor:
+        """The attention slice of recordLayerKV (kernels.ts:1707-1731): q/k/v projections in,
+        attention output out; K/V land in the cache."""
+        q_work = torch.empty_like(q_in) if q_work is None else q_work
+        out = torch.empty_like(q_in) if out is None else out
+        self.appendKv(kv, layer, cfg, q_in, k_in, v_in, q_work, past_len, stream)
+        return self.recAttention(kv, layer, cfg, q_work, out, past_len, kernel, stream)
+
+    def decodePartial(self, kv: KvCache, layer: int, cfg: AttnConfig, q: torch.Tensor, part_ml: torch.Tensor,
+                      part_o: torch.Tensor, past_len, stream=None):
+        """Split-KV partial (m, l, o) of this cache's rows (sequence-sharded contexts)."""
+        B = kv.batch
+        T = q.numel() // (B * cfg.n_heads * cfg.head_dim)
+        p = cfg.params()
+        pos = _positions(past_len, B)
+        check(L.lib().brk_attn_decode_partial(self.ctx.handle, kv.handle, layer, ctypes.byref(p), B, T, pos, _ptr(q),
+                                              _ptr(part_ml), _ptr(part_o), _stream_ptr(stream)))
+
+    def combine(self, n_parts: int, rows: int, head_dim: int, part_ml: torch.Tensor, part_o: torch.Tensor,
+                out: torch.Tensor, stream=None) -> torch.Tensor:
+        check(L.lib().brk_attn_combine(self.ctx.handle, n_parts, rows, head_dim, _ptr(part_ml), _ptr(part_o), _ptr(out),
+                                       _stream_ptr(stream)))
+        return out
+
+    def close(self):
+        self.resetKvGpu()
+        self.ctx.close()

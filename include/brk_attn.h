@@ -1,0 +1,168 @@
+/*
+ * brk_attn.h — C ABI of the B200 (sm_100a) attention operator for the Brimkern engine.
+ *
+ * Replaces the engine's attention / KV-cache operator path (RomainKH/Brimkern,
+ * src/lib/webgpu/kernels.ts): recAttention / recAttentionQ8 dispatch (:1626-1661), the f32 KV
+ * append (:1727-1730), the per-layer KV manager (:1749-1806) and the readback twins used by
+ * selfValidate (:556-704).  The WGSL kernels they launch (src/lib/webgpu/shaders.ts:1361-1944)
+ * are replaced by hand-written CUDA for sm_100a.
+ *
+ * Conventions
+ *   - Every entry point returns an int status: BRK_OK (0) or a negative BRK_ERR_* code; the
+ *     message of the last failure on the calling thread is brk_last_error().  Nothing aborts
+ *     and no C++ exception crosses the ABI.
+ *   - All tensor pointers are DEVICE pointers unless the parameter says "host".  Layouts are the
+ *     reference's (kernels.ts:608-609): q / out [batch][n_tokens][n_heads][head_dim] f32,
+ *     k / v inputs [batch][n_tokens][n_kv_heads][head_dim] f32.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).  Work is
+ *     stream-ordered; calls on one context come from one host thread at a time.
+ *   - Positions: token t of sequence b sits at absolute position past_len[b] + t and attends
+ *     keys [0, past_len[b] + t] (kernels.ts:1816, shaders.ts:1500), or the last `window` of
+ *     them when params->window > 0.
+ */
+#ifndef BRK_ATTN_H
+#define BRK_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BRK_ABI_VERSION 1
+#define BRK_MAX_BATCH 512 /* sequences per call (positions travel in the kernel parameters) */
+
+enum {
+    BRK_OK = 0,
+    BRK_ERR_INVALID = -1,     /* bad argument or unsupported shape */
+    BRK_ERR_CUDA = -2,        /* a CUDA runtime call failed */
+    BRK_ERR_CAPACITY = -3,    /* a position or row is beyond the cache / rope table */
+    BRK_ERR_UNSUPPORTED = -4, /* head_dim or dtype without a kernel */
+    BRK_ERR_DEVICE = -5       /* a kernel reported a bounded-wait timeout (brk_ctx_check) */
+};
+
+enum { BRK_KV_F16 = 0 };
+
+typedef struct brk_ctx brk_ctx;   /* one per GPU: device id, error flag, workspace */
+typedef struct brk_kv brk_kv;     /* persistent KV cache of n_layers layers (KvEntry, kernels.ts:93) */
+typedef struct brk_rope brk_rope; /* RoPE cos/sin table in HBM */
+
+typedef struct {
+    int n_layers;   /* layers held (the reference keys KvEntry by layer, kernels.ts:1749) */
+    int batch;      /* independent sequences */
+    int n_kv_heads;
+    int head_dim;   /* 64, 128 or 256 */
+    int capacity;   /* rows per (layer, sequence, kv head); brk_kv_grow enlarges it */
+    int dtype;      /* BRK_KV_F16 */
+} brk_kv_desc;
+
+/* Per-layer attention configuration: LayerCfg's attention fields (kernels.ts:24-56). */
+typedef struct {
+    int n_heads;
+    int n_kv_heads;      /* n_heads % n_kv_heads == 0 (GQA group = n_heads / n_kv_heads) */
+    int head_dim;
+    float scale;         /* attnScale; <= 0 selects 1/sqrt(head_dim) (kernels.ts:1627) */
+    float softcap;       /* attnLogitSoftcap; <= 0 disables s -> c*tanh(s/c) (shaders.ts:1490) */
+    int window;          /* sliding window in keys; <= 0 = global attention (extension) */
+    int kv_offset;       /* absolute position of cache row 0 (sequence-sharded caches); else 0 */
+    int norm_one_plus;   /* RMSNorm gain convention x*(1+w) (rmsGainOnePlus) */
+    double eps;          /* QK-norm epsilon (LayerCfg.eps) */
+    const float *q_norm; /* device [head_dim] per-head q RMSNorm gain, or NULL (kernels.ts:1708) */
+    const float *k_norm; /* device [head_dim] per-head k RMSNorm gain, or NULL (kernels.ts:1709) */
+    const brk_rope *rope; /* NeoX RoPE table, or NULL for no rotary embedding */
+} brk_attn_params;
+
+/* ---- errors / version -------------------------------------------------------------------- */
+const char *brk_last_error(void);
+int brk_abi_version(void);
+
+/* ---- context (the WebGpuEngine instance, kernels.ts:100) ------------------------------- */
+int brk_ctx_create(int device, brk_ctx **out);
+int brk_ctx_destroy(brk_ctx *ctx);
+/* Synchronises `stream` and reports BRK_ERR_DEVICE if any kernel of this context hit a wait
+ * limit since the last check (then clears the flag).  Mirrors the engine's health flags. */
+int brk_ctx_check(brk_ctx *ctx, void *stream);
+/* Pre-sizes the split-KV workspace (bytes) so that later calls allocate nothing. */
+int brk_ctx_reserve(brk_ctx *ctx, size_t bytes);
+/* Number of kernels this context has launched so far (diagnostics / benchmarks). */
+uint64_t brk_ctx_launches(const brk_ctx *ctx);
+
+/* ---- RoPE tables (rope / rope_factors, shaders.ts:1361-1408; ropeCpu kernels.ts:3428-3460) -
+ * cos/sin of pos / (base^(2i/D) * ff[i]) for pos in [0, max_positions), computed on the host in
+ * double exactly as the reference's CPU function does, so the device append reproduces it
+ * bit for bit.  ff_host: host [head_dim/2] divisors (rope_freqs.weight, model.ts:590-597) or
+ * NULL. */
+int brk_rope_create(brk_ctx *ctx, int head_dim, double base, const float *ff_host,
+                    int max_positions, brk_rope **out);
+int brk_rope_destroy(brk_rope *rope);
+int brk_rope_max_positions(const brk_rope *rope);
+/* Meta's published llama3 frequency scaling as divisors ff[i] (the values llama.cpp stores as
+ * rope_freqs.weight, which the reference reads at model.ts:590-597).  ff_out: host [head_dim/2]. */
+int brk_llama3_rope_factors(int head_dim, double base, double factor, double low_freq_factor,
+                            double high_freq_factor, int original_context, float *ff_out);
+
+/* ---- KV cache (ensureKv / resetKvGpu / clearKvCache, kernels.ts:1766-1806) ------------------
+ * Stored head-major, [layer][sequence][kv head][capacity][head_dim] fp16, zero-initialised. */
+int brk_kv_create(brk_ctx *ctx, const brk_kv_desc *desc, brk_kv **out);
+int brk_kv_destroy(brk_kv *kv);
+int brk_kv_capacity(const brk_kv *kv);
+/* ensureKv (kernels.ts:1782-1806): if rows > capacity, grow to max(rows, capacity+1024, 1024)
+ * with a device-side copy of the existing rows. */
+int brk_kv_grow(brk_kv *kv, int rows, void *stream);
+/* clearKvCache (kernels.ts:1777): zero every row. */
+int brk_kv_reset(brk_kv *kv, void *stream);
+/* Plain row store, f32 -> fp16 (round to nearest even), no norm or rotation: the f32 copy of
+ * kernels.ts:1729-1730 for callers that already hold final K/V.  k, v: [n_rows][n_kv_heads][D]. */
+int brk_kv_write_rows(brk_kv *kv, int layer, int seq, int row0, int n_rows, const float *k,
+                      const float *v, void *stream);
+/* Test hook: copy rows back in the reference's token-major layout as fp16 bit patterns.
+ * k_out, v_out: device [n_rows][n_kv_heads][D] uint16. */
+int brk_kv_read_rows(const brk_kv *kv, int layer, int seq, int row0, int n_rows,
+                     uint16_t *k_out, uint16_t *v_out, void *stream);
+
+/* ---- hot path ----------------------------------------------------------------------------- */
+/* KV append with the q/k prologue fused (kernels.ts:1707-1730): per-head RMSNorm of q and k
+ * (if gains are given), NeoX RoPE (if a table is given) at position past_len[b]+t, K and V
+ * stored as fp16 at cache row past_len[b]+t-kv_offset; the rotated q is written to q_out f32
+ * [B][T][Hq][D] for the attention call.  past_len: HOST [batch]. */
+int brk_attn_append(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, int batch,
+                    int n_tokens, const int32_t *past_len, const float *q_in, const float *k_in,
+                    const float *v_in, float *q_out, void *stream);
+
+/* recAttention (kernels.ts:1626-1641): attention of q [B][T][Hq][D] (already rotated) over
+ * cache rows [0, past_len[b]+t] -> out [B][T][Hq][D] f32.  Picks the decode kernel for small
+ * T*group, the tensor-core prefill kernel otherwise (env BRK_ATTN_DECODE=0 forces the latter,
+ * like ?attndecode=0, kernels.ts:181-215).  past_len: HOST [batch]. */
+int brk_attn_forward(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p,
+                     int batch, int n_tokens, const int32_t *past_len, const float *q, float *out,
+                     void *stream);
+/* The decode kernel alone (attention_decode, shaders.ts:1768-1851): one CTA per (sequence,
+ * kv head[, split]) so the whole query group shares each K/V read, split-KV + LSE combine. */
+int brk_attn_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p,
+                    int batch, int n_tokens, const int32_t *past_len, const float *q, float *out,
+                    void *stream);
+/* The tensor-core prefill kernel alone (replaces the 2-pass `attention`, shaders.ts:1482-1524):
+ * tcgen05.mma / TMEM tiles for QK^T and PV, causal with the chunk offset past_len. */
+int brk_attn_prefill(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p,
+                     int batch, int n_tokens, const int32_t *past_len, const float *q, float *out,
+                     void *stream);
+
+/* Split-KV partial over this cache's rows (extension, no reference counterpart; used to shard
+ * a long context across GPUs): per row R = (b*T + t)*Hq + h, part_ml[2R] = max score m (natural
+ * log units, -inf if no key), part_ml[2R+1] = sum l of exp(s - m), part_o[R*D..] = sum of
+ * exp(s - m) * v (unnormalised).  Keys are cache rows r at absolute position kv_offset + r. */
+int brk_attn_decode_partial(brk_ctx *ctx, const brk_kv *kv, int layer,
+                            const brk_attn_params *p, int batch, int n_tokens,
+                            const int32_t *past_len, const float *q, float *part_ml,
+                            float *part_o, void *stream);
+/* Log-sum-exp combine of n_parts partials laid out [n_parts][rows] (ml: 2 floats per row,
+ * o: head_dim floats per row) -> out [rows][head_dim] = sum e^{m-M} o / sum e^{m-M} l. */
+int brk_attn_combine(brk_ctx *ctx, int n_parts, int rows, int head_dim, const float *part_ml,
+                     const float *part_o, float *out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BRK_ATTN_H */

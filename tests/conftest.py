@@ -24,3 +24,15 @@ def golden():
     cases = json.load(open(os.path.join(here, "golden.json")))["cases"]
     return {c["name"]: (c, {k.split("/", 1)[1]: arrays[k] for k in arrays.files if k.startswith(c["name"] + "/")})
             for c in cases}
+
+
+@pytest.fixture(scope="session")
+def eng():
+    """One AttentionEngine (library context) on cuda:0 for the GPU tests."""
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from brimkern_b200.engine import AttentionEngine
+    e = AttentionEngine(0)
+    yield e
+    e.close()
