@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -152,9 +153,11 @@ int choose_splits(const brk_ctx *ctx, int head_dim, int units, int span) {
 }
 
 // The decode path (final output or a partial), splitting the key range over CTAs.
+// fixed_ws / fixed_bytes: when set, the split-KV partials go there and nothing is allocated
+// (brk_attn_decode_static); otherwise the context workspace is used and grown on demand.
 int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
                const int32_t *past_len, const float *q, float *out, float *part_ml, float *part_o, bool clamp_rows,
-               cudaStream_t stream) {
+               cudaStream_t stream, void *fixed_ws = nullptr, size_t fixed_bytes = 0) {
     const int D = p->head_dim, G = p->n_heads / p->n_kv_heads;
     brk::DecodeArgs a;
     memset(&a, 0, sizeof(a));
@@ -203,11 +206,20 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
         a.part_o = part_o;
     } else {
         const size_t need = (size_t)nsplit * rows * (2 + D) * sizeof(float);
-        if (need > ctx->ws_bytes) {
-            int rc = brk_ctx_reserve(ctx, need);
-            if (rc) return rc;
+        if (fixed_ws) {
+            if (need > fixed_bytes)
+                return fail(BRK_ERR_CAPACITY,
+                            "%d-way split-KV partials of %d rows need %zu bytes of scratch; the library's static "
+                            "scratch holds %zu (use brk_attn_decode, or fewer sequences per call)",
+                            nsplit, rows, need, fixed_bytes);
+            a.part_ml = static_cast<float *>(fixed_ws);
+        } else {
+            if (need > ctx->ws_bytes) {
+                int rc = brk_ctx_reserve(ctx, need);
+                if (rc) return rc;
+            }
+            a.part_ml = static_cast<float *>(ctx->ws);
         }
-        a.part_ml = static_cast<float *>(ctx->ws);
         a.part_o = a.part_ml + (size_t)nsplit * rows * 2;
     }
     cudaError_t e = brk::launch_decode(D, kv->tm_dec_k, kv->tm_dec_v, a, nsplit, p->n_kv_heads * a.mtiles, batch, stream);
@@ -235,6 +247,36 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
 namespace brk {
 int prefill_tile_keys() { return 128; }
 }  // namespace brk
+
+namespace {
+
+// Split-KV partials of brk_attn_decode_static.  A file-scope device array: every GPU that loads
+// this library holds BRK_DECODE_STATIC_SCRATCH_BYTES of it until the process exits, and all
+// calls on one GPU share it.
+static __device__ __align__(256) unsigned char g_decode_static_scratch[BRK_DECODE_STATIC_SCRATCH_BYTES];
+
+// Device address of the array on the current device.  In host code the symbol only names a
+// host-side stand-in, so the real address is looked up once per device (with that device
+// current) and cached.
+int static_scratch_address(void **out) {
+    static std::mutex mu;
+    static void *addr[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return fail(BRK_ERR_UNSUPPORTED, "device %d: static scratch supports devices 0..63", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_decode_static_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static decode scratch)");
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return BRK_OK;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -568,6 +610,20 @@ int brk_attn_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_pa
     DeviceGuard g(ctx->device);
     return run_decode(ctx, kv, layer, p, batch, n_tokens, past_len, q, out, nullptr, nullptr, false,
                       static_cast<cudaStream_t>(stream));
+}
+
+// No-allocation variant of brk_attn_decode (declared in brk_attn.h with the reasons).
+int brk_attn_decode_static(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch,
+                           int n_tokens, const int32_t *past_len, const float *q, float *out, void *stream) {
+    int rc = check_call(ctx, kv, layer, p, batch, n_tokens, past_len);
+    if (rc) return rc;
+    if (!q || !out) return fail(BRK_ERR_INVALID, "null q or out");
+    DeviceGuard g(ctx->device);
+    void *scratch = nullptr;
+    rc = static_scratch_address(&scratch);
+    if (rc) return rc;
+    return run_decode(ctx, kv, layer, p, batch, n_tokens, past_len, q, out, nullptr, nullptr, false,
+                      static_cast<cudaStream_t>(stream), scratch, BRK_DECODE_STATIC_SCRATCH_BYTES);
 }
 
 int brk_attn_prefill(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,

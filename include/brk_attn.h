@@ -142,6 +142,29 @@ int brk_attn_forward(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_p
 int brk_attn_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p,
                     int batch, int n_tokens, const int32_t *past_len, const float *q, float *out,
                     void *stream);
+/* No-allocation variant of brk_attn_decode.  No counterpart in the reference: it exists for
+ * callers of this library that cannot allocate device memory while they run attention -- for
+ * example serving hosts that hand nearly all of HBM to their own KV-cache pool at start-up (a
+ * later cudaMalloc would fail), or hosts whose decode loop must not stall on the device-wide
+ * synchronisation that cudaMalloc / cudaFree imply.  brk_attn_decode may grow the context's
+ * workspace the first time a call needs more split-KV partials; this entry point instead keeps
+ * the partials in a fixed array compiled into the library and calls no allocator.
+ *   - Same arguments, outputs and split choice as brk_attn_decode.  The caller still provides
+ *     q and out.
+ *   - The array holds BRK_DECODE_STATIC_SCRATCH_BYTES.  A call whose split-KV partials need
+ *     more (nsplit * batch * n_tokens * n_heads * (head_dim + 2) * 4 bytes) fails with
+ *     BRK_ERR_CAPACITY and a message giving both sizes.
+ *   - Every GPU that loads the library holds one such array until the process exits.
+ *   - The first call on each device looks up the array's device address (with that device
+ *     current); make that first call before any stream capture.
+ *   - All calls on a device share the array and it keeps the last call's contents.  Each call
+ *     writes every partial it reads before reading it, so nothing needs clearing, but calls
+ *     whose kernels overlap on the GPU (other streams, other contexts on the same device) race
+ *     on it: serialise them. */
+#define BRK_DECODE_STATIC_SCRATCH_BYTES (8u << 20)
+int brk_attn_decode_static(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p,
+                           int batch, int n_tokens, const int32_t *past_len, const float *q,
+                           float *out, void *stream);
 /* The tensor-core prefill kernel alone (replaces the 2-pass `attention`, shaders.ts:1482-1524):
  * tcgen05.mma / TMEM tiles for QK^T and PV, causal with the chunk offset past_len. */
 int brk_attn_prefill(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p,
