@@ -71,6 +71,7 @@ SIGNATURES = [
     ("brk_kv_write_rows", _i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     ("brk_kv_read_rows", _i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     ("brk_attn_append", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp, _vp, _vp]),
+    ("brk_attn_step", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp, _vp, _vp, _vp]),
     ("brk_attn_forward", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp]),
     ("brk_attn_decode", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp]),
     ("brk_attn_decode_static", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp]),

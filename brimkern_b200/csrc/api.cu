@@ -153,11 +153,15 @@ int choose_splits(const brk_ctx *ctx, int head_dim, int units, int span) {
 }
 
 // The decode path (final output or a partial), splitting the key range over CTAs.
-// fixed_ws / fixed_bytes: when set, the split-KV partials go there and nothing is allocated
+// Split-KV scratch layout: arrival counters (kept zero between launches), then the partials.
+size_t counters_bytes(int units) { return ((size_t)units * sizeof(int) + 255) / 256 * 256; }
+
+// fixed_ws / fixed_bytes: when set, the split-KV scratch goes there and nothing is allocated
 // (brk_attn_decode_static); otherwise the context workspace is used and grown on demand.
+// pdl: the decode kernel is a programmatic dependent of the append launched just before it.
 int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
                const int32_t *past_len, const float *q, float *out, float *part_ml, float *part_o, bool clamp_rows,
-               cudaStream_t stream, void *fixed_ws = nullptr, size_t fixed_bytes = 0) {
+               cudaStream_t stream, void *fixed_ws = nullptr, size_t fixed_bytes = 0, bool pdl = false) {
     const int D = p->head_dim, G = p->n_heads / p->n_kv_heads;
     brk::DecodeArgs a;
     memset(&a, 0, sizeof(a));
@@ -197,48 +201,42 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
     a.nsplit = nsplit;
     const int rows = batch * n_tokens * p->n_heads;
 
-    const bool direct = out != nullptr && nsplit == 1;
-    const bool direct_partial = out == nullptr && nsplit == 1;
-    if (direct) {
-        a.out = out;
-    } else if (direct_partial) {
+    if (nsplit == 1) {
+        a.out = out;  // final output, or (out == nullptr) the caller's partial buffer directly
         a.part_ml = part_ml;
         a.part_o = part_o;
     } else {
-        const size_t need = (size_t)nsplit * rows * (2 + D) * sizeof(float);
+        const size_t cbytes = counters_bytes(batch * p->n_kv_heads * a.mtiles);
+        const size_t need = cbytes + (size_t)nsplit * rows * (2 + D) * sizeof(float);
+        char *ws;
         if (fixed_ws) {
             if (need > fixed_bytes)
                 return fail(BRK_ERR_CAPACITY,
                             "%d-way split-KV partials of %d rows need %zu bytes of scratch; the library's static "
                             "scratch holds %zu (use brk_attn_decode, or fewer sequences per call)",
                             nsplit, rows, need, fixed_bytes);
-            a.part_ml = static_cast<float *>(fixed_ws);
+            ws = static_cast<char *>(fixed_ws);
+            // The counters must start at zero; the array keeps whatever the last call left.
+            cudaError_t e = cudaMemsetAsync(ws, 0, cbytes, stream);
+            if (e != cudaSuccess) return cuda_fail(e, "clearing the static split counters");
         } else {
             if (need > ctx->ws_bytes) {
                 int rc = brk_ctx_reserve(ctx, need);
                 if (rc) return rc;
             }
-            a.part_ml = static_cast<float *>(ctx->ws);
+            ws = static_cast<char *>(ctx->ws);
         }
+        a.counters = reinterpret_cast<int *>(ws);
+        a.part_ml = reinterpret_cast<float *>(ws + cbytes);
         a.part_o = a.part_ml + (size_t)nsplit * rows * 2;
+        a.out = out;
+        a.res_ml = part_ml;
+        a.res_o = part_o;
     }
-    cudaError_t e = brk::launch_decode(D, kv->tm_dec_k, kv->tm_dec_v, a, nsplit, p->n_kv_heads * a.mtiles, batch, stream);
+    cudaError_t e = brk::launch_decode(D, kv->tm_dec_k, kv->tm_dec_v, a, nsplit, p->n_kv_heads * a.mtiles, batch, stream,
+                                       pdl);
     if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
     ++ctx->launches;
-    if (!direct && !direct_partial) {
-        brk::CombineArgs c;
-        c.part_ml = a.part_ml;
-        c.part_o = a.part_o;
-        c.out = out;
-        c.out_ml = out ? nullptr : part_ml;
-        c.out_o = out ? nullptr : part_o;
-        c.n_parts = nsplit;
-        c.rows = rows;
-        c.D = D;
-        e = brk::launch_combine(c, stream);
-        if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
-        ++ctx->launches;
-    }
     return BRK_OK;
 }
 
@@ -325,6 +323,8 @@ int brk_ctx_check(brk_ctx *ctx, void *stream) {
     BRK_CUDA(cudaMemcpy(&err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (err) {
         BRK_CUDA(cudaMemset(ctx->d_err, 0, sizeof(int)));
+        // A kernel that gave up may have left split counters mid-count: start them from zero.
+        if (ctx->ws) BRK_CUDA(cudaMemset(ctx->ws, 0, ctx->ws_bytes));
         return fail(BRK_ERR_DEVICE, "a kernel gave up on a bounded wait (code %d)", err);
     }
     return BRK_OK;
@@ -341,6 +341,7 @@ int brk_ctx_reserve(brk_ctx *ctx, size_t bytes) {
     ctx->ws = nullptr;
     ctx->ws_bytes = 0;
     BRK_CUDA(cudaMalloc(&ctx->ws, bytes));
+    BRK_CUDA(cudaMemset(ctx->ws, 0, bytes));  // split counters start at zero
     ctx->ws_bytes = bytes;
     return BRK_OK;
 }
@@ -543,9 +544,10 @@ int brk_kv_read_rows(const brk_kv *kv, int layer, int seq, int row0, int n_rows,
     return e == cudaSuccess ? BRK_OK : cuda_fail(e, "kv read");
 }
 
-int brk_attn_append(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
-                    const int32_t *past_len, const float *q_in, const float *k_in, const float *v_in, float *q_out,
-                    void *stream) {
+namespace {
+int append_impl(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
+                const int32_t *past_len, const float *q_in, const float *k_in, const float *v_in, float *q_out,
+                void *stream, bool pdl) {
     if ((q_in == nullptr) != (q_out == nullptr)) return fail(BRK_ERR_INVALID, "q_in and q_out go together");
     if ((k_in == nullptr) != (v_in == nullptr)) return fail(BRK_ERR_INVALID, "k_in and v_in go together");
     if (kv) {
@@ -596,10 +598,36 @@ int brk_attn_append(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *
     a.layer = layer;
     a.cap = kv ? kv->cap : 0;
     a.kv_offset = p->kv_offset;
-    cudaError_t e = brk::launch_append(a, static_cast<cudaStream_t>(stream));
+    cudaError_t e = brk::launch_append(a, static_cast<cudaStream_t>(stream), pdl);
     if (e != cudaSuccess) return cuda_fail(e, "append kernel launch");
     ++ctx->launches;
     return BRK_OK;
+}
+}  // namespace
+
+int brk_attn_append(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
+                    const int32_t *past_len, const float *q_in, const float *k_in, const float *v_in, float *q_out,
+                    void *stream) {
+    return append_impl(ctx, kv, layer, p, batch, n_tokens, past_len, q_in, k_in, v_in, q_out, stream, false);
+}
+
+int brk_attn_step(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
+                  const int32_t *past_len, const float *q_in, const float *k_in, const float *v_in, float *q_work,
+                  float *out, void *stream) {
+    if (!q_in || !k_in || !v_in || !q_work || !out) return fail(BRK_ERR_INVALID, "null tensor argument");
+    int rc = check_call(ctx, kv, layer, p, batch, n_tokens, past_len);
+    if (rc) return rc;
+    if (n_tokens * (p->n_heads / p->n_kv_heads) > 64)
+        return fail(BRK_ERR_UNSUPPORTED, "brk_attn_step covers decode (n_tokens * group <= 64); use append + forward");
+    for (int b = 0; b < batch; ++b)
+        if (past_len[b] + n_tokens - p->kv_offset > kv->cap)
+            return fail(BRK_ERR_CAPACITY, "sequence %d needs %d cache rows, capacity is %d (grow the cache)", b,
+                        past_len[b] + n_tokens - p->kv_offset, kv->cap);
+    rc = append_impl(ctx, kv, layer, p, batch, n_tokens, past_len, q_in, k_in, v_in, q_work, stream, true);
+    if (rc) return rc;
+    DeviceGuard g(ctx->device);
+    return run_decode(ctx, kv, layer, p, batch, n_tokens, past_len, q_work, out, nullptr, nullptr, false,
+                      static_cast<cudaStream_t>(stream), nullptr, 0, true);
 }
 
 int brk_attn_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,

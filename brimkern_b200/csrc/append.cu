@@ -21,6 +21,10 @@ constexpr int kRowsPerBlock = 4;  // one warp per head-vector row
 
 __global__ void __launch_bounds__(kRowsPerBlock * 32) append_kernel(const __grid_constant__ AppendArgs a) {
     extern __shared__ float xs_all[];
+    // The dependent decode may be scheduled now (it waits for this grid before reading q or the
+    // new rows); this grid itself waits for whatever the stream ran before it.
+    griddep_launch_dependents();
+    griddep_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int D = a.D, half = D >> 1;
     const int per_tok = a.Hq + 2 * a.Hkv;
@@ -136,12 +140,20 @@ __global__ void kv_read_rows_kernel(const __half *kc, const __half *vc, uint16_t
 
 }  // namespace
 
-cudaError_t launch_append(const AppendArgs &a, cudaStream_t s) {
+cudaError_t launch_append(const AppendArgs &a, cudaStream_t s, bool pdl) {
     const long long rows = (long long)a.B * a.T * (a.Hq + 2 * a.Hkv);
     if (rows == 0) return cudaSuccess;
-    const unsigned grid = (unsigned)((rows + kRowsPerBlock - 1) / kRowsPerBlock);
-    append_kernel<<<grid, kRowsPerBlock * 32, kRowsPerBlock * a.D * sizeof(float), s>>>(a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((rows + kRowsPerBlock - 1) / kRowsPerBlock));
+    cfg.blockDim = dim3(kRowsPerBlock * 32);
+    cfg.dynamicSmemBytes = kRowsPerBlock * a.D * sizeof(float);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, append_kernel, a);
 }
 
 cudaError_t launch_kv_write_rows(__half *kc, __half *vc, const float *k, const float *v, int n_rows, int Hkv, int D,

@@ -49,7 +49,7 @@ struct DecodeLayout {
     static constexpr uint32_t kQBytes = kBlocks * 16 * 128;        // 16 rows of q, fp16, swizzled
     static constexpr uint32_t kBarBytes = 2 * DecodeCfg<D>::kStages * 8;
     static constexpr uint32_t kSmemBytes = 1024 + kRingBytes + kQBytes + kBarBytes;
-    static_assert(kConsumerWarps * 16 * D * 4 + 2 * kConsumerWarps * 16 * 4 <= kRingBytes,
+    static_assert(kConsumerWarps * 16 * D * 4 + 2 * kConsumerWarps * 16 * 4 + 16 + 32 * 4 + 16 * 64 * 4 <= kRingBytes,
                   "merge buffers must fit in the ring");
 };
 
@@ -98,34 +98,23 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, DecodeCfg<D>::kMinB
         }
         fence_barrier_init();
     }
-    // Stage this CTA's 16 q rows as fp16 in the same swizzled layout as the K boxes.
-    for (int idx = threadIdx.x; idx < 16 * (D / 8); idx += blockDim.x) {
-        const int r = idx / (D / 8), ch = idx % (D / 8);
-        const int rr = row0 + r;
-        float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
-        if (rr < nrows) {
-            const int t = rr / G, h = kvh * G + rr % G;
-            const float *src = a.q + (((size_t)b * T + t) * a.Hq + h) * D + ch * 8;
-            x0 = *reinterpret_cast<const float4 *>(src);
-            x1 = *reinterpret_cast<const float4 *>(src + 4);
-        }
-        uint4 pk;
-        pk.x = pack_half2(x0.x, x0.y);
-        pk.y = pack_half2(x0.z, x0.w);
-        pk.z = pack_half2(x1.x, x1.y);
-        pk.w = pack_half2(x1.z, x1.w);
-        *reinterpret_cast<uint4 *>(qs + (ch >> 3) * 2048 + sw128(r, ch & 7)) = pk;
-    }
-    __syncthreads();
-
+    __syncthreads();  // barrier initialisation visible to every warp
     if (warp == kConsumerWarps) {
         // ---- producer: one elected lane streams K/V tiles through the ring.
         if (lane == 0 && ntiles > 0) {
             tma_prefetch_desc(&tmk);
             tma_prefetch_desc(&tmv);
             int issued = 0;
+            bool waited = false;
+            // Rows from dep_row on may be written by a preceding kernel (the append, when this
+            // launch is its programmatic dependent): tiles touching them wait for it to finish.
+            const int dep_row = past - a.kv_offset;
             for (int i = 0; i < ntiles; ++i) {
                 const int s = i % S;
+                if (!waited && k_begin + (i + 1) * kStageKeys > dep_row) {
+                    griddep_wait();
+                    waited = true;
+                }
                 if (i >= S && !mbar_wait(&empty[s], ((i / S) - 1) & 1, a.err, kErrSlotTimeout)) break;
                 mbar_arrive_expect_tx(&full[s], L::kStageBytes);
                 uint8_t *st = ring + s * L::kStageBytes;
@@ -144,7 +133,28 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, DecodeCfg<D>::kMinB
         return;
     }
 
-    // ---- consumers
+    // ---- consumers: stage this CTA's 16 q rows as fp16, in the same swizzled layout as the K
+    // boxes (q comes from the preceding append when launched as its dependent).
+    griddep_wait();
+    for (int idx = threadIdx.x; idx < 16 * (D / 8); idx += kConsumerWarps * 32) {
+        const int r = idx / (D / 8), ch = idx % (D / 8);
+        const int rr = row0 + r;
+        float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
+        if (rr < nrows) {
+            const int t = rr / G, h = kvh * G + rr % G;
+            const float *src = a.q + (((size_t)b * T + t) * a.Hq + h) * D + ch * 8;
+            x0 = *reinterpret_cast<const float4 *>(src);
+            x1 = *reinterpret_cast<const float4 *>(src + 4);
+        }
+        uint4 pk;
+        pk.x = pack_half2(x0.x, x0.y);
+        pk.y = pack_half2(x0.z, x0.w);
+        pk.z = pack_half2(x1.x, x1.y);
+        pk.w = pack_half2(x1.z, x1.w);
+        *reinterpret_cast<uint4 *>(qs + (ch >> 3) * 2048 + sw128(r, ch & 7)) = pk;
+    }
+    named_barrier_sync(1, kConsumerWarps * 32);
+
     const int qr = lane >> 2, qc = lane & 3;
     uint32_t qf[kQInRegs ? KS : 1][4];
     if constexpr (kQInRegs) {
@@ -293,6 +303,8 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, DecodeCfg<D>::kMinB
 
     const int nvalid = min(16, nrows - row0);
     const int rows_total = a.B * T * a.Hq;
+    // (a) This CTA's (m, l, o) per row.  Single split: the final output (or the caller's
+    // partial); several splits: this split's partial in the workspace.
     for (int idx = threadIdx.x; idx < nvalid * D; idx += kConsumerWarps * 32) {
         const int r = idx / D, d = idx % D;
         float M = -CUDART_INF_F;
@@ -310,7 +322,7 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, DecodeCfg<D>::kMinB
         const int rr = row0 + r;
         const int t = rr / G, h = kvh * G + rr % G;
         const size_t R = ((size_t)b * T + t) * a.Hq + h;
-        if (a.out) {
+        if (a.nsplit == 1 && a.out) {
             a.out[R * D + d] = O / Lsum;
         } else {
             const size_t PR = (size_t)split * rows_total + R;
@@ -318,6 +330,59 @@ __global__ void __launch_bounds__((kConsumerWarps + 1) * 32, DecodeCfg<D>::kMinB
             if (d == 0) {
                 a.part_ml[PR * 2] = M == -CUDART_INF_F ? -CUDART_INF_F : M * kLn2;
                 a.part_ml[PR * 2 + 1] = Lsum;
+            }
+        }
+    }
+    griddep_launch_dependents();
+    if (a.nsplit == 1) return;
+
+    // (b) Split-KV: the last CTA to finish for this (sequence, kv head, row tile) merges every
+    // split's partial (threadfence-reduction pattern: release fence, counter, acquire fence).
+    __threadfence();
+    named_barrier_sync(1, kConsumerWarps * 32);
+    int *flag = reinterpret_cast<int *>(co + kConsumerWarps * 16 * D);
+    float *row_l = reinterpret_cast<float *>(flag + 4);  // [16]
+    float *row_m = row_l + 16;                            // [16]
+    float *wts = row_m + 16;                              // [16][nsplit]
+    if (threadIdx.x == 0) {
+        const int tile = (b * a.Hkv + kvh) * a.mtiles + mt;
+        const int prev = atomicAdd(&a.counters[tile], 1);
+        flag[0] = prev == a.nsplit - 1;
+        if (prev == a.nsplit - 1) a.counters[tile] = 0;  // every arrival is in: ready for the next launch
+    }
+    named_barrier_sync(1, kConsumerWarps * 32);
+    if (!flag[0]) return;
+    __threadfence();
+    for (int r = threadIdx.x; r < nvalid; r += kConsumerWarps * 32) {
+        const int rr = row0 + r;
+        const size_t R = ((size_t)b * T + rr / G) * a.Hq + kvh * G + rr % G;
+        float M = -CUDART_INF_F;
+        for (int sp = 0; sp < a.nsplit; ++sp) M = fmaxf(M, __ldcg(&a.part_ml[((size_t)sp * rows_total + R) * 2]));
+        float Lsum = 0.f;
+        for (int sp = 0; sp < a.nsplit; ++sp) {
+            const float m = __ldcg(&a.part_ml[((size_t)sp * rows_total + R) * 2]);
+            const float w = m == -CUDART_INF_F ? 0.f : expf(m - M);
+            wts[r * a.nsplit + sp] = w;
+            Lsum += w * __ldcg(&a.part_ml[((size_t)sp * rows_total + R) * 2 + 1]);
+        }
+        row_l[r] = Lsum;
+        row_m[r] = M;
+    }
+    named_barrier_sync(1, kConsumerWarps * 32);
+    for (int idx = threadIdx.x; idx < nvalid * D; idx += kConsumerWarps * 32) {
+        const int r = idx / D, d = idx % D;
+        const int rr = row0 + r;
+        const size_t R = ((size_t)b * T + rr / G) * a.Hq + kvh * G + rr % G;
+        float O = 0.f;
+        for (int sp = 0; sp < a.nsplit; ++sp)
+            O += wts[r * a.nsplit + sp] * __ldcg(&a.part_o[((size_t)sp * rows_total + R) * D + d]);
+        if (a.out) {
+            a.out[R * D + d] = O / row_l[r];
+        } else {
+            a.res_o[R * D + d] = O;
+            if (d == 0) {
+                a.res_ml[R * 2] = row_m[r];
+                a.res_ml[R * 2 + 1] = row_l[r];
             }
         }
     }
@@ -357,7 +422,7 @@ __global__ void combine_kernel(const __grid_constant__ CombineArgs a) {
 
 template <int D>
 cudaError_t launch_decode_t(const CUtensorMap &tmk, const CUtensorMap &tmv, const DecodeArgs &a, dim3 grid,
-                            cudaStream_t s) {
+                            cudaStream_t s, bool pdl) {
     static unsigned long long configured = 0;  // one bit per device: the opt-in is per device
     int dev = 0;
     cudaGetDevice(&dev);
@@ -367,8 +432,17 @@ cudaError_t launch_decode_t(const CUtensorMap &tmk, const CUtensorMap &tmv, cons
         if (e != cudaSuccess) return e;
         if (dev < 64) configured |= 1ull << dev;
     }
-    decode_attn_kernel<D><<<grid, (kConsumerWarps + 1) * 32, DecodeLayout<D>::kSmemBytes, s>>>(tmk, tmv, a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3((kConsumerWarps + 1) * 32);
+    cfg.dynamicSmemBytes = DecodeLayout<D>::kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, decode_attn_kernel<D>, tmk, tmv, a);
 }
 
 template <int D>
@@ -399,12 +473,12 @@ int decode_ctas_per_sm(int head_dim) {
 }
 
 cudaError_t launch_decode(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const DecodeArgs &a,
-                          int grid_x, int grid_y, int grid_z, cudaStream_t s) {
+                          int grid_x, int grid_y, int grid_z, cudaStream_t s, bool pdl) {
     const dim3 grid(grid_x, grid_y, grid_z);
     switch (head_dim) {
-        case 64: return launch_decode_t<64>(tmk, tmv, a, grid, s);
-        case 128: return launch_decode_t<128>(tmk, tmv, a, grid, s);
-        case 256: return launch_decode_t<256>(tmk, tmv, a, grid, s);
+        case 64: return launch_decode_t<64>(tmk, tmv, a, grid, s, pdl);
+        case 128: return launch_decode_t<128>(tmk, tmv, a, grid, s, pdl);
+        case 256: return launch_decode_t<256>(tmk, tmv, a, grid, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -54,9 +54,12 @@ struct AppendArgs {
 
 struct DecodeArgs {
     const float *q;       // [B][T][Hq][D] f32
-    float *out;           // [B][T][Hq][D] f32 (final mode) or nullptr
-    float *part_ml;       // [nsplit][B*T*Hq][2] (partial mode) or nullptr
-    float *part_o;        // [nsplit][B*T*Hq][D]
+    float *out;           // [B][T][Hq][D] f32 final output, or nullptr (partial mode)
+    float *part_ml;       // per-split partials [nsplit][B*T*Hq][2]: workspace, or with a single
+    float *part_o;        //   split in partial mode the caller's buffer; [nsplit][B*T*Hq][D]
+    float *res_ml;        // partial mode with splits: the caller's buffer for the merged partial
+    float *res_o;
+    int *counters;        // [B*Hkv*mtiles] split arrival counters, zero between launches
     int *err;
     int B, T, Hq, Hkv, G;
     int layer, cap, mtiles, nsplit, keys_per_split;
@@ -76,9 +79,11 @@ struct CombineArgs {
 int decode_stage_keys(int head_dim);
 int prefill_tile_keys();
 
-cudaError_t launch_append(const AppendArgs &a, cudaStream_t s);
+// pdl: launch so that the next (dependent) decode kernel may start during this one.
+cudaError_t launch_append(const AppendArgs &a, cudaStream_t s, bool pdl);
+// pdl: launch as a programmatic dependent of the preceding kernel (the append of brk_attn_step).
 cudaError_t launch_decode(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const DecodeArgs &a,
-                          int grid_x, int grid_y, int grid_z, cudaStream_t s);
+                          int grid_x, int grid_y, int grid_z, cudaStream_t s, bool pdl);
 cudaError_t launch_combine(const CombineArgs &a, cudaStream_t s);
 // Concurrent CTAs per SM of the decode kernel for a head dim (occupancy query).
 int decode_ctas_per_sm(int head_dim);

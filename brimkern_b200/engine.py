@@ -352,6 +352,15 @@ class AttentionEngine:
         attention output out; K/V land in the cache."""
         q_work = torch.empty_like(q_in) if q_work is None else q_work
         out = torch.empty_like(q_in) if out is None else out
+        B = kv.batch
+        T = q_in.numel() // (B * cfg.n_heads * cfg.head_dim)
+        if kernel == "auto" and self.attnDecodeOk and T * (cfg.n_heads // cfg.n_kv_heads) <= 64:
+            # Decode: append and attention as one overlapped launch pair.
+            p = cfg.params()
+            pos = _positions(past_len, B)
+            check(L.lib().brk_attn_step(self.ctx.handle, kv.handle, layer, ctypes.byref(p), B, T, pos, _ptr(q_in),
+                                        _ptr(k_in), _ptr(v_in), _ptr(q_work), _ptr(out), _stream_ptr(stream)))
+            return out
         self.appendKv(kv, layer, cfg, q_in, k_in, v_in, q_work, past_len, stream)
         return self.recAttention(kv, layer, cfg, q_work, out, past_len, kernel, stream)
 

@@ -125,10 +125,20 @@ int brk_kv_read_rows(const brk_kv *kv, int layer, int seq, int row0, int n_rows,
 /* KV append with the q/k prologue fused (kernels.ts:1707-1730): per-head RMSNorm of q and k
  * (if gains are given), NeoX RoPE (if a table is given) at position past_len[b]+t, K and V
  * stored as fp16 at cache row past_len[b]+t-kv_offset; the rotated q is written to q_out f32
- * [B][T][Hq][D] for the attention call.  past_len: HOST [batch]. */
+ * [B][T][Hq][D] for the attention call.  With kv == NULL only q is processed (the rope / rmsnorm
+ * readback twins, any even head_dim up to 1024).  past_len: HOST [batch]. */
 int brk_attn_append(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, int batch,
                     int n_tokens, const int32_t *past_len, const float *q_in, const float *k_in,
                     const float *v_in, float *q_out, void *stream);
+
+/* One decode step of a layer's attention slice (recordLayerKV, kernels.ts:1707-1731): the
+ * append above followed by the decode kernel, launched so that the decode kernel starts
+ * streaming the cache rows that the append does not touch while the append still runs
+ * (programmatic dependent launch).  q_work receives the rotated q; out [B][T][Hq][D] f32.
+ * Decode shapes only (n_tokens * group <= 64).  past_len: HOST [batch]. */
+int brk_attn_step(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, int batch,
+                  int n_tokens, const int32_t *past_len, const float *q_in, const float *k_in,
+                  const float *v_in, float *q_work, float *out, void *stream);
 
 /* recAttention (kernels.ts:1626-1641): attention of q [B][T][Hq][D] (already rotated) over
  * cache rows [0, past_len[b]+t] -> out [B][T][Hq][D] f32.  Picks the decode kernel for small
