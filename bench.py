@@ -204,6 +204,8 @@ def main():
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (tests only)")
     ap.add_argument("--kv-len", type=int, default=None, help="override the KV length (tests only)")
+    ap.add_argument("--softcap", type=float, default=None, help="override the logit softcap (diagnostics)")
+    ap.add_argument("--window", type=int, default=None, help="override the even-layer window (diagnostics)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
@@ -212,6 +214,10 @@ def main():
         c["layers"] = args.layers
     if args.kv_len:
         c["L"] = args.kv_len
+    if args.softcap is not None:
+        c["softcap"] = args.softcap
+    if args.window is not None:
+        c["window_even"] = args.window
     args.batch = args.batch or c["batch"]
     args.warmup = max(args.warmup, 3)
     workload = args.workload

@@ -180,6 +180,11 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
     a.scale = effective_scale(p);
     a.scale_log2 = a.scale * 1.4426950408889634f;
     a.softcap = p->softcap > 0.f ? p->softcap : 0.f;
+    if (a.softcap > 0.f) {
+        const double log2e = 1.4426950408889634;
+        a.cap_k1 = (float)(2.0 * (double)a.scale * log2e / (double)a.softcap);
+        a.cap_k2 = (float)((double)a.softcap * log2e);
+    }
     int span = 1;
     for (int b = 0; b < batch; ++b) {
         a.past_len[b] = past_len[b];

@@ -65,6 +65,8 @@ struct DecodeArgs {
     int layer, cap, mtiles, nsplit, keys_per_split;
     int kv_offset, window;
     float scale, scale_log2, softcap;
+    float cap_k1;           // softcap: 2 * scale * log2(e) / softcap  (exp2 argument of e^{2z})
+    float cap_k2;           // softcap: softcap * log2(e)              (score in log2 units)
     int past_len[BRK_MAX_BATCH];
 };
 
