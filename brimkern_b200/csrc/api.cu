@@ -663,14 +663,56 @@ int brk_attn_prefill(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_p
                      const int32_t *past_len, const float *q, float *out, void *stream) {
     int rc = check_call(ctx, kv, layer, p, batch, n_tokens, past_len);
     if (rc) return rc;
-    (void)q;
-    (void)out;
-    (void)stream;
-    return fail(BRK_ERR_UNSUPPORTED, "the tensor-core prefill kernel is not built in this library version");
+    if (!q || !out) return fail(BRK_ERR_INVALID, "null q or out");
+    if (p->head_dim != 64 && p->head_dim != 128)
+        return fail(BRK_ERR_UNSUPPORTED, "tensor-core prefill covers head_dim 64 and 128 (got %d)", p->head_dim);
+    brk::PrefillArgs a;
+    memset(&a, 0, sizeof(a));
+    for (int b = 0; b < batch; ++b) {
+        if (past_len[b] + n_tokens - p->kv_offset > kv->cap)
+            return fail(BRK_ERR_CAPACITY, "sequence %d needs %d cache rows, capacity is %d (grow the cache)", b,
+                        past_len[b] + n_tokens - p->kv_offset, kv->cap);
+        a.past_len[b] = past_len[b];
+    }
+    if ((n_tokens + 127) / 128 > 65535) return fail(BRK_ERR_INVALID, "n_tokens %d too large", n_tokens);
+    DeviceGuard g(ctx->device);
+    a.q = q;
+    a.out = out;
+    a.err = ctx->d_err;
+    a.B = batch;
+    a.T = n_tokens;
+    a.Hq = p->n_heads;
+    a.Hkv = p->n_kv_heads;
+    a.layer = layer;
+    a.cap = kv->cap;
+    a.kv_offset = p->kv_offset;
+    a.window = p->window > 0 ? p->window : 0;
+    const float scale = effective_scale(p);
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.softcap = p->softcap > 0.f ? p->softcap : 0.f;
+    if (a.softcap > 0.f) {
+        const double log2e = 1.4426950408889634;
+        a.cap_k1 = (float)(2.0 * (double)scale * log2e / (double)a.softcap);
+        a.cap_k2 = (float)((double)a.softcap * log2e);
+    }
+    cudaError_t e = brk::launch_prefill(p->head_dim, kv->tm_pre_k, kv->tm_pre_v, a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "prefill kernel launch");
+    ++ctx->launches;
+    return BRK_OK;
 }
 
 int brk_attn_forward(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
                      const int32_t *past_len, const float *q, float *out, void *stream) {
+    // recAttention's choice (kernels.ts:1634): the decode kernel for few (token, head) rows per kv
+    // head, the tensor-core kernel for prefill chunks.  BRK_ATTN_DECODE=0 forces the latter where
+    // it exists (the reference's ?attndecode=0 kill switch).
+    if (p && p->n_kv_heads > 0 && (p->head_dim == 64 || p->head_dim == 128)) {
+        const char *env = getenv("BRK_ATTN_DECODE");
+        const bool decode_off = env && env[0] == '0';
+        const int rows = n_tokens * (p->n_heads / p->n_kv_heads);
+        if (decode_off || rows > 128)
+            return brk_attn_prefill(ctx, kv, layer, p, batch, n_tokens, past_len, q, out, stream);
+    }
     return brk_attn_decode(ctx, kv, layer, p, batch, n_tokens, past_len, q, out, stream);
 }
 

@@ -70,6 +70,15 @@ struct DecodeArgs {
     int past_len[BRK_MAX_BATCH];
 };
 
+struct PrefillArgs {
+    const float *q;  // [B][T][Hq][D] f32 (rotated)
+    float *out;      // [B][T][Hq][D] f32
+    int *err;
+    int B, T, Hq, Hkv, layer, cap, kv_offset, window;
+    float scale_log2, softcap, cap_k1, cap_k2;
+    int past_len[BRK_MAX_BATCH];
+};
+
 struct CombineArgs {
     const float *part_ml, *part_o;
     float *out;             // normalised output, or nullptr
@@ -87,6 +96,9 @@ cudaError_t launch_append(const AppendArgs &a, cudaStream_t s, bool pdl);
 cudaError_t launch_decode(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const DecodeArgs &a,
                           int grid_x, int grid_y, int grid_z, cudaStream_t s, bool pdl);
 cudaError_t launch_combine(const CombineArgs &a, cudaStream_t s);
+// Tensor-core prefill (head_dim 64 or 128); maps with prefill_tile_keys()-row boxes.
+cudaError_t launch_prefill(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const PrefillArgs &a,
+                           cudaStream_t s);
 // Concurrent CTAs per SM of the decode kernel for a head dim (occupancy query).
 int decode_ctas_per_sm(int head_dim);
 

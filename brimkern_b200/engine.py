@@ -364,6 +364,30 @@ class AttentionEngine:
         self.appendKv(kv, layer, cfg, q_in, k_in, v_in, q_work, past_len, stream)
         return self.recAttention(kv, layer, cfg, q_work, out, past_len, kernel, stream)
 
+    def prefillChunked(self, kv: KvCache, layer: int, cfg: AttnConfig, q_in: torch.Tensor, k_in: torch.Tensor,
+                       v_in: torch.Tensor, past_len, chunk: int = 512, out: Optional[torch.Tensor] = None,
+                       stream=None) -> torch.Tensor:
+        """Chunked causal prefill of T new tokens per sequence ([B, T, H, D] inputs): per chunk,
+        append its K/V at pastLen + offset, then attend over everything cached so far -- the
+        reference's chunk loop (lfm2Model.ts:320-333, recAttention with pastLen) on the
+        tensor-core kernel."""
+        B = kv.batch
+        T = q_in.shape[1]
+        out = torch.empty_like(q_in) if out is None else out
+        base = [int(past_len)] * B if np.isscalar(past_len) else [int(x) for x in past_len]
+        q_work = torch.empty((B, min(chunk, T), cfg.n_heads, cfg.head_dim), dtype=torch.float32, device=q_in.device)
+        for c0 in range(0, T, chunk):
+            c1 = min(T, c0 + chunk)
+            pos = [p + c0 for p in base]
+            qc = q_in[:, c0:c1].contiguous()
+            qw = q_work[:, :c1 - c0]
+            oc = torch.empty_like(qc)
+            self.appendKv(kv, layer, cfg, qc, k_in[:, c0:c1].contiguous(), v_in[:, c0:c1].contiguous(), qw, pos,
+                          stream)
+            self.recAttention(kv, layer, cfg, qw, oc, pos, "auto", stream)
+            out[:, c0:c1].copy_(oc)
+        return out
+
     def decodePartial(self, kv: KvCache, layer: int, cfg: AttnConfig, q: torch.Tensor, part_ml: torch.Tensor,
                       part_o: torch.Tensor, past_len, stream=None):
         """Split-KV partial (m, l, o) of this cache's rows (sequence-sharded contexts)."""

@@ -1,0 +1,93 @@
+"""Tensor-core prefill parity (GPU): brk_attn_prefill (tcgen05.mma, TMEM accumulators) against
+the oracle (attentionCpu, kernels.ts:3466) fed the same fp16-rounded K/V, within the north-star
+tolerance; causal chunks with a past offset (the reference's recAttention with pastLen), GQA,
+partial tiles, window and softcap, and the chunked prefill loop end to end."""
+import zlib
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests.util import assert_close, f16_round, normal
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(eng, name, Hq, Hkv, D, pasts, T, scale=None, softcap=0.0, window=0, kernel="prefill"):
+    import torch
+    from brimkern_b200.engine import AttnConfig, KvCache
+    rng = np.random.default_rng(zlib.crc32(name.encode()))
+    B = len(pasts)
+    rows = max(pasts) + T
+    kv = KvCache(eng.ctx, 1, B, Hkv, D, rows)
+    ks, vs = [], []
+    for b in range(B):
+        k = normal(rng, rows, Hkv, D)
+        v = normal(rng, rows, Hkv, D)
+        kv.write_rows(0, b, 0, torch.from_numpy(k).to(eng.device), torch.from_numpy(v).to(eng.device))
+        ks.append(f16_round(k))
+        vs.append(f16_round(v))
+    q = normal(rng, B, T, Hq, D)
+    out = torch.full((B, T, Hq, D), float("nan"), dtype=torch.float32, device=eng.device)
+    cfg = AttnConfig(Hq, Hkv, D, scale=scale, softcap=softcap, window=window)
+    eng.recAttention(kv, 0, cfg, torch.from_numpy(q).to(eng.device), out, pasts, kernel=kernel)
+    eng.ctx.check()
+    got = out.cpu().numpy()
+    kv.close()
+    refs, _ = O.attention_batch(q.ravel(), np.stack(ks).ravel(), np.stack(vs).ravel(), B, rows * Hkv * D, T, Hq, Hkv,
+                                D, pasts, scale, softcap, window)
+    assert_close(got.ravel(), refs, what=name)
+
+
+@pytest.mark.parametrize("T,past", [(1, 0), (7, 0), (128, 0), (129, 0), (300, 173), (256, 1000)])
+def test_prefill_shapes_d128(eng, T, past):
+    _run(eng, f"pf128_{T}_{past}", 8, 2, 128, [past], T)
+
+
+@pytest.mark.parametrize("T,past", [(5, 3), (200, 0), (130, 64)])
+def test_prefill_gqa7_d64(eng, T, past):
+    """The Qwen2.5-0.5B grouping (14 q / 2 kv heads, group 7) at head_dim 64."""
+    _run(eng, f"pf64_{T}_{past}", 14, 2, 64, [past, past + 5], T)
+
+
+def test_prefill_config3_chunk(eng):
+    """BASELINE config 3 shape: Qwen3-4B 32 q / 8 kv, D 128, a 512-token chunk after 1536 cached
+    tokens (the 4th chunk of a 2048 prompt) and a first chunk, batch 2."""
+    _run(eng, "pf_cfg3", 32, 8, 128, [1536, 0], 512)
+
+
+def test_prefill_window_softcap(eng):
+    _run(eng, "pf_win_cap", 8, 4, 128, [700, 20], 200, scale=1 / 16, softcap=50.0, window=256)
+
+
+def test_prefill_matches_decode_kernel(eng):
+    """Both kernels on one multi-token shape agree through the dispatch paths."""
+    _run(eng, "pf_vs_dec_p", 8, 2, 64, [77], 12, kernel="prefill")
+    _run(eng, "pf_vs_dec_d", 8, 2, 64, [77], 12, kernel="decode")
+
+
+def test_chunked_prefill_end_to_end(eng):
+    """A 2048-token prompt in 512-token chunks through append + prefill (QK-norm + RoPE), checked
+    against the oracle chain rmsnorm -> rope -> attentionCpu over the whole prompt."""
+    import torch
+    from brimkern_b200.engine import AttnConfig, KvCache, RopeTable
+    rng = np.random.default_rng(31)
+    Hq, Hkv, D, T, base = 8, 2, 128, 2048, 1e6
+    qn = (1 + 0.02 * rng.standard_normal(D)).astype(np.float32)
+    kn = (1 + 0.02 * rng.standard_normal(D)).astype(np.float32)
+    q_in = normal(rng, 1, T, Hq, D)
+    k_in = normal(rng, 1, T, Hkv, D)
+    v_in = normal(rng, 1, T, Hkv, D)
+    dev = eng.device
+    rope = RopeTable(eng.ctx, D, base, None, T)
+    cfg = AttnConfig(Hq, Hkv, D, q_norm=torch.from_numpy(qn).to(dev), k_norm=torch.from_numpy(kn).to(dev), rope=rope)
+    kv = KvCache(eng.ctx, 1, 1, Hkv, D, T)
+    out = eng.prefillChunked(kv, 0, cfg, torch.from_numpy(q_in).to(dev), torch.from_numpy(k_in).to(dev),
+                             torch.from_numpy(v_in).to(dev), [0], chunk=512)
+    eng.ctx.check()
+    q = O.rope(O.rmsnorm(q_in.ravel(), qn, T * Hq, D, 1e-6), T * Hq, D, Hq, 0, base)
+    k = O.rope(O.rmsnorm(k_in.ravel(), kn, T * Hkv, D, 1e-6), T * Hkv, D, Hkv, 0, base)
+    ref, _ = O.attention_batch(q, f16_round(k), f16_round(v_in.ravel()), 1, T * Hkv * D, T, Hq, Hkv, D, [0])
+    assert_close(out.cpu().numpy().ravel(), ref, what="chunked prefill")
+    kv.close()
+    rope.close()
