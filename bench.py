@@ -38,6 +38,9 @@ CONFIGS = {
     # BASELINE config 4.
     "gemma2-2b": dict(layers=26, Hq=8, Hkv=4, D=256, L=8192, base=1e4, qk_norm=False, batch=32, scale=1 / 16,
                       softcap=50.0, window_even=4096, ff=None),
+    # 2048-token prompt in 512-token chunks on the tensor-core prefill kernel.
+    "qwen3-4b-prefill": dict(layers=36, Hq=32, Hkv=8, D=128, L=2048, chunk=512, base=1e6, qk_norm=True, batch=4,
+                             scale=None, softcap=0.0, window_even=0, ff=None, prefill=True),
     # BASELINE config 5 on one GPU (the long-context shape; sequence sharding is the multi-GPU form).
     "llama3.2-1b-long": dict(layers=16, Hq=32, Hkv=8, D=64, L=131072, base=5e5, qk_norm=False, batch=8, scale=None,
                              softcap=0.0, window_even=0, ff=(32.0, 1.0, 4.0, 8192)),
@@ -54,6 +57,267 @@ def kv_bytes_per_step(c, batch):
             keys = min(keys, c["window_even"])
         total += batch * keys * c["Hkv"] * c["D"] * 2 * 2
     return total
+
+
+def prefill_flops(c, batch):
+    """Causal-exact FLOPs of one prefill launch per chunk: QK^T and PV, 2 FLOPs per MAC, over the
+    keys each query attends (pastLen + t + 1)."""
+    out = []
+    T = c["chunk"]
+    for c0 in range(0, c["L"], T):
+        keys = sum(c0 + t + 1 for t in range(min(T, c["L"] - c0)))
+        out.append(4 * c["D"] * keys * c["Hq"] * batch)
+    return out
+
+
+def load_tflops_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            js = json.load(fh)
+            return float(js["bf16_tflops_sustained"]), float(js["bf16_tflops"]), "measured"
+    except Exception:
+        return 1400.0, 1590.0, "fallback"
+
+
+def run_prefill(args, c, workload):
+    """Prefill bench: a step is the whole prompt through every layer, chunk by chunk: append
+    (QK-norm + RoPE + fp16 store) then the tensor-core prefill kernel over the cache so far."""
+    import torch
+    import torch.distributed as dist
+
+    from brimkern_b200.engine import AttentionEngine, AttnConfig, KvCache, RopeTable
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B, P, CH, layers = args.batch, c["L"], c["chunk"], c["layers"]
+    Hq, Hkv, D = c["Hq"], c["Hkv"], c["D"]
+    nch = (P + CH - 1) // CH
+    eng = AttentionEngine(local)
+    rope = RopeTable(eng.ctx, D, c["base"], None, P)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2000 + rank)
+    qn = (1 + 0.02 * torch.randn(D, generator=gen, device=dev)).float()
+    kn = (1 + 0.02 * torch.randn(D, generator=gen, device=dev)).float()
+    cfg = AttnConfig(Hq, Hkv, D, q_norm=qn, k_norm=kn, rope=rope)
+    kv = KvCache(eng.ctx, layers, B, Hkv, D, P)
+    q_in = torch.randn((layers, nch, B, CH, Hq, D), generator=gen, device=dev)
+    k_in = torch.randn((layers, nch, B, CH, Hkv, D), generator=gen, device=dev)
+    v_in = torch.randn((layers, nch, B, CH, Hkv, D), generator=gen, device=dev)
+    q_work = torch.empty((B, CH, Hq, D), dtype=torch.float32, device=dev)
+    out = torch.empty((layers, nch, B, CH, Hq, D), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+    flops = prefill_flops(c, B)
+
+    def step(ev=None, qi=q_in, ki=k_in, vi=v_in, oo=out):
+        for layer in range(layers):
+            for ci in range(nch):
+                pos = [ci * CH] * B
+                eng.appendKv(kv, layer, cfg, qi[layer, ci], ki[layer, ci], vi[layer, ci], q_work, pos)
+                if ev is not None:
+                    ev[layer][ci][0].record(stream)
+                eng.recAttention(kv, layer, cfg, q_work, oo[layer, ci], pos, kernel="prefill")
+                if ev is not None:
+                    ev[layer][ci][1].record(stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    eng.ctx.check()
+    barrier()
+    torch.cuda.synchronize()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+    sampler = ClockSampler(int(vis[local]) if len(vis) > local and vis[local].strip().isdigit() else local)
+    sampler.start()
+    time.sleep(0.3)
+    n0 = eng.ctx.launches
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = eng.ctx.launches - n0
+    clocks = sampler.stop()
+    eng.ctx.check()
+    barrier()
+    ms_total = e0.elapsed_time(e1)
+    rsteps = max(2, min(args.steps, 3))
+    ev = [[[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(nch)]
+           for _ in range(layers)] for _ in range(rsteps)]
+    for si in range(rsteps):
+        step(ev[si])
+    torch.cuda.synchronize()
+    eng.ctx.check()
+    kern_ms = sum(ev[si][l][ci][0].elapsed_time(ev[si][l][ci][1]) for si in range(rsteps) for l in range(layers)
+                  for ci in range(nch)) / rsteps
+    if world > 1:
+        t = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    step_flops = sum(flops) * layers
+    value = world * step_flops / (ms_step * 1e-3) / 1e12
+    sus, burst, kind = load_tflops_peak()
+    achieved = step_flops / (kern_ms * 1e-3) / 1e12
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv = q_in.cpu().pin_memory(), k_in.cpu().pin_memory(), v_in.cpu().pin_memory()
+        hout = torch.empty(out.shape, dtype=torch.float32, pin_memory=True)
+        dq, dk, dv, do = torch.empty_like(q_in), torch.empty_like(k_in), torch.empty_like(v_in), torch.empty_like(out)
+
+        def e2e_step():
+            dq.copy_(hq, non_blocking=True)
+            dk.copy_(hk, non_blocking=True)
+            dv.copy_(hv, non_blocking=True)
+            step(None, dq, dk, dv, do)
+            hout.copy_(do, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        esteps = max(1, min(args.steps, 3))
+        f0.record(stream)
+        for _ in range(esteps):
+            e2e_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = f0.elapsed_time(f1) / esteps
+        e2e = {"value": round(world * step_flops / (e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+               "h2d_bytes_per_step": int((hq.numel() + hk.numel() + hv.numel()) * 4),
+               "d2h_bytes_per_step": int(hout.numel() * 4), "ms_per_step": round(e_ms, 3)}
+    if rank == 0:
+        line = {
+            "metric": "prefill-attn TFLOP/s (causal-exact)", "value": round(value, 2), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 in / f32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": workload, "global_batch": B * world, "prompt": P, "chunk": CH, "layers": layers,
+                       "heads": f"{Hq}q/{Hkv}kv", "head_dim": D, "parallelism": f"batch-sharded x{world}",
+                       "l2": "no flush: KV + inputs of a step are 4.2 GB > L2"},
+            "tokens_per_s": round(world * B * P / (ms_step * 1e-3), 1),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": sus, "unit": "TFLOP/s",
+                         "frac": round(achieved / sus, 4), "frac_of_burst": round(achieved / burst, 4),
+                         "traffic": None, "peak_kind": kind + " sustained bf16 (fp16 runs at the same rate)",
+                         "kernel": "prefill_attn_kernel", "timing": f"CUDA events around each prefill launch, {rsteps} steps",
+                         "flops_per_step": step_flops, "kernel_ms_per_step": round(kern_ms, 4)},
+            "cpu_baseline": None, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def run_sharded(args, c, workload):
+    """Config 5 on N GPUs: the KV sequence is split across ranks (ShardPlan), each rank decodes
+    its slice to (m, l, o) partials, one NCCL all-gather per layer, LSE combine on every rank.
+    Strong scaling: the context (and total KV bytes) is fixed, N GPUs share it."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from brimkern_b200.engine import AttentionEngine, AttnConfig, RopeTable, llama3_rope_factors
+    from brimkern_b200.sharded import ShardedDecoder, ShardPlan
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    B, Lkv, layers = args.batch, c["L"], c["layers"]
+    Hq, Hkv, D = c["Hq"], c["Hkv"], c["D"]
+    context = Lkv - 1                      # cached positions; the step appends position Lkv - 1
+    plan = ShardPlan(context, world, rank)
+    eng = AttentionEngine(local)
+    ff = llama3_rope_factors(D, c["base"], *c["ff"]) if c["ff"] else None
+    rope = RopeTable(eng.ctx, D, c["base"], ff, Lkv)
+    cfg = AttnConfig(Hq, Hkv, D, scale=c["scale"], softcap=c["softcap"], rope=rope)
+    dec = ShardedDecoder(eng, plan, layers, B, Hkv, D, extra=1)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3000 + rank)
+    rows = plan.hi - plan.lo
+    if rows > 0:
+        tmp_k = torch.empty((rows, Hkv, D), dtype=torch.float32, device=dev)
+        tmp_v = torch.empty_like(tmp_k)
+        for layer in range(layers):
+            for b in range(B):
+                tmp_k.normal_(generator=gen)
+                tmp_v.normal_(generator=gen)
+                dec.kv.write_rows(layer, b, 0, tmp_k, tmp_v)
+        del tmp_k, tmp_v
+    shared = torch.Generator(device=dev)
+    shared.manual_seed(4000)  # q / k / v inputs replicated on every rank
+    q_in = torch.randn((layers, B, 1, Hq, D), generator=shared, device=dev)
+    k_in = torch.randn((layers, B, 1, Hkv, D), generator=shared, device=dev)
+    v_in = torch.randn((layers, B, 1, Hkv, D), generator=shared, device=dev)
+    q_work = torch.empty((B, 1, Hq, D), dtype=torch.float32, device=dev)
+    out = torch.empty((layers, B, 1, Hq, D), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+    position = Lkv - 1
+
+    def step():
+        for layer in range(layers):
+            dec.step(layer, cfg, q_in[layer], k_in[layer], v_in[layer], position, q_work, out[layer])
+
+    for _ in range(args.warmup):
+        step()
+    eng.ctx.check()
+    dist.barrier()
+    torch.cuda.synchronize()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+    sampler = ClockSampler(int(vis[local]) if len(vis) > local and vis[local].strip().isdigit() else local)
+    sampler.start()
+    time.sleep(0.3)
+    n0 = eng.ctx.launches
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = eng.ctx.launches - n0
+    clocks = sampler.stop()
+    eng.ctx.check()
+    dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = float(t.item()) / args.steps
+    bytes_step = kv_bytes_per_step(c, B)
+    value = bytes_step / (ms_step * 1e-3) / 1e9
+    peak, peak_kind = load_peak()
+    if rank == 0:
+        line = {
+            "metric": "decode-attn KV-read GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16 KV / f32 accumulate", "data": "synthetic",
+            "config": {"workload": workload, "global_batch": B, "kv_len": Lkv, "layers": layers,
+                       "heads": f"{Hq}q/{Hkv}kv", "head_dim": D,
+                       "parallelism": f"sequence-sharded x{world}: per-layer NCCL all-gather of (m, l, o) partials",
+                       "l2": f"no flush: each step streams {bytes_step / 1e9:.1f} GB of KV > L2"},
+            "tokens_per_s": round(B / (ms_step * 1e-3), 1),
+            "frac_of_measured_hbm_per_gpu": round(value / world / peak, 4),
+            "allgather_bytes_per_rank_per_layer": B * Hq * (D + 2) * 4,
+            "roofline": None, "cpu_baseline": None, "e2e": None, "gpu_launches": int(launches), "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    dec.close()
+    eng.close()
+    dist.destroy_process_group()
+    return 0
 
 
 def load_peak():
@@ -223,6 +487,10 @@ def main():
     workload = args.workload
     if args.impl == "reference":
         return run_reference(args, c, workload)
+    if c.get("prefill"):
+        return run_prefill(args, c, workload)
+    if workload == "llama3.2-1b-long" and int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        return run_sharded(args, c, workload)
 
     import numpy as np
     import torch

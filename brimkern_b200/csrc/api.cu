@@ -728,13 +728,15 @@ int brk_attn_decode_partial(brk_ctx *ctx, const brk_kv *kv, int layer, const brk
 }
 
 int brk_attn_combine(brk_ctx *ctx, int n_parts, int rows, int head_dim, const float *part_ml, const float *part_o,
-                     float *out, void *stream) {
+                     size_t part_stride, float *out, void *stream) {
     if (!ctx || !part_ml || !part_o || !out) return fail(BRK_ERR_INVALID, "null argument");
     if (n_parts < 1 || rows < 0 || head_dim < 1) return fail(BRK_ERR_INVALID, "invalid combine shape");
     DeviceGuard g(ctx->device);
     brk::CombineArgs c;
     c.part_ml = part_ml;
     c.part_o = part_o;
+    c.stride_ml = part_stride ? part_stride : (size_t)rows * 2;
+    c.stride_o = part_stride ? part_stride : (size_t)rows * head_dim;
     c.out = out;
     c.out_ml = nullptr;
     c.out_o = nullptr;

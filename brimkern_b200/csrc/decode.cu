@@ -432,14 +432,14 @@ __global__ void combine_kernel(const __grid_constant__ CombineArgs a) {
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (row >= a.rows) return;
     float M = -CUDART_INF_F;
-    for (int p = lane; p < a.n_parts; p += 32) M = fmaxf(M, a.part_ml[((size_t)p * a.rows + row) * 2]);
+    for (int p = lane; p < a.n_parts; p += 32) M = fmaxf(M, a.part_ml[(size_t)p * a.stride_ml + (size_t)row * 2]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
     float Lsum = 0.f;
     if (M != -CUDART_INF_F)
         for (int p = lane; p < a.n_parts; p += 32) {
-            const float m = a.part_ml[((size_t)p * a.rows + row) * 2];
-            if (m != -CUDART_INF_F) Lsum += a.part_ml[((size_t)p * a.rows + row) * 2 + 1] * expf(m - M);
+            const float m = a.part_ml[(size_t)p * a.stride_ml + (size_t)row * 2];
+            if (m != -CUDART_INF_F) Lsum += a.part_ml[(size_t)p * a.stride_ml + (size_t)row * 2 + 1] * expf(m - M);
         }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, off);
@@ -447,8 +447,8 @@ __global__ void combine_kernel(const __grid_constant__ CombineArgs a) {
         float O = 0.f;
         if (M != -CUDART_INF_F)
             for (int p = 0; p < a.n_parts; ++p) {
-                const float m = a.part_ml[((size_t)p * a.rows + row) * 2];
-                if (m != -CUDART_INF_F) O += a.part_o[((size_t)p * a.rows + row) * a.D + d] * expf(m - M);
+                const float m = a.part_ml[(size_t)p * a.stride_ml + (size_t)row * 2];
+                if (m != -CUDART_INF_F) O += a.part_o[(size_t)p * a.stride_o + (size_t)row * a.D + d] * expf(m - M);
             }
         if (a.out) {
             a.out[(size_t)row * a.D + d] = O / Lsum;

@@ -81,6 +81,7 @@ struct PrefillArgs {
 
 struct CombineArgs {
     const float *part_ml, *part_o;
+    size_t stride_ml, stride_o;  // floats between consecutive parts
     float *out;             // normalised output, or nullptr
     float *out_ml, *out_o;  // combined partial (m, l, o), or nullptr
     int n_parts, rows, D;

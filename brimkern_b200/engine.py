@@ -399,9 +399,10 @@ class AttentionEngine:
                                               _ptr(part_ml), _ptr(part_o), _stream_ptr(stream)))
 
     def combine(self, n_parts: int, rows: int, head_dim: int, part_ml: torch.Tensor, part_o: torch.Tensor,
-                out: torch.Tensor, stream=None) -> torch.Tensor:
-        check(L.lib().brk_attn_combine(self.ctx.handle, n_parts, rows, head_dim, _ptr(part_ml), _ptr(part_o), _ptr(out),
-                                       _stream_ptr(stream)))
+                out: torch.Tensor, stream=None, part_stride: int = 0) -> torch.Tensor:
+        """LSE combine of partials (dense [n_parts][rows] layouts, or a packed stride)."""
+        check(L.lib().brk_attn_combine(self.ctx.handle, n_parts, rows, head_dim, _ptr(part_ml), _ptr(part_o),
+                                       int(part_stride), _ptr(out), _stream_ptr(stream)))
         return out
 
     def close(self):

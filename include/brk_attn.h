@@ -189,10 +189,13 @@ int brk_attn_decode_partial(brk_ctx *ctx, const brk_kv *kv, int layer,
                             const brk_attn_params *p, int batch, int n_tokens,
                             const int32_t *past_len, const float *q, float *part_ml,
                             float *part_o, void *stream);
-/* Log-sum-exp combine of n_parts partials laid out [n_parts][rows] (ml: 2 floats per row,
- * o: head_dim floats per row) -> out [rows][head_dim] = sum e^{m-M} o / sum e^{m-M} l. */
+/* Log-sum-exp combine of n_parts partials -> out [rows][head_dim] = sum e^{m-M} o / sum e^{m-M} l.
+ * Part p's (m, l) pairs start at part_ml + p * part_stride and its outputs at
+ * part_o + p * part_stride (floats); part_stride 0 means the dense layouts [n_parts][rows][2]
+ * and [n_parts][rows][head_dim].  A packed per-GPU buffer [rows*2 | rows*head_dim] gathered from
+ * N GPUs is combined with part_ml = buf, part_o = buf + 2*rows, part_stride = rows*(2+head_dim). */
 int brk_attn_combine(brk_ctx *ctx, int n_parts, int rows, int head_dim, const float *part_ml,
-                     const float *part_o, float *out, void *stream);
+                     const float *part_o, size_t part_stride, float *out, void *stream);
 
 #ifdef __cplusplus
 }
