@@ -1,5 +1,5 @@
 // Device helpers shared by the attention kernels (sm_100a): shared-memory barriers with bounded
-// waits, TMA tile loads (no cluster multicast anywhere), ldmatrix / mma.sync fragments, and the
+// waits, CTA-local TMA tile loads, ldmatrix / mma.sync fragments, and the
 // 128-byte swizzle that TMA applies to [rows][64 x fp16] boxes.
 #pragma once
 
@@ -80,7 +80,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     return false;
 }
 
-// 2-D tiled TMA load (non-multicast) of the box at (x = column, y = row) into shared memory,
+// 2-D tiled TMA load (into this CTA only) of the box at (x = column, y = row) into shared memory,
 // completing `bar`'s transaction count.  x * sizeof(element) must be a multiple of 16 bytes.
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(

@@ -5,7 +5,7 @@
 // q head) pairs of one kv head's query group, so every K/V byte read from HBM serves the whole
 // group (the reference re-reads K/V once per q head).  A producer warp streams the CTA's key
 // range through a ring of shared-memory stages with 2-D TMA loads (128-byte swizzled
-// [keys][64 x fp16] boxes, no multicast).  Consumer warps come in key groups (four, or two for
+// [keys][64 x fp16] boxes, CTA-local).  Consumer warps come in key groups (four, or two for
 // head_dim 256), each taking 16 keys of every stage; with the head-dim split DS = 2 (head_dim
 // 256) each key group is a warp pair that owns one half of the head dimension and swaps partial
 // QK^T scores through shared memory.  QK^T and PV run on the tensor cores (mma.m16n8k16, fp16 in, fp32 accumulate) with an

@@ -6,7 +6,7 @@
 // One CTA per (128-query tile, q head, sequence); keys stream in 128-key tiles from the fp16
 // cache.  Roles (192 threads):
 //   warps 0-3  softmax / epilogue: thread r owns query row r (TMEM lane r);
-//   warp 4     TMA producer: K and V tiles (128-byte swizzled [keys][64] boxes, no multicast)
+//   warp 4     TMA producer: K and V tiles (128-byte swizzled [keys][64] boxes, CTA-local loads)
 //              into a 2-stage ring;
 //   warp 5     TMEM allocator and MMA issuer (one elected lane).
 // Per key tile j: S_j = Q K_j^T (M 128, N 128, fp16 -> fp32 in TMEM, double-buffered), the
