@@ -17,27 +17,20 @@ namespace brk {
 
 namespace {
 
-constexpr int kAppendThreads = 128;  // one thread per head-vector row, as the reference's shaders
+constexpr int kRowsPerBlock = 4;  // one warp per head-vector row
 
-__device__ __forceinline__ double norm_gain(const float *gain, int i, int one_plus) {
-    const double w = gain[i];
-    return one_plus ? __dadd_rn(1.0, w) : w;
-}
-
-// rmsnormCpu's output element: f32((x * inv) * g), or x unchanged without a gain.
-__device__ __forceinline__ double normed(float x, const float *gain, int i, double inv, int one_plus) {
-    if (!gain) return (double)x;
-    return (double)(float)__dmul_rn(__dmul_rn((double)x, inv), norm_gain(gain, i, one_plus));
-}
-
-__global__ void __launch_bounds__(kAppendThreads) append_kernel(const __grid_constant__ AppendArgs a) {
+// DT: the head dim as a compile-time constant (64 / 128 / 256), or 0 for any other even size.
+template <int DT>
+__global__ void __launch_bounds__(kRowsPerBlock * 32) append_kernel(const __grid_constant__ AppendArgs a) {
     // The dependent decode may be scheduled now (it waits for this grid before reading q or the
     // new rows); this grid itself waits for whatever the stream ran before it.
     griddep_launch_dependents();
     griddep_wait();
-    const int D = a.D, half = D >> 1;
+    extern __shared__ double sq_all[];  // per warp: D squares (double), then D values (float)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int D = DT ? DT : a.D, half = D >> 1;
     const int per_tok = a.Hq + 2 * a.Hkv;
-    const long long row = (long long)blockIdx.x * kAppendThreads + threadIdx.x;
+    const long long row = (long long)blockIdx.x * kRowsPerBlock + warp;
     if (row >= (long long)a.B * a.T * per_tok) return;
     const int bt = (int)(row / per_tok), kind = (int)(row % per_tok);
     const int b = bt / a.T, t = bt % a.T;
@@ -68,25 +61,44 @@ __global__ void __launch_bounds__(kAppendThreads) append_kernel(const __grid_con
         }
     }
 
-    // rmsnormCpu (kernels.ts:3395): ss = sum of x^2 in index order (double), inv = 1/sqrt(ss/dim + eps).
-    double inv = 0.0;
+    double *sq = sq_all + (size_t)warp * D * 3 / 2;  // D doubles + D floats per warp
+    float *xs = reinterpret_cast<float *>(sq + D);
+    for (int d = lane; d < D; d += 32) {
+        const float x = src[d];
+        xs[d] = x;
+        sq[d] = __dmul_rn((double)x, (double)x);  // exact: an f32 square fits a double
+    }
+    __syncwarp();
+
     if (gain) {
-        double ss = 0.0;
-        for (int d = 0; d < D; ++d) {
-            const double x = src[d];
-            ss = __dadd_rn(ss, __dmul_rn(x, x));
+        // rmsnormCpu (kernels.ts:3395): ss = sum of x^2 in index order (double), inv = 1/sqrt(ss/dim + eps),
+        // y = f32(x*inv*g).  Only the ordered additions are sequential.
+        double inv = 0.0;
+        if (lane == 0) {
+            double ss = 0.0;
+            if constexpr (DT > 0) {
+#pragma unroll
+                for (int d = 0; d < DT; ++d) ss = __dadd_rn(ss, sq[d]);
+            } else {
+                for (int d = 0; d < D; ++d) ss = __dadd_rn(ss, sq[d]);
+            }
+            inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)D), a.eps)));
         }
-        inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)D), a.eps)));
+        inv = __shfl_sync(0xffffffffu, inv, 0);
+        for (int d = lane; d < D; d += 32) {
+            const double w = gain[d];
+            const double g = a.one_plus ? __dadd_rn(1.0, w) : w;
+            xs[d] = (float)__dmul_rn(__dmul_rn((double)xs[d], inv), g);
+        }
+        __syncwarp();
     }
 
     if (rotate) {
-        // ropeCpu (kernels.ts:3445): o_i = f32(x_i c - x_{i+D/2} s), o_{i+D/2} = f32(x_{i+D/2} c + x_i s),
-        // on the normalised f32 values.
+        // ropeCpu (kernels.ts:3445): o_i = f32(x_i c - x_{i+D/2} s), o_{i+D/2} = f32(x_{i+D/2} c + x_i s).
         const double2 *cs = a.rope + (size_t)pos * half;
-        for (int i = 0; i < half; ++i) {
+        for (int i = lane; i < half; i += 32) {
             const double2 e = cs[i];
-            const double x0 = normed(src[i], gain, i, inv, a.one_plus);
-            const double x1 = normed(src[i + half], gain, i + half, inv, a.one_plus);
+            const double x0 = xs[i], x1 = xs[i + half];
             const float o0 = (float)__dsub_rn(__dmul_rn(x0, e.x), __dmul_rn(x1, e.y));
             const float o1 = (float)__dadd_rn(__dmul_rn(x1, e.x), __dmul_rn(x0, e.y));
             if (qdst) {
@@ -98,12 +110,11 @@ __global__ void __launch_bounds__(kAppendThreads) append_kernel(const __grid_con
             }
         }
     } else {
-        for (int d = 0; d < D; ++d) {
-            const float y = (float)normed(src[d], gain, d, inv, a.one_plus);
+        for (int d = lane; d < D; d += 32) {
             if (qdst)
-                qdst[d] = y;
+                qdst[d] = xs[d];
             else
-                cdst[d] = __float2half_rn(y);
+                cdst[d] = __float2half_rn(xs[d]);
         }
     }
 }
@@ -142,16 +153,21 @@ cudaError_t launch_append(const AppendArgs &a, cudaStream_t s, bool pdl) {
     const long long rows = (long long)a.B * a.T * (a.Hq + 2 * a.Hkv);
     if (rows == 0) return cudaSuccess;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((rows + kAppendThreads - 1) / kAppendThreads));
-    cfg.blockDim = dim3(kAppendThreads);
-    cfg.dynamicSmemBytes = 0;
+    cfg.gridDim = dim3((unsigned)((rows + kRowsPerBlock - 1) / kRowsPerBlock));
+    cfg.blockDim = dim3(kRowsPerBlock * 32);
+    cfg.dynamicSmemBytes = (size_t)kRowsPerBlock * a.D * 12;  // squares (double) + values (float)
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, append_kernel, a);
+    switch (a.D) {
+        case 64: return cudaLaunchKernelEx(&cfg, append_kernel<64>, a);
+        case 128: return cudaLaunchKernelEx(&cfg, append_kernel<128>, a);
+        case 256: return cudaLaunchKernelEx(&cfg, append_kernel<256>, a);
+        default: return cudaLaunchKernelEx(&cfg, append_kernel<0>, a);
+    }
 }
 
 cudaError_t launch_kv_write_rows(__half *kc, __half *vc, const float *k, const float *v, int n_rows, int Hkv, int D,
