@@ -247,10 +247,6 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
 
 }  // namespace
 
-namespace brk {
-int prefill_tile_keys() { return 128; }
-}  // namespace brk
-
 namespace {
 
 // Split-KV partials of brk_attn_decode_static.  A file-scope device array: every GPU that loads

@@ -3,17 +3,20 @@
 // Replaces the reference's 2-pass thread-per-(token, head) `attention` kernel
 // (shaders.ts:1482-1524) that recAttention dispatches for prefill chunks (kernels.ts:1634-1638).
 //
-// One CTA per (128-query tile, q head, sequence); keys stream in 128-key tiles from the fp16
-// cache.  Roles (192 threads):
-//   warps 0-3  softmax / epilogue: thread r owns query row r (TMEM lane r);
-//   warp 4     TMA producer: K and V tiles (128-byte swizzled [keys][64] boxes, CTA-local loads)
-//              into a 2-stage ring;
-//   warp 5     TMEM allocator and MMA issuer (one elected lane).
-// Per key tile j: S_j = Q K_j^T (M 128, N 128, fp16 -> fp32 in TMEM, double-buffered), the
-// softmax warps read S_j, apply the causal / window mask, scale and online-softmax, write
-// P_j = exp(S_j - m) as fp16 to shared memory, and the MMA warp issues O_j = P_j V_j into a
-// TMEM tile that the softmax warps fold into their register accumulator o = o*alpha + O_j.
-// S_{j+1} is computed while the softmax warps work on S_j.
+// One CTA runs two query streams that share every K/V tile: two q heads of the same kv head
+// (even group size) or two consecutive 128-query tiles of one head (odd group size).  Roles
+// (320 threads):
+//   warps 0-3 / 4-7  softmax warpgroup of stream 0 / 1: thread r owns query row r (TMEM lane r);
+//   warp 8           TMA producer: 64-key K and V tiles (128-byte swizzled [keys][64] boxes,
+//                    CTA-local loads) into a 3-stage ring;
+//   warp 9           TMEM allocator and MMA issuer (one elected lane).
+// Per 64-key tile j and stream s: S_s = Q_s K_j^T (tcgen05.mma, M 128, N 64, fp16 -> fp32 in
+// TMEM); the stream's warpgroup reads S_s once, masks (causal offset pastLen, window) only on
+// boundary tiles, and writes P_s = exp2(s - m) as fp16 to shared memory; the MMA warp
+// accumulates O_s += P_s V_j in TMEM.  The running max m is only raised (and O_s rescaled in
+// TMEM) when a tile's max exceeds it by more than 2^8, so P stays <= 256 and rescaling is rare.
+// The tensor core alternates between the streams: while one warpgroup works on its scores the
+// other stream's MMAs run.
 #include <math_constants.h>
 
 #include "common.cuh"
@@ -23,46 +26,42 @@ namespace brk {
 
 namespace {
 
-constexpr int kTQ = 128;  // queries per CTA (the MMA's M)
-constexpr int kTK = 128;  // keys per tile (N of QK^T, K of PV)
-constexpr int kSoftmaxWarps = 4;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
-constexpr int kThreads = 6 * 32;
-constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O tile | unused
-constexpr float kLn2f = 0.6931471805599453f;
+constexpr int kTQ = 128;       // queries per stream (the MMA's M)
+constexpr int kTK = 64;        // keys per tile (N of QK^T, K of PV)
+constexpr int kStages = 3;     // K/V ring depth
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 10 * 32;
+constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O0 | O1
+constexpr float kRescaleLog2 = 8.f;  // raise the running max only when a tile exceeds it by 2^8
 
 template <int D>
 struct PrefillLayout {
     static constexpr int kBlocks = D / 64;
-    static constexpr uint32_t kQBlock = kTQ * 128;          // [128 rows][64] fp16 block
-    static constexpr uint32_t kKVBlock = kTK * 128;
-    static constexpr uint32_t kQBytes = kBlocks * kQBlock;
-    static constexpr uint32_t kTileBytes = kBlocks * kKVBlock;  // one K (or V) tile
-    static constexpr uint32_t kPBytes = 2 * kTQ * 128;          // [128 rows][128 keys] fp16
-    static constexpr uint32_t kOffQ = 0;
-    static constexpr uint32_t kOffK0 = kOffQ + kQBytes;
-    static constexpr uint32_t kOffV0 = kOffK0 + kTileBytes;
-    static constexpr uint32_t kOffK1 = kOffV0 + kTileBytes;
-    static constexpr uint32_t kOffV1 = kOffK1 + kTileBytes;
-    static constexpr uint32_t kOffP = kOffV1 + kTileBytes;
-    static constexpr uint32_t kOffBar = kOffP + kPBytes;
-    static constexpr uint32_t kNumBars = 16;
+    static constexpr uint32_t kQBlock = kTQ * 128;             // [128 rows][64] fp16
+    static constexpr uint32_t kKVBlock = kTK * 128;            // [64 keys][64] fp16
+    static constexpr uint32_t kQBytes = kBlocks * kQBlock;     // one stream's q
+    static constexpr uint32_t kTileBytes = kBlocks * kKVBlock; // one K (or V) tile
+    static constexpr uint32_t kPBytes = kTQ * 128;             // [128 rows][64 keys] fp16
+    static constexpr uint32_t kOffQ = 0;                       // 2 streams
+    static constexpr uint32_t kOffKV = 2 * kQBytes;            // kStages x (K, V)
+    static constexpr uint32_t kOffP = kOffKV + kStages * 2 * kTileBytes;  // 2 streams
+    static constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;
+    static constexpr uint32_t kNumBars = 24;
     static constexpr uint32_t kSmemBytes = 1024 + kOffBar + kNumBars * 8 + 16;
+    static constexpr uint32_t kColS = 0, kColO = 2 * kTK;     // TMEM columns: S_s at s*64, O_s at 128 + s*D
 };
 
 // Barrier slots.
 enum : int {
-    kBarKFull = 0,    // [2] TMA -> MMA
-    kBarVFull = 2,    // [2] TMA -> MMA (and the softmax warps on the last tile)
-    kBarKvEmpty = 4,  // [2] MMA commit -> producer
-    kBarSFull = 6,    // [2] MMA commit -> softmax
-    kBarSFree = 8,    // [2] softmax -> MMA
-    kBarQFull = 10,   // softmax (q staged) -> MMA
-    kBarPFull = 11,   // softmax (P written) -> MMA
-    kBarOFull = 12,   // MMA commit (O tile ready, P consumed) -> softmax
-    kBarOFree = 13,   // softmax (O tile read) -> MMA
-    kBarMmaDone = 14, // MMA commit of everything -> teardown
+    kBarKvFull = 0,   // [3] TMA -> MMA
+    kBarKvEmpty = 3,  // [3] MMA commit -> producer
+    kBarSFull = 6,    // [2] MMA commit (S_s ready) -> softmax s
+    kBarSFree = 8,    // [2] softmax s (S_s read) -> MMA
+    kBarPFull = 10,   // [2] softmax s (P_s written, O_s rescaled) -> MMA
+    kBarODone = 12,   // [2] MMA commit (PV_s done: P_s free, O_s stable) -> softmax s
+    kBarQFull = 14,   // both warpgroups staged q -> MMA
+    kBarMmaDone = 15, // everything issued has completed -> teardown
 };
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -84,9 +83,8 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
         : "memory");
 }
 
-// 32 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
+// 32 consecutive 32-bit TMEM columns of this thread's lane (no wait).
+__device__ __forceinline__ void tc_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
         "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
@@ -95,9 +93,27 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
           "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
           "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+// Hardware 2^x (MUFU; ~2 ulp, flushes subnormals), for the probabilities.
+__device__ __forceinline__ float ex2_fast(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 // Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field.
@@ -112,7 +128,19 @@ __host__ __device__ constexpr uint32_t f16_idesc(int M, int N, int a_mn_major, i
            ((uint32_t)(M >> 4) << 24);
 }
 
-template <int D>
+// Score in log2 units from a raw q.k dot product (monotonic, so maxima commute with it).
+template <bool CAP>
+__device__ __forceinline__ float score_log2(float dot, const PrefillArgs &a) {
+    if constexpr (CAP) {
+        // c*tanh(s/c) (shaders.ts:1490) with tanh z = 1 - 2/(1 + e^{2z}), in log2 units.
+        const float e2z = exp2f(dot * a.cap_k1);
+        return a.cap_k2 * (1.f - 2.f * __frcp_rn(1.f + e2z));
+    } else {
+        return dot * a.scale_log2;
+    }
+}
+
+template <int D, bool CAP>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                         const __grid_constant__ PrefillArgs a) {
@@ -123,35 +151,42 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kOffBar + L::kNumBars * 8);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.x;
-    const int qt = gridDim.y - 1 - blockIdx.y;  // heaviest (latest) query tiles first
-    const int b = blockIdx.z;
-    const int G = a.Hq / a.Hkv, kvh = h / G;
+    const int G = a.Hq / a.Hkv;
     const int T = a.T;
-    const int q0 = qt * kTQ;
+    const int b = blockIdx.z;
     const int past = a.past_len[b];
-    const int nq = min(kTQ, T - q0);  // valid query rows of this tile
-
-    // Key range (cache rows) of the whole tile: causal up to the last query, window from the first.
-    int khi = past + q0 + nq - a.kv_offset;
+    const int ntq = (T + kTQ - 1) / kTQ;
+    // Streams: two heads of one kv group sharing a query tile, or (odd group) two query tiles of
+    // one head.  Heaviest (latest) query tiles are scheduled first.
+    const bool pair_heads = G % 2 == 0;
+    const int head0 = pair_heads ? 2 * (int)blockIdx.x : (int)blockIdx.x;
+    const int head1 = pair_heads ? head0 + 1 : head0;
+    const int q00 = pair_heads ? (ntq - 1 - (int)blockIdx.y) * kTQ : 2 * ((ntq + 1) / 2 - 1 - (int)blockIdx.y) * kTQ;
+    const int q01 = pair_heads ? q00 : q00 + kTQ;
+    const int kvh = head0 / G;
+    const int nq0 = max(0, min(kTQ, T - q00)), nq1 = max(0, min(kTQ, T - q01));
+    const bool active1 = nq1 > 0;
+    // Key range (cache rows) of the CTA: causal up to its last query, window from its first.
+    const int q_last = (active1 ? q01 + nq1 : q00 + nq0) - 1;
+    int khi = past + q_last + 1 - a.kv_offset;
     if (khi > a.cap) khi = a.cap;
     int klo = 0;
-    if (a.window > 0) klo = max(0, past + q0 - a.window + 1 - a.kv_offset);
+    if (a.window > 0) klo = max(0, past + q00 - a.window + 1 - a.kv_offset);
     const int nk = khi > klo ? (khi - klo + kTK - 1) / kTK : 0;
     const int seg_row = ((a.layer * a.B + b) * a.Hkv + kvh) * a.cap;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&bars[kBarKFull + i], 1);
-            mbar_init(&bars[kBarVFull + i], 1);
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&bars[kBarKvFull + i], 1);
             mbar_init(&bars[kBarKvEmpty + i], 1);
-            mbar_init(&bars[kBarSFull + i], 1);
-            mbar_init(&bars[kBarSFree + i], kSoftmaxWarps * 32);
         }
-        mbar_init(&bars[kBarQFull], kSoftmaxWarps * 32);
-        mbar_init(&bars[kBarPFull], kSoftmaxWarps * 32);
-        mbar_init(&bars[kBarOFull], 1);
-        mbar_init(&bars[kBarOFree], kSoftmaxWarps * 32);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&bars[kBarSFull + s], 1);
+            mbar_init(&bars[kBarSFree + s], 128);
+            mbar_init(&bars[kBarPFull + s], 128);
+            mbar_init(&bars[kBarODone + s], 1);
+        }
+        mbar_init(&bars[kBarQFull], 256);
         mbar_init(&bars[kBarMmaDone], 1);
         fence_barrier_init();
     }
@@ -165,12 +200,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tS0 = tmem, tO = tmem + 2 * kTK;
 
-    uint8_t *sQ = smem + L::kOffQ;
-    uint8_t *sP = smem + L::kOffP;
-    uint8_t *sK[2] = {smem + L::kOffK0, smem + L::kOffK1};
-    uint8_t *sV[2] = {smem + L::kOffV0, smem + L::kOffV1};
+    auto sQ = [&](int s) { return smem + L::kOffQ + s * L::kQBytes; };
+    auto sP = [&](int s) { return smem + L::kOffP + s * L::kPBytes; };
+    auto sK = [&](int st) { return smem + L::kOffKV + st * 2 * L::kTileBytes; };
+    auto sV = [&](int st) { return smem + L::kOffKV + st * 2 * L::kTileBytes + L::kTileBytes; };
 
     if (warp == kProducerWarp) {
         if (lane == 0 && nk > 0) {
@@ -178,77 +212,84 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&tmv);
             int issued = 0;
             for (int j = 0; j < nk; ++j) {
-                const int st = j & 1;
-                if (j >= 2 && !mbar_wait(&bars[kBarKvEmpty + st], ((j >> 1) - 1) & 1, a.err, kErrSlotTimeout)) break;
+                const int st = j % kStages;
+                if (j >= kStages &&
+                    !mbar_wait(&bars[kBarKvEmpty + st], ((j / kStages) - 1) & 1, a.err, kErrSlotTimeout))
+                    break;
                 const int y = seg_row + klo + j * kTK;
-                mbar_arrive_expect_tx(&bars[kBarKFull + st], L::kTileBytes);
+                mbar_arrive_expect_tx(&bars[kBarKvFull + st], 2 * L::kTileBytes);
 #pragma unroll
-                for (int blk = 0; blk < L::kBlocks; ++blk)
-                    tma_load_2d(sK[st] + blk * L::kKVBlock, &tmk, blk * 64, y, &bars[kBarKFull + st]);
-                mbar_arrive_expect_tx(&bars[kBarVFull + st], L::kTileBytes);
-#pragma unroll
-                for (int blk = 0; blk < L::kBlocks; ++blk)
-                    tma_load_2d(sV[st] + blk * L::kKVBlock, &tmv, blk * 64, y, &bars[kBarVFull + st]);
+                for (int blk = 0; blk < L::kBlocks; ++blk) {
+                    tma_load_2d(sK(st) + blk * L::kKVBlock, &tmk, blk * 64, y, &bars[kBarKvFull + st]);
+                    tma_load_2d(sV(st) + blk * L::kKVBlock, &tmv, blk * 64, y, &bars[kBarKvFull + st]);
+                }
                 issued = j + 1;
             }
-            for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) {
-                mbar_wait(&bars[kBarKFull + (j & 1)], (j >> 1) & 1, a.err, kErrTmaTimeout);
-                mbar_wait(&bars[kBarVFull + (j & 1)], (j >> 1) & 1, a.err, kErrTmaTimeout);
-            }
+            for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j)
+                mbar_wait(&bars[kBarKvFull + j % kStages], (j / kStages) & 1, a.err, kErrTmaTimeout);
         }
         __syncwarp();
     } else if (warp == kMmaWarp) {
-        if (lane == 0) {
+        if (lane == 0 && nk > 0) {
             constexpr uint32_t idesc_qk = f16_idesc(kTQ, kTK, 0, 0);
             constexpr uint32_t idesc_pv = f16_idesc(kTQ, D, 0, 1);
-            bool ok = nk > 0 && mbar_wait(&bars[kBarQFull], 0, a.err, kErrMmaTimeout);
-            tc_fence_after();
-            auto issue_pv = [&](int i) -> bool {
-                const int st = i & 1;
-                if (!mbar_wait(&bars[kBarPFull], i & 1, a.err, kErrMmaTimeout)) return false;
-                if (!mbar_wait(&bars[kBarVFull + st], (i >> 1) & 1, a.err, kErrTmaTimeout)) return false;
-                if (i >= 1 && !mbar_wait(&bars[kBarOFree], (i - 1) & 1, a.err, kErrMmaTimeout)) return false;
+            const int ns = active1 ? 2 : 1;
+            bool ok = mbar_wait(&bars[kBarQFull], 0, a.err, kErrMmaTimeout);
+            auto issue_s = [&](int s, int j) -> bool {
+                const int st = j % kStages;
+                if (s == 0 && !mbar_wait(&bars[kBarKvFull + st], (j / kStages) & 1, a.err, kErrTmaTimeout))
+                    return false;
+                if (j >= 1 && !mbar_wait(&bars[kBarSFree + s], (j - 1) & 1, a.err, kErrMmaTimeout)) return false;
                 tc_fence_after();
-                const uint32_t p_base = smem_addr(sP), v_base = smem_addr(sV[st]);
-#pragma unroll
-                for (int kk = 0; kk < kTK / 16; ++kk) {
-                    const uint64_t ad = sw128_desc(p_base + (kk >> 2) * (kTQ * 128) + (kk & 3) * 32, 16, 1024);
-                    const uint64_t bd = sw128_desc(v_base + kk * 16 * 128, L::kKVBlock, 1024);
-                    tc_mma(tO, ad, bd, idesc_pv, kk > 0);
-                }
-                tc_commit(&bars[kBarOFull]);
-                tc_commit(&bars[kBarKvEmpty + st]);
-                return true;
-            };
-            for (int j = 0; ok && j < nk; ++j) {
-                const int st = j & 1;
-                if (!mbar_wait(&bars[kBarKFull + st], (j >> 1) & 1, a.err, kErrTmaTimeout)) break;
-                if (j >= 2 && !mbar_wait(&bars[kBarSFree + st], ((j >> 1) - 1) & 1, a.err, kErrMmaTimeout)) break;
-                tc_fence_after();
-                const uint32_t q_base = smem_addr(sQ), k_base = smem_addr(sK[st]);
+                const uint32_t q_base = smem_addr(sQ(s)), k_base = smem_addr(sK(st));
 #pragma unroll
                 for (int ks = 0; ks < D / 16; ++ks) {
                     const uint64_t ad = sw128_desc(q_base + (ks >> 2) * L::kQBlock + (ks & 3) * 32, 16, 1024);
                     const uint64_t bd = sw128_desc(k_base + (ks >> 2) * L::kKVBlock + (ks & 3) * 32, 16, 1024);
-                    tc_mma(tS0 + st * kTK, ad, bd, idesc_qk, ks > 0);
+                    tc_mma(tmem + L::kColS + s * kTK, ad, bd, idesc_qk, ks > 0);
                 }
-                tc_commit(&bars[kBarSFull + st]);
-                if (j >= 1 && !issue_pv(j - 1)) {
-                    ok = false;
-                    break;
+                tc_commit(&bars[kBarSFull + s]);
+                return true;
+            };
+            auto issue_pv = [&](int s, int j) -> bool {
+                const int st = j % kStages;
+                if (!mbar_wait(&bars[kBarPFull + s], j & 1, a.err, kErrMmaTimeout)) return false;
+                tc_fence_after();
+                const uint32_t p_base = smem_addr(sP(s)), v_base = smem_addr(sV(st));
+#pragma unroll
+                for (int kk = 0; kk < kTK / 16; ++kk) {
+                    const uint64_t ad = sw128_desc(p_base + kk * 32, 16, 1024);
+                    const uint64_t bd = sw128_desc(v_base + kk * 16 * 128, L::kKVBlock, 1024);
+                    tc_mma(tmem + L::kColO + s * D, ad, bd, idesc_pv, j > 0 || kk > 0);
                 }
+                tc_commit(&bars[kBarODone + s]);
+                return true;
+            };
+            if (ok) ok = issue_s(0, 0) && (ns < 2 || issue_s(1, 0));
+            for (int j = 0; ok && j < nk; ++j) {
+                if (!issue_pv(0, j)) break;
+                if (j + 1 < nk && !issue_s(0, j + 1)) break;
+                if (ns == 2) {
+                    if (!issue_pv(1, j)) break;
+                    if (j + 1 < nk && !issue_s(1, j + 1)) break;
+                }
+                tc_commit(&bars[kBarKvEmpty + j % kStages]);
             }
-            if (ok && nk > 0) issue_pv(nk - 1);
             // Every MMA this thread issued must finish before TMEM is released.
             tc_commit(&bars[kBarMmaDone]);
             mbar_wait(&bars[kBarMmaDone], 0, a.err, kErrMmaTimeout);
         }
         __syncwarp();
     } else {
-        // ---- softmax warps: thread r <-> query row r.
-        const int r = threadIdx.x;
+        // ---- softmax warpgroups: stream s = warp / 4, thread r <-> query row r (TMEM lane r).
+        const int s = warp >> 2;
+        const int r = threadIdx.x & 127;
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        const int h = s ? head1 : head0, q0 = s ? q01 : q00, nqs = s ? nq1 : nq0;
+        uint8_t *sq = sQ(s);
+        uint8_t *sp = sP(s);
+        const bool row_ok = r < nqs;
         const int t = q0 + r;
-        const bool row_ok = r < nq;
         // Stage q row r as fp16 in the 128-byte swizzled K-major layout of the MMA's A operand.
         {
             const float *src = a.q + (((size_t)b * T + (row_ok ? t : 0)) * a.Hq + h) * D;
@@ -264,151 +305,149 @@ __global__ void __launch_bounds__(kThreads, 1)
                 pk.y = pack_half2(x0.z, x0.w);
                 pk.z = pack_half2(x1.x, x1.y);
                 pk.w = pack_half2(x1.z, x1.w);
-                *reinterpret_cast<uint4 *>(sQ + (c >> 3) * L::kQBlock + sw128(r, c & 7)) = pk;
+                *reinterpret_cast<uint4 *>(sq + (c >> 3) * L::kQBlock + sw128(r, c & 7)) = pk;
             }
             fence_proxy_async_smem();
             mbar_arrive(&bars[kBarQFull]);
         }
-        const int pos = past + t;                         // absolute position of this query
-        const int hi = row_ok ? pos - a.kv_offset : -1;   // last key (cache row) it attends
-        const int lo = a.window > 0 ? pos - a.window + 1 - a.kv_offset : INT_MIN;
-        const bool use_cap = a.softcap > 0.f;
-        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-
-        float o[D];
-#pragma unroll
-        for (int d = 0; d < D; ++d) o[d] = 0.f;
-        float m_run = -CUDART_INF_F, l_run = 0.f, alpha_prev = 1.f;
-        bool ok = true;
-        for (int j = 0; j < nk; ++j) {
-            const int st = j & 1;
-            const int kbase = klo + j * kTK;
-            if (!mbar_wait(&bars[kBarSFull + st], (j >> 1) & 1, a.err, kErrMmaTimeout)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const uint32_t ts = tS0 + st * kTK + lane_base;
-            // Pass 1: masked, scaled scores (log2 units) -> tile row max.
-            float mx = -CUDART_INF_F;
-#pragma unroll
-            for (int c = 0; c < kTK / 32; ++c) {
-                float v[32];
-                tc_ld32(ts + c * 32, v);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int key = kbase + c * 32 + e;
-                    float x = v[e];
-                    if (use_cap) {
-                        const float e2z = exp2f(x * a.cap_k1);
-                        x = a.cap_k2 * (1.f - 2.f * __frcp_rn(1.f + e2z));
-                    } else {
-                        x *= a.scale_log2;
-                    }
-                    x = (key <= hi && key >= lo && key < khi) ? x : -CUDART_INF_F;
-                    mx = fmaxf(mx, x);
-                }
-            }
-            const float m_new = fmaxf(m_run, mx);
-            const float m_use = m_new == -CUDART_INF_F ? 0.f : m_new;
-            const float alpha = exp2f(m_run - m_use);
-            m_run = m_new;
-            // Fold the previous tile's PV result; afterwards P may be overwritten.
-            if (j >= 1) {
-                if (!mbar_wait(&bars[kBarOFull], (j - 1) & 1, a.err, kErrMmaTimeout)) {
+        if (s == 1 && !active1) {
+            // Nothing to do for an empty second stream (odd group, last tile pair).
+        } else {
+            const int pos = past + t;                        // absolute position of this query
+            const int hi = row_ok ? pos - a.kv_offset : -1;  // last key (cache row) it attends
+            const int lo = a.window > 0 ? pos - a.window + 1 - a.kv_offset : INT_MIN;
+            // Tiles that need no per-element mask: all 128 rows see all 64 keys.
+            const int hi_min = past + q0 - a.kv_offset;
+            const int lo_max = a.window > 0 ? past + q0 + nqs - 1 - a.window + 1 - a.kv_offset : INT_MIN;
+            const uint32_t tS = tmem + L::kColS + s * kTK + lane_base;
+            const uint32_t tO = tmem + L::kColO + s * D + lane_base;
+            float m_used = -CUDART_INF_F;  // max the probabilities are relative to (log2 units)
+            float l_run = 0.f;
+            bool ok = true;
+            for (int j = 0; j < nk; ++j) {
+                const int kbase = klo + j * kTK;
+                if (!mbar_wait(&bars[kBarSFull + s], j & 1, a.err, kErrMmaTimeout)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-#pragma unroll
-                for (int c = 0; c < D / 32; ++c) {
-                    float v[32];
-                    tc_ld32(tO + lane_base + c * 32, v);
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) o[c * 32 + e] = o[c * 32 + e] * alpha_prev + v[e];
-                }
+                uint32_t raw[2][32];
+                tc_ld32_nowait(tS, raw[0]);
+                tc_ld32_nowait(tS + 32, raw[1]);
+                tc_wait_ld();
                 tc_fence_before();
-                mbar_arrive(&bars[kBarOFree]);
-            }
-            // Pass 2: P = exp2(s - m) as fp16 into shared memory (K-major, swizzled), row sums.
-            float rsum = 0.f;
+                mbar_arrive(&bars[kBarSFree + s]);  // S_s may be overwritten by the next tile
+                float v[64];
 #pragma unroll
-            for (int c = 0; c < kTK / 32; ++c) {
-                float v[32];
-                tc_ld32(ts + c * 32, v);
-                uint32_t pk[16];
+                for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(raw[i >> 5][i & 31]);
+                const bool full = kbase + kTK - 1 <= hi_min && kbase >= lo_max && kbase + kTK <= khi;
+                if (!full) {
 #pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    float pe[2];
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int key = kbase + c * 32 + e + u;
-                        float x = v[e + u];
-                        if (use_cap) {
-                            const float e2z = exp2f(x * a.cap_k1);
-                            x = a.cap_k2 * (1.f - 2.f * __frcp_rn(1.f + e2z));
-                        } else {
-                            x *= a.scale_log2;
-                        }
-                        const bool valid = key <= hi && key >= lo && key < khi;
-                        pe[u] = valid ? exp2f(x - m_use) : 0.f;
-                        rsum += pe[u];
+                    for (int i = 0; i < 64; ++i) {
+                        const int key = kbase + i;
+                        v[i] = (key <= hi && key >= lo && key < khi) ? v[i] : -CUDART_INF_F;
                     }
-                    pk[e >> 1] = pack_half2(pe[0], pe[1]);
                 }
+                float mraw = -CUDART_INF_F;
 #pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
-                    const int chunk = c * 4 + q4;  // 16-byte chunk over the 128 keys
-                    *reinterpret_cast<uint4 *>(sP + (chunk >> 3) * (kTQ * 128) + sw128(r, chunk & 7)) =
-                        make_uint4(pk[q4 * 4], pk[q4 * 4 + 1], pk[q4 * 4 + 2], pk[q4 * 4 + 3]);
+                for (int i = 0; i < 64; ++i) mraw = fmaxf(mraw, v[i]);
+                const float mt = mraw == -CUDART_INF_F ? -CUDART_INF_F : score_log2<CAP>(mraw, a);
+                bool waited_o = false;
+                if (mt > m_used + kRescaleLog2 || (m_used == -CUDART_INF_F && mt != -CUDART_INF_F)) {
+                    if (m_used != -CUDART_INF_F && j >= 1) {
+                        // Rescale O_s (and l) to the new max once PV_s(j-1) has landed.
+                        if (!mbar_wait(&bars[kBarODone + s], (j - 1) & 1, a.err, kErrMmaTimeout)) {
+                            ok = false;
+                            break;
+                        }
+                        waited_o = true;
+                        tc_fence_after();
+                        const float alpha = ex2_fast(m_used - mt);
+#pragma unroll
+                        for (int c = 0; c < D / 32; ++c) {
+                            uint32_t o[32];
+                            tc_ld32_nowait(tO + c * 32, o);
+                            tc_wait_ld();
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                            tc_st32(tO + c * 32, o);
+                        }
+                        tc_wait_st();
+                        l_run *= alpha;
+                    }
+                    m_used = mt;
                 }
-            }
-            tc_fence_before();
-            mbar_arrive(&bars[kBarSFree + st]);
-            // Keys past the range end: zero their V rows so that 0 * (stale data) stays 0.
-            if (kbase + kTK > khi) {
-                if (!mbar_wait(&bars[kBarVFull + st], (j >> 1) & 1, a.err, kErrTmaTimeout)) {
-                    ok = false;
-                    break;
+                const float m_eff = m_used == -CUDART_INF_F ? 0.f : m_used;
+                // P_s (fp16) into shared memory once PV_s(j-1) no longer reads it.
+                if (j >= 1 && !waited_o) {
+                    if (!mbar_wait(&bars[kBarODone + s], (j - 1) & 1, a.err, kErrMmaTimeout)) {
+                        ok = false;
+                        break;
+                    }
                 }
-                if (kbase + r >= khi) {
+                float rsum = 0.f;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        float p0, p1;
+                        if constexpr (CAP) {
+                            p0 = v[c * 8 + 2 * u] == -CUDART_INF_F ? 0.f
+                                                                    : ex2_fast(score_log2<CAP>(v[c * 8 + 2 * u], a) - m_eff);
+                            p1 = v[c * 8 + 2 * u + 1] == -CUDART_INF_F
+                                     ? 0.f
+                                     : ex2_fast(score_log2<CAP>(v[c * 8 + 2 * u + 1], a) - m_eff);
+                        } else {
+                            p0 = ex2_fast(fmaf(v[c * 8 + 2 * u], a.scale_log2, -m_eff));
+                            p1 = ex2_fast(fmaf(v[c * 8 + 2 * u + 1], a.scale_log2, -m_eff));
+                        }
+                        rsum += p0 + p1;
+                        pk[u] = pack_half2(p0, p1);
+                    }
+                    *reinterpret_cast<uint4 *>(sp + sw128(r, c)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                }
+                // Keys past the range end: zero their V rows so that 0 * (stale data) stays 0
+                // (one warpgroup does it; PV of both streams waits for both P_s arrivals).
+                if (s == 0 && kbase + kTK > khi && r < kTK && kbase + r >= khi) {
+                    if (!mbar_wait(&bars[kBarKvFull + j % kStages], (j / kStages) & 1, a.err, kErrTmaTimeout)) {
+                        ok = false;
+                        break;
+                    }
 #pragma unroll
                     for (int blk = 0; blk < L::kBlocks; ++blk)
 #pragma unroll
                         for (int c = 0; c < 8; ++c)
-                            *reinterpret_cast<uint4 *>(sV[st] + blk * L::kKVBlock + sw128(r, c)) =
+                            *reinterpret_cast<uint4 *>(sV(j % kStages) + blk * L::kKVBlock + sw128(r, c)) =
                                 make_uint4(0u, 0u, 0u, 0u);
                 }
+                fence_proxy_async_smem();
+                tc_fence_before();
+                mbar_arrive(&bars[kBarPFull + s]);
+                l_run += rsum;
             }
-            fence_proxy_async_smem();
-            mbar_arrive(&bars[kBarPFull]);
-            l_run = l_run * alpha + rsum;
-            alpha_prev = alpha;
-        }
-        if (ok && nk > 0) {
-            if (mbar_wait(&bars[kBarOFull], (nk - 1) & 1, a.err, kErrMmaTimeout)) {
+            if (ok && nk > 0 && mbar_wait(&bars[kBarODone + s], (nk - 1) & 1, a.err, kErrMmaTimeout)) {
                 tc_fence_after();
+                const float inv = 1.f / l_run;
+                float *dst = a.out + (((size_t)b * T + (row_ok ? t : 0)) * a.Hq + h) * D;
 #pragma unroll
                 for (int c = 0; c < D / 32; ++c) {
-                    float v[32];
-                    tc_ld32(tO + lane_base + c * 32, v);
+                    uint32_t o[32];
+                    tc_ld32_nowait(tO + c * 32, o);
+                    tc_wait_ld();
+                    if (row_ok) {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) o[c * 32 + e] = o[c * 32 + e] * alpha_prev + v[e];
-                }
-                if (row_ok) {
-                    const float inv = 1.f / l_run;
-                    float *dst = a.out + (((size_t)b * T + t) * a.Hq + h) * D;
-#pragma unroll
-                    for (int d = 0; d < D; d += 4)
-                        *reinterpret_cast<float4 *>(dst + d) =
-                            make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+                        for (int e = 0; e < 32; e += 4)
+                            *reinterpret_cast<float4 *>(dst + c * 32 + e) =
+                                make_float4(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv,
+                                            __uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+                    }
                 }
             }
         }
-        (void)kLn2f;
     }
 
-    // Teardown: every TMEM read and MMA is complete; the allocating warp releases TMEM.
+    // Teardown: every TMEM access and MMA is complete; the allocating warp releases TMEM.
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -416,29 +455,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
 }
 
-template <int D>
+template <int D, bool CAP>
 cudaError_t launch_prefill_t(const CUtensorMap &tmk, const CUtensorMap &tmv, const PrefillArgs &a, cudaStream_t s) {
     static unsigned long long configured = 0;
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 64 || !(configured & (1ull << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<D, CAP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              PrefillLayout<D>::kSmemBytes);
         if (e != cudaSuccess) return e;
         if (dev < 64) configured |= 1ull << dev;
     }
-    const dim3 grid(a.Hq, (a.T + kTQ - 1) / kTQ, a.B);
-    prefill_attn_kernel<D><<<grid, kThreads, PrefillLayout<D>::kSmemBytes, s>>>(tmk, tmv, a);
+    const int G = a.Hq / a.Hkv;
+    const int ntq = (a.T + kTQ - 1) / kTQ;
+    const dim3 grid(G % 2 == 0 ? a.Hq / 2 : a.Hq, G % 2 == 0 ? ntq : (ntq + 1) / 2, a.B);
+    prefill_attn_kernel<D, CAP><<<grid, kThreads, PrefillLayout<D>::kSmemBytes, s>>>(tmk, tmv, a);
     return cudaGetLastError();
 }
 
 }  // namespace
 
+int prefill_tile_keys() { return kTK; }
+
 cudaError_t launch_prefill(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const PrefillArgs &a,
                            cudaStream_t s) {
+    const bool cap = a.softcap > 0.f;
     switch (head_dim) {
-        case 64: return launch_prefill_t<64>(tmk, tmv, a, s);
-        case 128: return launch_prefill_t<128>(tmk, tmv, a, s);
+        case 64: return cap ? launch_prefill_t<64, true>(tmk, tmv, a, s) : launch_prefill_t<64, false>(tmk, tmv, a, s);
+        case 128:
+            return cap ? launch_prefill_t<128, true>(tmk, tmv, a, s) : launch_prefill_t<128, false>(tmk, tmv, a, s);
         default: return cudaErrorInvalidValue;
     }
 }
