@@ -141,7 +141,7 @@ __device__ __forceinline__ float score_log2(float dot, const PrefillArgs &a) {
 }
 
 template <int D, bool CAP>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __maxnreg__(200)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                         const __grid_constant__ PrefillArgs a) {
     using L = PrefillLayout<D>;

@@ -27,6 +27,10 @@ CASES = {
     "llama_ff_pos131071": (32, 8, 64, 5e5, "llama3", False, False, [131070, 7, 65535], 1, 131072),
     "gemma_d256": (8, 4, 256, 1e4, None, False, False, [8191, 0], 1, 8192),
     "oneplus_norm_d64": (4, 2, 64, 1e4, "distinct", True, True, [5, 17], 3, 64),
+    # Prefill-sized appends (>= 16384 head rows) take the 32-rows-per-warp kernel.
+    "rows32_qwen3_d128": (32, 8, 128, 1e6, None, True, False, [0, 1000], 300, 1300),
+    "rows32_llama_d64": (32, 8, 64, 5e5, "llama3", False, False, [100, 131000], 200, 131200),
+    "rows32_oneplus_d256": (8, 4, 256, 1e4, None, True, True, [0, 50], 600, 700),
 }
 
 
