@@ -141,7 +141,7 @@ __device__ __forceinline__ float score_log2(float dot, const PrefillArgs &a) {
 }
 
 template <int D, bool CAP>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kThreads, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                         const __grid_constant__ PrefillArgs a) {
     using L = PrefillLayout<D>;
@@ -363,7 +363,7 @@ __global__ void __maxnreg__(200)
                         waited_o = true;
                         tc_fence_after();
                         const float alpha = ex2_fast(m_used - mt);
-#pragma unroll
+#pragma unroll 1
                         for (int c = 0; c < D / 32; ++c) {
                             uint32_t o[32];
                             tc_ld32_nowait(tO + c * 32, o);
@@ -430,7 +430,7 @@ __global__ void __maxnreg__(200)
                 tc_fence_after();
                 const float inv = 1.f / l_run;
                 float *dst = a.out + (((size_t)b * T + (row_ok ? t : 0)) * a.Hq + h) * D;
-#pragma unroll
+#pragma unroll 1
                 for (int c = 0; c < D / 32; ++c) {
                     uint32_t o[32];
                     tc_ld32_nowait(tO + c * 32, o);
