@@ -569,6 +569,8 @@ int append_impl(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, i
         return fail(BRK_ERR_INVALID, "rope table head_dim %d != %d", p->rope->head_dim, p->head_dim);
     brk::AppendArgs a;
     memset(&a, 0, sizeof(a));
+    if ((long long)batch * n_tokens * (p->n_heads + 2LL * p->n_kv_heads) >= (1LL << 31))
+        return fail(BRK_ERR_INVALID, "batch * n_tokens * (n_heads + 2 n_kv_heads) must stay below 2^31 rows");
     for (int b = 0; b < batch; ++b) {
         const int last = past_len[b] + n_tokens;
         if (p->rope && last > p->rope->max_pos)

@@ -18,7 +18,6 @@ namespace brk {
 namespace {
 
 constexpr int kRowsPerBlock = 4;  // one warp per head-vector row
-constexpr long long kRows32Threshold = 16384;  // from here on, 32 rows per warp
 
 // DT: the head dim as a compile-time constant (64 / 128 / 256), or 0 for any other even size.
 template <int DT>
@@ -120,117 +119,6 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32) append_kernel(const __grid
     }
 }
 
-// Prefill-sized appends: one warp per 32 rows.  Rows are loaded cooperatively (coalesced) into
-// shared memory with an odd row stride, each lane then runs the ordered sum of squares of its own
-// row (32 chains side by side instead of one lane working while 31 wait), and the lanes
-// normalise, rotate and store each row together.  Same arithmetic as append_kernel.
-template <int D>
-__global__ void __launch_bounds__(32) append_rows32_kernel(const __grid_constant__ AppendArgs a) {
-    griddep_launch_dependents();
-    griddep_wait();
-    constexpr int kStride = D + 1;  // floats; odd, so lane-per-row reads hit distinct banks
-    constexpr int half = D / 2;
-    extern __shared__ float xs[];   // [32][D + 1]
-    const int lane = threadIdx.x;
-    const int per_tok = a.Hq + 2 * a.Hkv;
-    const long long nrows = (long long)a.B * a.T * per_tok;
-    const long long row0 = (long long)blockIdx.x * 32;
-
-    // Where row `row` comes from and goes to; src == nullptr means the row is skipped.
-    struct RowRef {
-        const float *src;
-        const float *gain;
-        float *qdst;
-        __half *cdst;
-        int pos;
-        bool rotate;
-    };
-    auto ref = [&](long long row) {
-        RowRef rf{nullptr, nullptr, nullptr, nullptr, 0, a.rope != nullptr};
-        const int bt = (int)(row / per_tok), kind = (int)(row % per_tok);
-        const int b = bt / a.T, t = bt % a.T;
-        rf.pos = a.past_len[b] + t;
-        if (kind < a.Hq) {
-            if (!a.q_out) return rf;
-            rf.src = a.q_in + ((size_t)bt * a.Hq + kind) * D;
-            rf.gain = a.q_norm;
-            rf.qdst = a.q_out + ((size_t)bt * a.Hq + kind) * D;
-        } else {
-            const bool is_k = kind < a.Hq + a.Hkv;
-            const int h = is_k ? kind - a.Hq : kind - a.Hq - a.Hkv;
-            const float *in = is_k ? a.k_in : a.v_in;
-            if (!in) return rf;
-            rf.src = in + ((size_t)bt * a.Hkv + h) * D;
-            const size_t crow = ((size_t)(a.layer * a.B + b) * a.Hkv + h) * a.cap + (size_t)(rf.pos - a.kv_offset);
-            rf.cdst = (is_k ? a.kc : a.vc) + crow * D;
-            rf.gain = is_k ? a.k_norm : nullptr;
-            rf.rotate = rf.rotate && is_k;
-        }
-        return rf;
-    };
-
-    const int nr = nrows - row0 < 32 ? (int)(nrows - row0) : 32;
-    for (int r = 0; r < nr; ++r) {
-        const RowRef rf = ref(row0 + r);
-        if (!rf.src) continue;
-        for (int d = lane; d < D; d += 32) xs[r * kStride + d] = rf.src[d];
-    }
-    __syncwarp();
-
-    // rmsnormCpu (kernels.ts:3395): ordered sum of x^2 in double, inv = 1/sqrt(ss/dim + eps).
-    double inv = 0.0;
-    if (lane < nr) {
-        const RowRef rf = ref(row0 + lane);
-        if (rf.src && rf.gain) {
-            double ss = 0.0;
-#pragma unroll 8
-            for (int d = 0; d < D; ++d) {
-                const double x = xs[lane * kStride + d];
-                ss = __dadd_rn(ss, __dmul_rn(x, x));
-            }
-            inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)D), a.eps)));
-        }
-    }
-
-    for (int r = 0; r < nr; ++r) {
-        const double inv_r = __shfl_sync(0xffffffffu, inv, r);
-        const RowRef rf = ref(row0 + r);
-        if (!rf.src) continue;
-        const float *x = xs + r * kStride;
-        auto normed = [&](int i) -> double {
-            if (!rf.gain) return (double)x[i];
-            const double w = rf.gain[i];
-            const double g = a.one_plus ? __dadd_rn(1.0, w) : w;
-            return (double)(float)__dmul_rn(__dmul_rn((double)x[i], inv_r), g);
-        };
-        if (rf.rotate) {
-            // ropeCpu (kernels.ts:3445) on the normalised f32 values.
-            const double2 *cs = a.rope + (size_t)rf.pos * half;
-            for (int i = lane; i < half; i += 32) {
-                const double2 e = cs[i];
-                const double x0 = normed(i), x1 = normed(i + half);
-                const float o0 = (float)__dsub_rn(__dmul_rn(x0, e.x), __dmul_rn(x1, e.y));
-                const float o1 = (float)__dadd_rn(__dmul_rn(x1, e.x), __dmul_rn(x0, e.y));
-                if (rf.qdst) {
-                    rf.qdst[i] = o0;
-                    rf.qdst[i + half] = o1;
-                } else {
-                    rf.cdst[i] = __float2half_rn(o0);
-                    rf.cdst[i + half] = __float2half_rn(o1);
-                }
-            }
-        } else {
-            for (int d = lane; d < D; d += 32) {
-                const float y = (float)normed(d);
-                if (rf.qdst)
-                    rf.qdst[d] = y;
-                else
-                    rf.cdst[d] = __float2half_rn(y);
-            }
-        }
-    }
-}
-
 // Plain f32 -> fp16 row store into one (layer, sequence) segment: rows [row0, row0+n) of every
 // kv head.  kc/vc point at row row0 of kv head 0 of the segment; heads are `cap` rows apart.
 __global__ void kv_write_rows_kernel(__half *kc, __half *vc, const float *k, const float *v, int n_rows, int Hkv,
@@ -274,23 +162,6 @@ cudaError_t launch_append(const AppendArgs &a, cudaStream_t s, bool pdl) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    if (rows >= kRows32Threshold && (a.D == 64 || a.D == 128 || a.D == 256)) {
-        // Many rows (prefill chunks): 32 rows per warp.
-        cfg.gridDim = dim3((unsigned)((rows + 31) / 32));
-        cfg.blockDim = dim3(32);
-        cfg.dynamicSmemBytes = (size_t)32 * (a.D + 1) * sizeof(float);
-        switch (a.D) {
-            case 64: return cudaLaunchKernelEx(&cfg, append_rows32_kernel<64>, a);
-            case 128: return cudaLaunchKernelEx(&cfg, append_rows32_kernel<128>, a);
-            default: {
-                cudaError_t e = cudaFuncSetAttribute(append_rows32_kernel<256>,
-                                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                     (int)cfg.dynamicSmemBytes);
-                if (e != cudaSuccess) return e;
-                return cudaLaunchKernelEx(&cfg, append_rows32_kernel<256>, a);
-            }
-        }
-    }
     switch (a.D) {
         case 64: return cudaLaunchKernelEx(&cfg, append_kernel<64>, a);
         case 128: return cudaLaunchKernelEx(&cfg, append_kernel<128>, a);
