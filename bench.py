@@ -120,11 +120,14 @@ def run_prefill(args, c, workload):
         for layer in range(layers):
             for ci in range(nch):
                 pos = [ci * CH] * B
-                eng.appendKv(kv, layer, cfg, qi[layer, ci], ki[layer, ci], vi[layer, ci], q_work, pos)
-                if ev is not None:
+                if ev is None:
+                    # The product path: K/V append + tensor-core kernel with the q prologue fused.
+                    eng.prefillStep(kv, layer, cfg, qi[layer, ci], ki[layer, ci], vi[layer, ci], oo[layer, ci], pos)
+                else:
+                    # Roofline pass: the attention kernel alone, on pre-rotated q.
+                    eng.appendKv(kv, layer, cfg, qi[layer, ci], ki[layer, ci], vi[layer, ci], q_work, pos)
                     ev[layer][ci][0].record(stream)
-                eng.recAttention(kv, layer, cfg, q_work, oo[layer, ci], pos, kernel="prefill")
-                if ev is not None:
+                    eng.recAttention(kv, layer, cfg, q_work, oo[layer, ci], pos, kernel="prefill")
                     ev[layer][ci][1].record(stream)
 
     def barrier():

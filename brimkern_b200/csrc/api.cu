@@ -657,11 +657,21 @@ int brk_attn_decode_static(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_
                       static_cast<cudaStream_t>(stream), scratch, BRK_DECODE_STATIC_SCRATCH_BYTES);
 }
 
-int brk_attn_prefill(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
-                     const int32_t *past_len, const float *q, float *out, void *stream) {
+namespace {
+// The tensor-core prefill launch: q rotated (q) or raw with the prologue fused (q_raw).
+int prefill_impl(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
+                 const int32_t *past_len, const float *q, const float *q_raw, float *out, void *stream) {
     int rc = check_call(ctx, kv, layer, p, batch, n_tokens, past_len);
     if (rc) return rc;
-    if (!q || !out) return fail(BRK_ERR_INVALID, "null q or out");
+    if ((!q && !q_raw) || !out) return fail(BRK_ERR_INVALID, "null q or out");
+    if (q_raw && p->rope) {
+        if (p->rope->head_dim != p->head_dim || p->rope->ctx != ctx)
+            return fail(BRK_ERR_INVALID, "rope table head_dim %d != %d", p->rope->head_dim, p->head_dim);
+        for (int b = 0; b < batch; ++b)
+            if (past_len[b] + n_tokens > p->rope->max_pos)
+                return fail(BRK_ERR_CAPACITY, "position %d beyond the rope table (%d positions)",
+                            past_len[b] + n_tokens - 1, p->rope->max_pos);
+    }
     if (p->head_dim != 64 && p->head_dim != 128)
         return fail(BRK_ERR_UNSUPPORTED, "tensor-core prefill covers head_dim 64 and 128 (got %d)", p->head_dim);
     brk::PrefillArgs a;
@@ -674,7 +684,12 @@ int brk_attn_prefill(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_p
     }
     if ((n_tokens + 127) / 128 > 65535) return fail(BRK_ERR_INVALID, "n_tokens %d too large", n_tokens);
     DeviceGuard g(ctx->device);
-    a.q = q;
+    a.q = q_raw ? nullptr : q;
+    a.q_raw = q_raw;
+    a.q_norm = q_raw ? p->q_norm : nullptr;
+    a.rope = q_raw && p->rope ? p->rope->table : nullptr;
+    a.eps = p->eps;
+    a.one_plus = p->norm_one_plus ? 1 : 0;
     a.out = out;
     a.err = ctx->d_err;
     a.B = batch;
@@ -697,6 +712,22 @@ int brk_attn_prefill(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_p
     if (e != cudaSuccess) return cuda_fail(e, "prefill kernel launch");
     ++ctx->launches;
     return BRK_OK;
+}
+}  // namespace
+
+int brk_attn_prefill(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
+                     const int32_t *past_len, const float *q, float *out, void *stream) {
+    return prefill_impl(ctx, kv, layer, p, batch, n_tokens, past_len, q, nullptr, out, stream);
+}
+
+int brk_attn_prefill_step(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
+                          const int32_t *past_len, const float *q_in, const float *k_in, const float *v_in, float *out,
+                          void *stream) {
+    if (!q_in || !k_in || !v_in || !out) return fail(BRK_ERR_INVALID, "null tensor argument");
+    // K/V rows only: the q prologue runs inside the prefill kernel.
+    int rc = append_impl(ctx, kv, layer, p, batch, n_tokens, past_len, nullptr, k_in, v_in, nullptr, stream, false);
+    if (rc) return rc;
+    return prefill_impl(ctx, kv, layer, p, batch, n_tokens, past_len, nullptr, q_in, out, stream);
 }
 
 int brk_attn_forward(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,

@@ -71,8 +71,14 @@ struct DecodeArgs {
 };
 
 struct PrefillArgs {
-    const float *q;  // [B][T][Hq][D] f32 (rotated)
+    const float *q;  // [B][T][Hq][D] f32 (rotated), or nullptr when q_raw is given
     float *out;      // [B][T][Hq][D] f32
+    // Fused q prologue (brk_attn_prefill_step): raw projection q, gain, rope table.
+    const float *q_raw;
+    const float *q_norm;
+    const double2 *rope;
+    double eps;
+    int one_plus;
     int *err;
     int B, T, Hq, Hkv, layer, cap, kv_offset, window;
     float scale_log2, softcap, cap_k1, cap_k2;

@@ -376,16 +376,33 @@ class AttentionEngine:
         out = torch.empty_like(q_in) if out is None else out
         base = [int(past_len)] * B if np.isscalar(past_len) else [int(x) for x in past_len]
         q_work = torch.empty((B, min(chunk, T), cfg.n_heads, cfg.head_dim), dtype=torch.float32, device=q_in.device)
+        G = cfg.n_heads // cfg.n_kv_heads
         for c0 in range(0, T, chunk):
             c1 = min(T, c0 + chunk)
             pos = [p + c0 for p in base]
             qc = q_in[:, c0:c1].contiguous()
-            qw = q_work[:, :c1 - c0]
             oc = torch.empty_like(qc)
-            self.appendKv(kv, layer, cfg, qc, k_in[:, c0:c1].contiguous(), v_in[:, c0:c1].contiguous(), qw, pos,
-                          stream)
-            self.recAttention(kv, layer, cfg, qw, oc, pos, "auto", stream)
+            if (self.attnDecodeOk is False or (c1 - c0) * G > 128) and cfg.head_dim in (64, 128):
+                # Tensor-core chunk with the q prologue fused into the kernel.
+                self.prefillStep(kv, layer, cfg, qc, k_in[:, c0:c1].contiguous(), v_in[:, c0:c1].contiguous(), oc,
+                                 pos, stream)
+            else:
+                qw = q_work[:, :c1 - c0]
+                self.appendKv(kv, layer, cfg, qc, k_in[:, c0:c1].contiguous(), v_in[:, c0:c1].contiguous(), qw, pos,
+                              stream)
+                self.recAttention(kv, layer, cfg, qw, oc, pos, "auto", stream)
             out[:, c0:c1].copy_(oc)
+        return out
+
+    def prefillStep(self, kv: KvCache, layer: int, cfg: AttnConfig, q_in: torch.Tensor, k_in: torch.Tensor,
+                    v_in: torch.Tensor, out: torch.Tensor, past_len, stream=None) -> torch.Tensor:
+        """One prefill chunk: K/V append, then the tensor-core kernel with the q prologue fused."""
+        B = kv.batch
+        T = q_in.numel() // (B * cfg.n_heads * cfg.head_dim)
+        p = cfg.params()
+        pos = _positions(past_len, B)
+        check(L.lib().brk_attn_prefill_step(self.ctx.handle, kv.handle, layer, ctypes.byref(p), B, T, pos,
+                                            _ptr(q_in), _ptr(k_in), _ptr(v_in), _ptr(out), _stream_ptr(stream)))
         return out
 
     def decodePartial(self, kv: KvCache, layer: int, cfg: AttnConfig, q: torch.Tensor, part_ml: torch.Tensor,

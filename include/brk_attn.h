@@ -181,6 +181,15 @@ int brk_attn_prefill(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_p
                      int batch, int n_tokens, const int32_t *past_len, const float *q, float *out,
                      void *stream);
 
+/* One prefill chunk of a layer's attention slice (recordLayerKV, kernels.ts:1707-1731, as the
+ * chunked prefill of lfm2Model.ts:320-333): K/V appended as by brk_attn_append, then the
+ * tensor-core kernel with the q prologue (QK-norm + RoPE, same arithmetic) fused into its q
+ * staging, so the rotated q never round-trips through HBM.  head_dim 64 or 128.
+ * q_in [B][T][Hq][D], k_in / v_in [B][T][Hkv][D] f32 projections; out [B][T][Hq][D] f32. */
+int brk_attn_prefill_step(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p,
+                          int batch, int n_tokens, const int32_t *past_len, const float *q_in,
+                          const float *k_in, const float *v_in, float *out, void *stream);
+
 /* Split-KV partial over this cache's rows (extension, no reference counterpart; used to shard
  * a long context across GPUs): per row R = (b*T + t)*Hq + h, part_ml[2R] = max score m (natural
  * log units, -inf if no key), part_ml[2R+1] = sum l of exp(s - m), part_o[R*D..] = sum of

@@ -91,3 +91,39 @@ def test_chunked_prefill_end_to_end(eng):
     assert_close(out.cpu().numpy().ravel(), ref, what="chunked prefill")
     kv.close()
     rope.close()
+
+
+@pytest.mark.parametrize("D,norm,one_plus", [(128, True, False), (64, False, False), (128, True, True)])
+def test_prefill_step_fused_prologue_is_identical(eng, D, norm, one_plus):
+    """brk_attn_prefill_step (q prologue fused into the prefill kernel) produces bit-for-bit the
+    output of append + prefill on the rotated q, and the same cache rows."""
+    import torch
+    from brimkern_b200.engine import AttnConfig, KvCache, RopeTable
+    rng = np.random.default_rng(D + 7 * norm + 13 * one_plus)
+    Hq, Hkv, T, pasts, base = 8, 2, 300, [0, 100], 1e6
+    dev = eng.device
+    g = (0.1 if one_plus else 0.02)
+    qn = torch.from_numpy(((0 if one_plus else 1) + g * rng.standard_normal(D)).astype(np.float32)).to(dev)
+    kn = torch.from_numpy(((0 if one_plus else 1) + g * rng.standard_normal(D)).astype(np.float32)).to(dev)
+    rope = RopeTable(eng.ctx, D, base, None, max(pasts) + T)
+    cfg = AttnConfig(Hq, Hkv, D, q_norm=qn if norm else None, k_norm=kn if norm else None, one_plus=one_plus,
+                     rope=rope)
+    q = torch.from_numpy(normal(rng, 2, T, Hq, D)).to(dev)
+    k = torch.from_numpy(normal(rng, 2, T, Hkv, D)).to(dev)
+    v = torch.from_numpy(normal(rng, 2, T, Hkv, D)).to(dev)
+    kv_a = KvCache(eng.ctx, 1, 2, Hkv, D, max(pasts) + T)
+    kv_b = KvCache(eng.ctx, 1, 2, Hkv, D, max(pasts) + T)
+    q_rot = torch.empty_like(q)
+    out_a = torch.empty_like(q)
+    out_b = torch.empty_like(q)
+    eng.appendKv(kv_a, 0, cfg, q, k, v, q_rot, pasts)
+    eng.recAttention(kv_a, 0, cfg, q_rot, out_a, pasts, kernel="prefill")
+    eng.prefillStep(kv_b, 0, cfg, q, k, v, out_b, pasts)
+    eng.ctx.check()
+    assert torch.equal(out_a, out_b)
+    for b, p in enumerate(pasts):
+        ka, va = kv_a.read_rows(0, b, p, T)
+        kb, vb = kv_b.read_rows(0, b, p, T)
+        assert torch.equal(ka.view(torch.int16), kb.view(torch.int16))
+        assert torch.equal(va.view(torch.int16), vb.view(torch.int16))
+    kv_a.close(), kv_b.close(), rope.close()
