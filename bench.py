@@ -49,13 +49,15 @@ CONFIGS = {
 
 def kv_bytes_per_step(c, batch):
     """Algorithmic KV bytes one step reads: per layer and sequence, K and V rows of the attended
-    range (the window on windowed layers), Hkv x D fp16 each."""
+    range (the window on windowed layers), Hkv x D fp16 each -- or, for the int8 cache, Hkv x D
+    one-byte codes plus one f32 scale per (row, kv head)."""
+    row_bytes = c["D"] + 4 if c.get("kv") == "q8" else c["D"] * 2
     total = 0
     for layer in range(c["layers"]):
         keys = c["L"]
         if c["window_even"] and layer % 2 == 0:
             keys = min(keys, c["window_even"])
-        total += batch * keys * c["Hkv"] * c["D"] * 2 * 2
+        total += batch * keys * c["Hkv"] * row_bytes * 2
     return total
 
 
@@ -427,10 +429,12 @@ def cpu_reference_sample(c, batch, target_s, threads=0, seed=7):
                           threads)
     dt = time.perf_counter() - t0
     units = reps * pool
-    gbs = units * keys * c["Hkv"] * c["D"] * 4 / dt / 1e9  # fp16 K+V bytes of those units
+    q8 = c.get("kv") == "q8"
+    row_bytes = c["D"] + 4 if q8 else c["D"] * 2
+    gbs = units * keys * c["Hkv"] * row_bytes * 2 / dt / 1e9  # K+V bytes of those units in the cache type
     desc = (f"{units} (layer, sequence) decode units at KV length {keys} ({c['Hq']}q/{c['Hkv']}kv, D {c['D']}), "
-            f"JS-faithful double arithmetic over f32 K/V, {used} threads, {dt:.1f} s; bytes counted as the fp16 "
-            f"KV of those units")
+            f"JS-faithful double arithmetic over f32 K/V, {used} threads, {dt:.1f} s; bytes counted as the "
+            f"{'int8 codes + scales' if q8 else 'fp16 KV'} of those units")
     return gbs, used, desc
 
 
@@ -473,6 +477,8 @@ def main():
     ap.add_argument("--kv-len", type=int, default=None, help="override the KV length (tests only)")
     ap.add_argument("--softcap", type=float, default=None, help="override the logit softcap (diagnostics)")
     ap.add_argument("--window", type=int, default=None, help="override the even-layer window (diagnostics)")
+    ap.add_argument("--kv", choices=["f16", "q8"], default="f16",
+                    help="KV cache type: fp16, or the reference's int8 mode (setKvQuant)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
@@ -487,6 +493,7 @@ def main():
         c["window_even"] = args.window
     args.batch = args.batch or c["batch"]
     args.warmup = max(args.warmup, 3)
+    c["kv"] = args.kv
     workload = args.workload
     if args.impl == "reference":
         return run_reference(args, c, workload)
@@ -527,7 +534,8 @@ def main():
         window = c["window_even"] if (c["window_even"] and layer % 2 == 0) else 0
         cfgs.append(AttnConfig(Hq, Hkv, D, scale=c["scale"], softcap=c["softcap"], window=window, q_norm=qn,
                                k_norm=kn, rope=rope))
-    kv = KvCache(eng.ctx, layers, B, Hkv, D, Lkv)
+    q8 = c["kv"] == "q8"
+    kv = KvCache(eng.ctx, layers, B, Hkv, D, Lkv, q8=q8)
     tmp_k = torch.empty((Lkv, Hkv, D), dtype=torch.float32, device=dev)
     tmp_v = torch.empty_like(tmp_k)
     for layer in range(layers):
@@ -607,10 +615,11 @@ def main():
     attn_avg_ms = sum(attn_ms) / len(attn_ms)
     bytes_launch = bytes_step / layers
     achieved = bytes_launch / (attn_avg_ms * 1e-3) / 1e9
-    traffic = read_traffic(workload)
+    traffic = read_traffic(workload + ("-q8" if q8 else ""))
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                "kernel": "decode_attn_kernel", "timing": f"CUDA events around each decode launch, {rsteps} steps",
+                "kernel": "decode_q8_kernel" if q8 else "decode_attn_kernel",
+                "timing": f"CUDA events around each decode launch, {rsteps} steps",
                 "bytes_per_launch": bytes_launch,
                 "avg_launch_ms": round(attn_avg_ms, 5), "frac_of_8TBs": round(achieved / 8000.0, 4)}
 
@@ -661,8 +670,11 @@ def main():
         line = {
             "metric": "decode-attn KV-read GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16 KV / f32 accumulate", "data": "synthetic",
-            "config": {"workload": workload, "global_batch": B * world, "batch_per_gpu": B, "kv_len": Lkv,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 KV + f32 row scales / f32 accumulate" if q8 else "f16 KV / f32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": workload, "kv_cache": "int8" if q8 else "fp16", "global_batch": B * world,
+                       "batch_per_gpu": B, "kv_len": Lkv,
                        "layers": layers, "heads": f"{Hq}q/{Hkv}kv", "head_dim": D,
                        "parallelism": f"batch-sharded x{world} (no communication)",
                        "l2": f"no flush: each step streams {bytes_step / 1e9:.1f} GB of KV > 126 MB L2"},

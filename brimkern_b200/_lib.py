@@ -21,6 +21,7 @@ BRK_ERR_UNSUPPORTED = -4
 BRK_ERR_DEVICE = -5
 BRK_MAX_BATCH = 512
 BRK_KV_F16 = 0
+BRK_KV_I8 = 1
 BRK_DECODE_STATIC_SCRATCH_BYTES = 8 << 20
 
 _ERR_NAMES = {BRK_ERR_INVALID: "INVALID", BRK_ERR_CUDA: "CUDA", BRK_ERR_CAPACITY: "CAPACITY",
@@ -70,6 +71,8 @@ SIGNATURES = [
     ("brk_kv_reset", _i, [_vp, _vp]),
     ("brk_kv_write_rows", _i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     ("brk_kv_read_rows", _i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp]),
+    ("brk_kv_write_codes", _i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp]),
+    ("brk_kv_read_codes", _i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp]),
     ("brk_attn_append", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp, _vp, _vp]),
     ("brk_attn_step", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp, _vp, _vp, _vp]),
     ("brk_attn_forward", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp]),

@@ -64,20 +64,34 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// 2-D map over a cache buffer viewed as [rows][head_dim] fp16, box = [box_rows][64] with the
-// 128-byte swizzle that the kernels' shared-memory addressing assumes.
-int make_cache_map(CUtensorMap *m, const __half *base, uint64_t rows, int head_dim, int box_rows) {
+// 2-D map over a row-major [rows][cols] buffer with box [box_rows][box_cols].
+int make_map(CUtensorMap *m, CUtensorMapDataType type, size_t esize, const void *base, uint64_t rows, uint64_t cols,
+             uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
     auto enc = tensor_map_encoder();
     if (!enc) return fail(BRK_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-    cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)head_dim * sizeof(__half)};
-    cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(cols * esize)};
+    cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1u, 1u};
-    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = enc(m, type, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(BRK_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return BRK_OK;
+}
+
+// fp16 cache rows [rows][head_dim], box = [box_rows][64] with the 128-byte swizzle that the
+// kernels' shared-memory addressing assumes.
+int make_cache_map(CUtensorMap *m, const __half *base, uint64_t rows, int head_dim, int box_rows) {
+    return make_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sizeof(__half), base, rows, (uint64_t)head_dim, 64u,
+                    (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// int8 code rows [rows][head_dim] bytes, box = [box_rows][min(head_dim, 128) B]: 128-byte swizzle,
+// or the 64-byte one for head_dim 64 (the addressing of decode_q8.cu).
+int make_code_map(CUtensorMap *m, const uint8_t *base, uint64_t rows, int head_dim, int box_rows) {
+    const bool narrow = head_dim < 128;
+    return make_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, rows, (uint64_t)head_dim, narrow ? 64u : 128u,
+                    (uint32_t)box_rows, narrow ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 bool supported_head_dim(int d) { return d == 64 || d == 128 || d == 256; }
@@ -86,9 +100,73 @@ size_t kv_elems(const brk_kv_desc &d, int cap) {
     return (size_t)d.n_layers * d.batch * d.n_kv_heads * (size_t)cap * d.head_dim;
 }
 
+size_t kv_segments(const brk_kv_desc &d) { return (size_t)d.n_layers * d.batch * d.n_kv_heads; }
+
+// Zeroes every buffer of the cache: fp16 rows, or int8 codes (byte 0x80 = code 0, the storage
+// being biased by +128) and scales.
+cudaError_t kv_zero(brk_kv *kv, cudaStream_t s) {
+    const size_t elems = kv_elems(kv->desc, kv->cap);
+    cudaError_t e = cudaSuccess;
+    if (kv->q8()) {
+        e = cudaMemsetAsync(kv->k8, 0x80, elems, s);
+        if (e == cudaSuccess) e = cudaMemsetAsync(kv->v8, 0x80, elems, s);
+        if (e == cudaSuccess)
+            e = cudaMemsetAsync(kv->scales, 0, kv_segments(kv->desc) * 2 * kv->scale_pitch * sizeof(float), s);
+    } else {
+        e = cudaMemsetAsync(kv->k, 0, elems * sizeof(__half), s);
+        if (e == cudaSuccess) e = cudaMemsetAsync(kv->v, 0, elems * sizeof(__half), s);
+    }
+    return e;
+}
+
+// Allocates zeroed buffers for capacity `cap` into kv (the previous pointers are overwritten, not
+// freed).  On failure the buffers that were allocated stay in kv for kv_free.
+cudaError_t kv_alloc(brk_kv *kv, int cap) {
+    kv->k = kv->v = nullptr;
+    kv->k8 = kv->v8 = nullptr;
+    kv->scales = nullptr;
+    const int saved_cap = kv->cap;
+    kv->cap = cap;
+    const size_t elems = kv_elems(kv->desc, cap);
+    cudaError_t e;
+    if (kv->q8()) {
+        kv->scale_pitch = (cap + 3) / 4 * 4;
+        e = cudaMalloc(&kv->k8, elems);
+        if (e == cudaSuccess) e = cudaMalloc(&kv->v8, elems);
+        if (e == cudaSuccess) e = cudaMalloc(&kv->scales, kv_segments(kv->desc) * 2 * kv->scale_pitch * sizeof(float));
+    } else {
+        e = cudaMalloc(&kv->k, elems * sizeof(__half));
+        if (e == cudaSuccess) e = cudaMalloc(&kv->v, elems * sizeof(__half));
+    }
+    if (e == cudaSuccess) e = kv_zero(kv, 0);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(0);
+    kv->cap = saved_cap;
+    return e;
+}
+
+void kv_free(brk_kv *kv) {
+    cudaFree(kv->k);
+    cudaFree(kv->v);
+    cudaFree(kv->k8);
+    cudaFree(kv->v8);
+    cudaFree(kv->scales);
+    kv->k = kv->v = nullptr;
+    kv->k8 = kv->v8 = nullptr;
+    kv->scales = nullptr;
+}
+
 int kv_build_maps(brk_kv *kv) {
     const uint64_t rows = (uint64_t)kv->desc.n_layers * kv->desc.batch * kv->desc.n_kv_heads * kv->cap;
     int rc;
+    if (kv->q8()) {
+        const int sk = brk::decode_stage_keys(kv->desc.head_dim);
+        if ((rc = make_code_map(&kv->tm_dec_k, kv->k8, rows, kv->desc.head_dim, sk))) return rc;
+        if ((rc = make_code_map(&kv->tm_dec_v, kv->v8, rows, kv->desc.head_dim, sk))) return rc;
+        // Scales [segment][K, V][pitch]: one box = both scale rows of a stage's keys.
+        return make_map(&kv->tm_dec_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, sizeof(float), kv->scales,
+                        kv_segments(kv->desc) * 2, (uint64_t)kv->scale_pitch, (uint32_t)sk, 2u,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
     if ((rc = make_cache_map(&kv->tm_dec_k, kv->k, rows, kv->desc.head_dim, brk::decode_stage_keys(kv->desc.head_dim))))
         return rc;
     if ((rc = make_cache_map(&kv->tm_dec_v, kv->v, rows, kv->desc.head_dim, brk::decode_stage_keys(kv->desc.head_dim))))
@@ -128,14 +206,14 @@ float effective_scale(const brk_attn_params *p) {
 
 // Splits of the key range per (sequence, kv head, row tile): enough CTAs to fill the GPU's
 // concurrent slots without leaving a mostly-empty last wave; BRK_DECODE_SPLITS overrides.
-int choose_splits(const brk_ctx *ctx, int head_dim, int units, int span) {
+int choose_splits(const brk_ctx *ctx, int head_dim, bool q8, int units, int span) {
     const int tk = brk::decode_stage_keys(head_dim);
     const int max_split = std::max(1, std::min(64, (span + tk - 1) / tk));
     if (const char *env = getenv("BRK_DECODE_SPLITS")) {
         int n = atoi(env);
         if (n >= 1) return std::min(n, max_split);
     }
-    const long long slots = (long long)ctx->num_sms * brk::decode_ctas_per_sm(head_dim);
+    const long long slots = (long long)ctx->num_sms * brk::decode_ctas_per_sm(head_dim, q8);
     double best = 1e30;
     int best_n = 1;
     for (int n = 1; n <= max_split; ++n) {
@@ -199,7 +277,7 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
         span = std::max(span, hi - lo);
     }
     const int units = batch * p->n_kv_heads * a.mtiles;
-    int nsplit = choose_splits(ctx, D, units, span);
+    int nsplit = choose_splits(ctx, D, kv->q8(), units, span);
     const int tk = brk::decode_stage_keys(D);
     a.keys_per_split = ((span + nsplit - 1) / nsplit + tk - 1) / tk * tk;
     nsplit = (span + a.keys_per_split - 1) / a.keys_per_split;
@@ -238,8 +316,10 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
         a.res_ml = part_ml;
         a.res_o = part_o;
     }
-    cudaError_t e = brk::launch_decode(D, kv->tm_dec_k, kv->tm_dec_v, a, nsplit, p->n_kv_heads * a.mtiles, batch, stream,
-                                       pdl);
+    cudaError_t e = kv->q8() ? brk::launch_decode_q8(D, kv->tm_dec_k, kv->tm_dec_v, kv->tm_dec_s, a, nsplit,
+                                                     p->n_kv_heads * a.mtiles, batch, stream, pdl)
+                             : brk::launch_decode(D, kv->tm_dec_k, kv->tm_dec_v, a, nsplit, p->n_kv_heads * a.mtiles,
+                                                  batch, stream, pdl);
     if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
     ++ctx->launches;
     return BRK_OK;
@@ -312,6 +392,7 @@ int brk_ctx_destroy(brk_ctx *ctx) {
     cudaDeviceSynchronize();
     cudaFree(ctx->d_err);
     cudaFree(ctx->ws);
+    cudaFree(ctx->stage);
     delete ctx;
     return BRK_OK;
 }
@@ -424,7 +505,8 @@ int brk_kv_create(brk_ctx *ctx, const brk_kv_desc *desc, brk_kv **out) {
     if (!ctx || !desc || !out) return fail(BRK_ERR_INVALID, "null argument");
     *out = nullptr;
     const brk_kv_desc &d = *desc;
-    if (d.dtype != BRK_KV_F16) return fail(BRK_ERR_UNSUPPORTED, "kv dtype %d (only BRK_KV_F16)", d.dtype);
+    if (d.dtype != BRK_KV_F16 && d.dtype != BRK_KV_I8)
+        return fail(BRK_ERR_UNSUPPORTED, "kv dtype %d (BRK_KV_F16 or BRK_KV_I8)", d.dtype);
     if (!supported_head_dim(d.head_dim)) return fail(BRK_ERR_UNSUPPORTED, "head_dim %d (64, 128 or 256)", d.head_dim);
     if (d.n_layers < 1 || d.batch < 1 || d.batch > BRK_MAX_BATCH || d.n_kv_heads < 1 || d.capacity < 1)
         return fail(BRK_ERR_INVALID, "invalid kv descriptor");
@@ -435,21 +517,15 @@ int brk_kv_create(brk_ctx *ctx, const brk_kv_desc *desc, brk_kv **out) {
     kv->ctx = ctx;
     kv->desc = d;
     kv->cap = d.capacity;
-    const size_t bytes = kv_elems(d, kv->cap) * sizeof(__half);
-    cudaError_t e = cudaMalloc(&kv->k, bytes);
-    if (e == cudaSuccess) e = cudaMalloc(&kv->v, bytes);
-    if (e == cudaSuccess) e = cudaMemset(kv->k, 0, bytes);
-    if (e == cudaSuccess) e = cudaMemset(kv->v, 0, bytes);
+    cudaError_t e = kv_alloc(kv, kv->cap);
     if (e != cudaSuccess) {
-        cudaFree(kv->k);
-        cudaFree(kv->v);
+        kv_free(kv);
         delete kv;
         return cuda_fail(e, "kv cache allocation");
     }
     int rc = kv_build_maps(kv);
     if (rc) {
-        cudaFree(kv->k);
-        cudaFree(kv->v);
+        kv_free(kv);
         delete kv;
         return rc;
     }
@@ -461,8 +537,7 @@ int brk_kv_destroy(brk_kv *kv) {
     if (!kv) return BRK_OK;
     DeviceGuard g(kv->ctx->device);
     cudaDeviceSynchronize();
-    cudaFree(kv->k);
-    cudaFree(kv->v);
+    kv_free(kv);
     delete kv;
     return BRK_OK;
 }
@@ -478,27 +553,32 @@ int brk_kv_grow(brk_kv *kv, int rows, void *stream) {
         return fail(BRK_ERR_CAPACITY, "growing to %d rows exceeds 2^31 cache rows", cap);
     DeviceGuard g(kv->ctx->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const size_t bytes = kv_elems(d, cap) * sizeof(__half);
-    __half *nk = nullptr, *nv = nullptr;
-    cudaError_t e = cudaMalloc(&nk, bytes);
-    if (e == cudaSuccess) e = cudaMalloc(&nv, bytes);
-    if (e != cudaSuccess) {
-        cudaFree(nk);
-        cudaFree(nv);
-        return cuda_fail(e, "kv cache growth");
-    }
-    const size_t segs = (size_t)d.n_layers * d.batch * d.n_kv_heads;
-    const size_t old_pitch = (size_t)kv->cap * d.head_dim * sizeof(__half);
-    const size_t new_pitch = (size_t)cap * d.head_dim * sizeof(__half);
-    BRK_CUDA(cudaMemsetAsync(nk, 0, bytes, s));
-    BRK_CUDA(cudaMemsetAsync(nv, 0, bytes, s));
-    BRK_CUDA(cudaMemcpy2DAsync(nk, new_pitch, kv->k, old_pitch, old_pitch, segs, cudaMemcpyDeviceToDevice, s));
-    BRK_CUDA(cudaMemcpy2DAsync(nv, new_pitch, kv->v, old_pitch, old_pitch, segs, cudaMemcpyDeviceToDevice, s));
-    BRK_CUDA(cudaStreamSynchronize(s));
-    cudaFree(kv->k);
-    cudaFree(kv->v);
-    kv->k = nk;
-    kv->v = nv;
+    brk_kv old = *kv;  // the current buffers, copied from below
+    // On failure: drop the new buffers and keep the cache as it was.
+    auto restore = [&](cudaError_t err, const char *what) {
+        kv_free(kv);
+        kv->k = old.k, kv->v = old.v, kv->k8 = old.k8, kv->v8 = old.v8, kv->scales = old.scales;
+        kv->scale_pitch = old.scale_pitch;
+        return cuda_fail(err, what);
+    };
+    cudaError_t e = kv_alloc(kv, cap);  // zeroed buffers of the new capacity
+    if (e != cudaSuccess) return restore(e, "kv cache growth");
+    const size_t segs = kv_segments(d);
+    const size_t esz = kv->q8() ? 1 : sizeof(__half);
+    const size_t old_pitch = (size_t)old.cap * d.head_dim * esz;
+    const size_t new_pitch = (size_t)cap * d.head_dim * esz;
+    void *dk = kv->q8() ? (void *)kv->k8 : (void *)kv->k, *dv = kv->q8() ? (void *)kv->v8 : (void *)kv->v;
+    const void *sk = kv->q8() ? (const void *)old.k8 : (const void *)old.k;
+    const void *sv = kv->q8() ? (const void *)old.v8 : (const void *)old.v;
+    e = cudaMemcpy2DAsync(dk, new_pitch, sk, old_pitch, old_pitch, segs, cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpy2DAsync(dv, new_pitch, sv, old_pitch, old_pitch, segs, cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess && kv->q8())
+        e = cudaMemcpy2DAsync(kv->scales, (size_t)kv->scale_pitch * sizeof(float), old.scales,
+                              (size_t)old.scale_pitch * sizeof(float), (size_t)old.cap * sizeof(float), segs * 2,
+                              cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return restore(e, "kv cache growth copy");
+    kv_free(&old);
     kv->cap = cap;
     return kv_build_maps(kv);
 }
@@ -506,10 +586,8 @@ int brk_kv_grow(brk_kv *kv, int rows, void *stream) {
 int brk_kv_reset(brk_kv *kv, void *stream) {
     if (!kv) return fail(BRK_ERR_INVALID, "null kv");
     DeviceGuard g(kv->ctx->device);
-    const size_t bytes = kv_elems(kv->desc, kv->cap) * sizeof(__half);
-    BRK_CUDA(cudaMemsetAsync(kv->k, 0, bytes, static_cast<cudaStream_t>(stream)));
-    BRK_CUDA(cudaMemsetAsync(kv->v, 0, bytes, static_cast<cudaStream_t>(stream)));
-    return BRK_OK;
+    cudaError_t e = kv_zero(kv, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? BRK_OK : cuda_fail(e, "kv reset");
 }
 
 static int check_rows(const brk_kv *kv, int layer, int seq, int row0, int n_rows) {
@@ -527,9 +605,16 @@ int brk_kv_write_rows(brk_kv *kv, int layer, int seq, int row0, int n_rows, cons
     if (rc) return rc;
     DeviceGuard g(kv->ctx->device);
     const brk_kv_desc &d = kv->desc;
-    const size_t off = ((size_t)(layer * d.batch + seq) * d.n_kv_heads * kv->cap + row0) * d.head_dim;
-    cudaError_t e = brk::launch_kv_write_rows(kv->k + off, kv->v + off, k, v, n_rows, d.n_kv_heads, d.head_dim, kv->cap,
-                                              static_cast<cudaStream_t>(stream));
+    const size_t seg0 = (size_t)(layer * d.batch + seq) * d.n_kv_heads;
+    const size_t off = (seg0 * kv->cap + row0) * d.head_dim;
+    cudaError_t e;
+    if (kv->q8())
+        e = brk::launch_kv_write_q8(kv->k8 + off, kv->v8 + off, kv->scales + seg0 * 2 * kv->scale_pitch + row0, k, v,
+                                    n_rows, d.n_kv_heads, d.head_dim, kv->cap, kv->scale_pitch,
+                                    static_cast<cudaStream_t>(stream));
+    else
+        e = brk::launch_kv_write_rows(kv->k + off, kv->v + off, k, v, n_rows, d.n_kv_heads, d.head_dim, kv->cap,
+                                      static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? BRK_OK : cuda_fail(e, "kv write");
 }
 
@@ -537,12 +622,44 @@ int brk_kv_read_rows(const brk_kv *kv, int layer, int seq, int row0, int n_rows,
                      void *stream) {
     int rc = check_rows(kv, layer, seq, row0, n_rows);
     if (rc) return rc;
+    if (kv->q8()) return fail(BRK_ERR_UNSUPPORTED, "int8 cache: read codes and scales with brk_kv_read_codes");
     DeviceGuard g(kv->ctx->device);
     const brk_kv_desc &d = kv->desc;
     const size_t off = ((size_t)(layer * d.batch + seq) * d.n_kv_heads * kv->cap + row0) * d.head_dim;
     cudaError_t e = brk::launch_kv_read_rows(kv->k + off, kv->v + off, k_out, v_out, n_rows, d.n_kv_heads, d.head_dim,
                                              kv->cap, static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? BRK_OK : cuda_fail(e, "kv read");
+}
+
+int brk_kv_write_codes(brk_kv *kv, int layer, int seq, int row0, int n_rows, const int8_t *k_codes,
+                       const float *k_scales, const int8_t *v_codes, const float *v_scales, void *stream) {
+    int rc = check_rows(kv, layer, seq, row0, n_rows);
+    if (rc) return rc;
+    if (!kv->q8()) return fail(BRK_ERR_UNSUPPORTED, "brk_kv_write_codes needs an int8 cache");
+    if (!k_codes != !k_scales || !v_codes != !v_scales) return fail(BRK_ERR_INVALID, "codes and scales go together");
+    DeviceGuard g(kv->ctx->device);
+    const brk_kv_desc &d = kv->desc;
+    const size_t seg0 = (size_t)(layer * d.batch + seq) * d.n_kv_heads;
+    const size_t off = (seg0 * kv->cap + row0) * d.head_dim;
+    cudaError_t e = brk::launch_kv_store_codes(kv->k8 + off, kv->v8 + off, kv->scales + seg0 * 2 * kv->scale_pitch + row0,
+                                               k_codes, k_scales, v_codes, v_scales, n_rows, d.n_kv_heads, d.head_dim,
+                                               kv->cap, kv->scale_pitch, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? BRK_OK : cuda_fail(e, "kv code store");
+}
+
+int brk_kv_read_codes(const brk_kv *kv, int layer, int seq, int row0, int n_rows, int8_t *k_codes, float *k_scales,
+                      int8_t *v_codes, float *v_scales, void *stream) {
+    int rc = check_rows(kv, layer, seq, row0, n_rows);
+    if (rc) return rc;
+    if (!kv->q8()) return fail(BRK_ERR_UNSUPPORTED, "brk_kv_read_codes needs an int8 cache");
+    DeviceGuard g(kv->ctx->device);
+    const brk_kv_desc &d = kv->desc;
+    const size_t seg0 = (size_t)(layer * d.batch + seq) * d.n_kv_heads;
+    const size_t off = (seg0 * kv->cap + row0) * d.head_dim;
+    cudaError_t e = brk::launch_kv_read_q8(kv->k8 + off, kv->v8 + off, kv->scales + seg0 * 2 * kv->scale_pitch + row0,
+                                           k_codes, k_scales, v_codes, v_scales, n_rows, d.n_kv_heads, d.head_dim,
+                                           kv->cap, kv->scale_pitch, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? BRK_OK : cuda_fail(e, "kv code read");
 }
 
 namespace {
@@ -587,6 +704,10 @@ int append_impl(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, i
     a.q_out = q_out;
     a.kc = kv ? kv->k : nullptr;
     a.vc = kv ? kv->v : nullptr;
+    a.kc8 = kv ? kv->k8 : nullptr;
+    a.vc8 = kv ? kv->v8 : nullptr;
+    a.scales = kv ? kv->scales : nullptr;
+    a.scale_pitch = kv ? kv->scale_pitch : 0;
     a.rope = p->rope ? p->rope->table : nullptr;
     a.rope_max = p->rope ? p->rope->max_pos : 0;
     a.q_norm = p->q_norm;
@@ -658,6 +779,18 @@ int brk_attn_decode_static(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_
 }
 
 namespace {
+// Grows the context's prefill staging buffer to at least `bytes` (int8 caches only).
+int ensure_stage(brk_ctx *ctx, size_t bytes) {
+    if (bytes <= ctx->stage_bytes) return BRK_OK;
+    BRK_CUDA(cudaDeviceSynchronize());  // queued kernels may still read the old buffer
+    cudaFree(ctx->stage);
+    ctx->stage = nullptr;
+    ctx->stage_bytes = 0;
+    BRK_CUDA(cudaMalloc(&ctx->stage, bytes));
+    ctx->stage_bytes = bytes;
+    return BRK_OK;
+}
+
 // The tensor-core prefill launch: q rotated (q) or raw with the prologue fused (q_raw).
 int prefill_impl(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
                  const int32_t *past_len, const float *q, const float *q_raw, float *out, void *stream) {
@@ -708,7 +841,32 @@ int prefill_impl(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_param
         a.cap_k1 = (float)(2.0 * (double)scale * log2e / (double)a.softcap);
         a.cap_k2 = (float)((double)a.softcap * log2e);
     }
-    cudaError_t e = brk::launch_prefill(p->head_dim, kv->tm_pre_k, kv->tm_pre_v, a, static_cast<cudaStream_t>(stream));
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (kv->q8()) {
+        // int8 cache: dequantise this layer's rows [0, rows) to fp16 staging (one pass over the
+        // codes, small next to the tensor-core work of a prefill chunk) and attend over it.
+        int rows = 1;
+        for (int b = 0; b < batch; ++b) rows = std::max(rows, past_len[b] + n_tokens - p->kv_offset);
+        const size_t half_elems = (size_t)batch * p->n_kv_heads * rows * p->head_dim;
+        rc = ensure_stage(ctx, 2 * half_elems * sizeof(__half));
+        if (rc) return rc;
+        __half *sk = static_cast<__half *>(ctx->stage), *sv = sk + half_elems;
+        cudaError_t e = brk::launch_kv_dequant(kv->k8, kv->v8, kv->scales, sk, sv, layer, batch, p->n_kv_heads,
+                                               p->head_dim, kv->cap, kv->scale_pitch, rows, st);
+        if (e != cudaSuccess) return cuda_fail(e, "kv dequantise launch");
+        ++ctx->launches;
+        CUtensorMap mk, mv;
+        const uint64_t srows = (uint64_t)batch * p->n_kv_heads * rows;
+        if ((rc = make_cache_map(&mk, sk, srows, p->head_dim, brk::prefill_tile_keys()))) return rc;
+        if ((rc = make_cache_map(&mv, sv, srows, p->head_dim, brk::prefill_tile_keys()))) return rc;
+        a.layer = 0;
+        a.cap = rows;
+        e = brk::launch_prefill(p->head_dim, mk, mv, a, st);
+        if (e != cudaSuccess) return cuda_fail(e, "prefill kernel launch");
+        ++ctx->launches;
+        return BRK_OK;
+    }
+    cudaError_t e = brk::launch_prefill(p->head_dim, kv->tm_pre_k, kv->tm_pre_v, a, st);
     if (e != cudaSuccess) return cuda_fail(e, "prefill kernel launch");
     ++ctx->launches;
     return BRK_OK;

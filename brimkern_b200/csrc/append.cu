@@ -1,4 +1,5 @@
-// KV append with the q/k prologue fused: per-head RMSNorm (QK-norm), NeoX RoPE, fp16 store.
+// KV append with the q/k prologue fused: per-head RMSNorm (QK-norm), NeoX RoPE, fp16 store (or,
+// for an int8 cache, the quantize_kv quantisation of shaders.ts:1673-1705, kernels.ts:1721-1725).
 //
 // Replaces, for one layer, the reference's chain rmsnorm(q), rmsnorm(k) (kernels.ts:1707-1709,
 // shaders.ts:580-598) -> rope / rope_factors (kernels.ts:1710-1718, shaders.ts:1361-1408) ->
@@ -9,9 +10,10 @@
 // kernel does the same in fp64 with explicitly rounded operations (no FMA contraction), the
 // sum of squares in the same sequential order, and cos/sin taken from a table the host built
 // with the same libm expression, so each stored f32 equals the oracle's; K and V are then
-// rounded f32 -> fp16 to nearest even.
+// rounded f32 -> fp16 to nearest even, or quantised to int8 from those same f32 values.
 #include "common.cuh"
 #include "internal.h"
+#include "kv_q8.cuh"
 
 namespace brk {
 
@@ -41,6 +43,8 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32) append_kernel(const __grid
     bool rotate = a.rope != nullptr;
     float *qdst = nullptr;
     __half *cdst = nullptr;
+    uint8_t *c8dst = nullptr;  // int8 cache: codes of this row, and its scale slot
+    float *sdst = nullptr;
     if (kind < a.Hq) {
         if (!a.q_out) return;
         src = a.q_in + ((size_t)bt * a.Hq + kind) * D;
@@ -52,8 +56,14 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32) append_kernel(const __grid
         const float *in = is_k ? a.k_in : a.v_in;
         if (!in) return;
         src = in + ((size_t)bt * a.Hkv + h) * D;
-        const size_t crow = ((size_t)(a.layer * a.B + b) * a.Hkv + h) * a.cap + (size_t)(pos - a.kv_offset);
-        cdst = (is_k ? a.kc : a.vc) + crow * D;
+        const size_t seg = (size_t)(a.layer * a.B + b) * a.Hkv + h;
+        const size_t crow = seg * a.cap + (size_t)(pos - a.kv_offset);
+        if (a.kc) {
+            cdst = (is_k ? a.kc : a.vc) + crow * D;
+        } else {
+            c8dst = (is_k ? a.kc8 : a.vc8) + crow * D;
+            sdst = a.scales + (seg * 2 + (is_k ? 0 : 1)) * a.scale_pitch + (size_t)(pos - a.kv_offset);
+        }
         if (is_k) {
             gain = a.k_norm;
         } else {
@@ -104,18 +114,25 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32) append_kernel(const __grid
             if (qdst) {
                 qdst[i] = o0;
                 qdst[i + half] = o1;
-            } else {
+            } else if (cdst) {
                 cdst[i] = __float2half_rn(o0);
                 cdst[i + half] = __float2half_rn(o1);
+            } else {
+                xs[i] = o0;  // int8: quantised below from the final f32 row
+                xs[i + half] = o1;
             }
         }
-    } else {
+    } else if (!c8dst) {
         for (int d = lane; d < D; d += 32) {
             if (qdst)
                 qdst[d] = xs[d];
             else
                 cdst[d] = __float2half_rn(xs[d]);
         }
+    }
+    if (c8dst) {
+        __syncwarp();
+        quantize_row_warp(xs, D, c8dst, sdst, lane);
     }
 }
 

@@ -100,6 +100,30 @@ __device__ __forceinline__ uint32_t sw128(uint32_t row, uint32_t chunk) {
     return row * 128u + ((chunk ^ (row & 7u)) << 4);
 }
 
+// Same for a [rows][64 B] box written with CU_TENSOR_MAP_SWIZZLE_64B into a 512-byte aligned
+// buffer: chunk (0..3) XOR address bits 7-8, i.e. (row / 2) % 4.
+__device__ __forceinline__ uint32_t sw64(uint32_t row, uint32_t chunk) {
+    return row * 64u + ((chunk ^ ((row >> 1) & 3u)) << 4);
+}
+
+// Byte permute: byte i of the result is byte sel[4i+3:4i] of the 8-byte value {b, a}.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+// Two int8 KV codes stored biased (u = code + 128, one byte each) -> fp16x2 of the signed codes,
+// exactly.  `sel` picks the two bytes of w into bytes 0 and 2 of the fp16 pair (0x4140: bytes
+// 0, 1; 0x4342: bytes 2, 3); bytes 1 and 3 become 0x64, so each half reads 1024 + u (0x64uu is
+// exponent 10 with u in the low mantissa bits), and subtracting 1152 = 1024 + 128 leaves the code.
+__device__ __forceinline__ uint32_t codes_to_half2(uint32_t w, uint32_t sel) {
+    const uint32_t h = prmt(w, 0x64646464u, sel);
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64806480u));
+    return r;
+}
+
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)

@@ -11,17 +11,13 @@
 // QK^T scores through shared memory.  QK^T and PV run on the tensor cores (mma.m16n8k16, fp16 in, fp32 accumulate) with an
 // online softmax per warp (quad shuffles).  The key groups merge their (max, sum, output) in
 // shared memory; with split-KV the last CTA of a (sequence, kv head, row tile) merges the splits.
-#include <math_constants.h>
-
-#include "common.cuh"
-#include "internal.h"
+#include "decode_common.cuh"
 
 namespace brk {
 
 namespace {
 
 constexpr int kKeysPerWarp = 16;
-constexpr float kLn2 = 0.6931471805599453f;
 
 template <int D>
 struct DecodeCfg;
@@ -58,8 +54,7 @@ struct DecodeLayout {
     static_assert(kXBytes <= kQBytes, "score swap must fit in the q staging area");
     static constexpr uint32_t kBarBytes = 2 * DecodeCfg<D>::kStages * 8;
     static constexpr uint32_t kSmemBytes = 1024 + kRingBytes + kQBytes + kBarBytes;
-    static_assert(kKG * 16 * D * 4 + 2 * kKG * 16 * 4 + 16 + 32 * 4 + 16 * 64 * 4 <= kRingBytes,
-                  "merge buffers must fit in the ring");
+    static_assert(decode_epilogue_bytes<D, kKG>() <= kRingBytes, "merge buffers must fit in the ring");
 };
 
 template <int D>
@@ -94,16 +89,9 @@ __global__ void __launch_bounds__(DecodeLayout<D>::kThreads, DecodeCfg<D>::kMinB
     const int row0 = mt * 16;
     const int past = a.past_len[b];
 
-    // Key range of this CTA, in cache rows.  Token t attends [pos_t - W + 1, pos_t] (W <= 0: from 0).
-    const int t_lo = row0 / G;
-    const int t_hi = min(row0 + 15, nrows - 1) / G;
-    int kv_hi = past + t_hi + 1 - a.kv_offset;
-    if (kv_hi > a.cap) kv_hi = a.cap;
-    int kv_lo = 0;
-    if (a.window > 0) kv_lo = max(0, past + t_lo - a.window + 1 - a.kv_offset);
-    const int k_begin = kv_lo + split * a.keys_per_split;
-    const int k_end = min(kv_hi, k_begin + a.keys_per_split);
-    const int ntiles = k_begin < k_end ? (k_end - k_begin + kStageKeys - 1) / kStageKeys : 0;
+    // Key range of this CTA, in cache rows.
+    const KeyRange kr = decode_key_range(a, past, row0, nrows, split, kStageKeys, 1);
+    const int k_begin = kr.k_begin, k_end = kr.k_end, ntiles = kr.ntiles;
     const int seg_row = ((a.layer * a.B + b) * a.Hkv + kvh) * a.cap;
 
     if (threadIdx.x == 0) {
@@ -339,91 +327,7 @@ __global__ void __launch_bounds__(DecodeLayout<D>::kThreads, DecodeCfg<D>::kMinB
     }
     named_barrier_sync(1, NC * 32);
 
-    const int nvalid = min(16, nrows - row0);
-    const int rows_total = a.B * T * a.Hq;
-    // (a) This CTA's (m, l, o) per row.  Single split: the final output (or the caller's
-    // partial); several splits: this split's partial in the workspace.
-    for (int idx = threadIdx.x; idx < nvalid * D; idx += NC * 32) {
-        const int r = idx / D, d = idx % D;
-        float M = -CUDART_INF_F;
-#pragma unroll
-        for (int w = 0; w < KG; ++w) M = fmaxf(M, cm[w * 16 + r]);
-        float Lsum = 0.f, O = 0.f;
-        if (M != -CUDART_INF_F) {
-#pragma unroll
-            for (int w = 0; w < KG; ++w) {
-                const float f = exp2f(cm[w * 16 + r] - M);
-                Lsum += cl[w * 16 + r] * f;
-                O += co[(w * 16 + r) * D + d] * f;
-            }
-        }
-        const int rr = row0 + r;
-        const int t = rr / G, h = kvh * G + rr % G;
-        const size_t R = ((size_t)b * T + t) * a.Hq + h;
-        if (a.nsplit == 1 && a.out) {
-            a.out[R * D + d] = O / Lsum;
-        } else {
-            const size_t PR = (size_t)split * rows_total + R;
-            a.part_o[PR * D + d] = O;
-            if (d == 0) {
-                a.part_ml[PR * 2] = M == -CUDART_INF_F ? -CUDART_INF_F : M * kLn2;
-                a.part_ml[PR * 2 + 1] = Lsum;
-            }
-        }
-    }
-    griddep_launch_dependents();
-    if (a.nsplit == 1) return;
-
-    // (b) Split-KV: the last CTA to finish for this (sequence, kv head, row tile) merges every
-    // split's partial (threadfence-reduction pattern: release fence, counter, acquire fence).
-    __threadfence();
-    named_barrier_sync(1, NC * 32);
-    int *flag = reinterpret_cast<int *>(co + KG * 16 * D);
-    float *row_l = reinterpret_cast<float *>(flag + 4);  // [16]
-    float *row_m = row_l + 16;                            // [16]
-    float *wts = row_m + 16;                              // [16][nsplit]
-    if (threadIdx.x == 0) {
-        const int tile = (b * a.Hkv + kvh) * a.mtiles + mt;
-        const int prev = atomicAdd(&a.counters[tile], 1);
-        flag[0] = prev == a.nsplit - 1;
-        if (prev == a.nsplit - 1) a.counters[tile] = 0;  // every arrival is in: ready for the next launch
-    }
-    named_barrier_sync(1, NC * 32);
-    if (!flag[0]) return;
-    __threadfence();
-    for (int r = threadIdx.x; r < nvalid; r += NC * 32) {
-        const int rr = row0 + r;
-        const size_t R = ((size_t)b * T + rr / G) * a.Hq + kvh * G + rr % G;
-        float M = -CUDART_INF_F;
-        for (int sp = 0; sp < a.nsplit; ++sp) M = fmaxf(M, __ldcg(&a.part_ml[((size_t)sp * rows_total + R) * 2]));
-        float Lsum = 0.f;
-        for (int sp = 0; sp < a.nsplit; ++sp) {
-            const float m = __ldcg(&a.part_ml[((size_t)sp * rows_total + R) * 2]);
-            const float w = m == -CUDART_INF_F ? 0.f : expf(m - M);
-            wts[r * a.nsplit + sp] = w;
-            Lsum += w * __ldcg(&a.part_ml[((size_t)sp * rows_total + R) * 2 + 1]);
-        }
-        row_l[r] = Lsum;
-        row_m[r] = M;
-    }
-    named_barrier_sync(1, NC * 32);
-    for (int idx = threadIdx.x; idx < nvalid * D; idx += NC * 32) {
-        const int r = idx / D, d = idx % D;
-        const int rr = row0 + r;
-        const size_t R = ((size_t)b * T + rr / G) * a.Hq + kvh * G + rr % G;
-        float O = 0.f;
-        for (int sp = 0; sp < a.nsplit; ++sp)
-            O += wts[r * a.nsplit + sp] * __ldcg(&a.part_o[((size_t)sp * rows_total + R) * D + d]);
-        if (a.out) {
-            a.out[R * D + d] = O / row_l[r];
-        } else {
-            a.res_o[R * D + d] = O;
-            if (d == 0) {
-                a.res_ml[R * 2] = row_m[r];
-                a.res_ml[R * 2 + 1] = row_l[r];
-            }
-        }
-    }
+    decode_epilogue<D, KG, NC>(a, ring, row0, nrows, kvh, mt, b, split);
 }
 
 // Log-sum-exp merge of partials (brk_attn_combine: partials gathered from several GPUs): one
@@ -512,7 +416,8 @@ int decode_stage_keys(int head_dim) {
     }
 }
 
-int decode_ctas_per_sm(int head_dim) {
+int decode_ctas_per_sm(int head_dim, bool q8) {
+    if (q8) return decode_q8_ctas_per_sm(head_dim);
     switch (head_dim) {
         case 64: return ctas_per_sm_t<64>();
         case 128: return ctas_per_sm_t<128>();

@@ -1,0 +1,143 @@
+// Pieces shared by the two decode kernels (fp16 cache: decode.cu, int8 cache: decode_q8.cu):
+// the key range of a CTA and the epilogue that merges the key groups and, with split-KV, the
+// splits (the last CTA of a (sequence, kv head, row tile) merges every split's partial).
+#pragma once
+
+#include <math_constants.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace brk {
+
+constexpr float kLn2 = 0.6931471805599453f;
+
+// Cache rows [k_begin, k_end) that one CTA attends, in stage-sized tiles.  Token t of the CTA's
+// rows attends [pos_t - W + 1, pos_t] (W <= 0: from 0).  `align` rounds the window's first key
+// down (the int8 kernel loads scales in 16-byte boxes); keys below a row's own limit are masked.
+struct KeyRange {
+    int k_begin, k_end, ntiles;
+};
+
+__device__ __forceinline__ KeyRange decode_key_range(const DecodeArgs &a, int past, int row0, int nrows, int split,
+                                                     int stage_keys, int align) {
+    const int G = a.G;
+    const int t_lo = row0 / G;
+    const int t_hi = min(row0 + 15, nrows - 1) / G;
+    int kv_hi = past + t_hi + 1 - a.kv_offset;
+    if (kv_hi > a.cap) kv_hi = a.cap;
+    int kv_lo = 0;
+    if (a.window > 0) kv_lo = max(0, past + t_lo - a.window + 1 - a.kv_offset) / align * align;
+    KeyRange r;
+    r.k_begin = kv_lo + split * a.keys_per_split;
+    r.k_end = min(kv_hi, r.k_begin + a.keys_per_split);
+    r.ntiles = r.k_begin < r.k_end ? (r.k_end - r.k_begin + stage_keys - 1) / stage_keys : 0;
+    return r;
+}
+
+// After every consumer warp has written its key group's running max (log2 units), sum and
+// unnormalised output rows into cm [KG][16], cl [KG][16] and co [KG][16][D] at the start of
+// `ring`: writes this CTA's rows (final output, or its split's partial), then, with split-KV,
+// lets the last CTA of the tile merge all splits.  Called by the NC consumer warps only.
+template <int D, int KG, int NC>
+__device__ __forceinline__ void decode_epilogue(const DecodeArgs &a, uint8_t *ring, int row0, int nrows, int kvh,
+                                                int mt, int b, int split) {
+    const float *cm = reinterpret_cast<const float *>(ring);
+    const float *cl = cm + KG * 16;
+    const float *co = cl + KG * 16;
+    const int G = a.G, T = a.T;
+    const int nvalid = min(16, nrows - row0);
+    const int rows_total = a.B * T * a.Hq;
+    // (a) This CTA's (m, l, o) per row.  Single split: the final output (or the caller's
+    // partial); several splits: this split's partial in the workspace.
+    for (int idx = threadIdx.x; idx < nvalid * D; idx += NC * 32) {
+        const int r = idx / D, d = idx % D;
+        float M = -CUDART_INF_F;
+#pragma unroll
+        for (int w = 0; w < KG; ++w) M = fmaxf(M, cm[w * 16 + r]);
+        float Lsum = 0.f, O = 0.f;
+        if (M != -CUDART_INF_F) {
+#pragma unroll
+            for (int w = 0; w < KG; ++w) {
+                const float f = exp2f(cm[w * 16 + r] - M);
+                Lsum += cl[w * 16 + r] * f;
+                O += co[(w * 16 + r) * D + d] * f;
+            }
+        }
+        const int rr = row0 + r;
+        const int t = rr / G, h = kvh * G + rr % G;
+        const size_t R = ((size_t)b * T + t) * a.Hq + h;
+        if (a.nsplit == 1 && a.out) {
+            a.out[R * D + d] = O / Lsum;
+        } else {
+            const size_t PR = (size_t)split * rows_total + R;
+            a.part_o[PR * D + d] = O;
+            if (d == 0) {
+                a.part_ml[PR * 2] = M == -CUDART_INF_F ? -CUDART_INF_F : M * kLn2;
+                a.part_ml[PR * 2 + 1] = Lsum;
+            }
+        }
+    }
+    griddep_launch_dependents();
+    if (a.nsplit == 1) return;
+
+    // (b) Split-KV: the last CTA to finish for this (sequence, kv head, row tile) merges every
+    // split's partial (threadfence-reduction pattern: release fence, counter, acquire fence).
+    __threadfence();
+    named_barrier_sync(1, NC * 32);
+    int *flag = reinterpret_cast<int *>(const_cast<float *>(co) + KG * 16 * D);
+    float *row_l = reinterpret_cast<float *>(flag + 4);  // [16]
+    float *row_m = row_l + 16;                            // [16]
+    float *wts = row_m + 16;                              // [16][nsplit]
+    if (threadIdx.x == 0) {
+        const int tile = (b * a.Hkv + kvh) * a.mtiles + mt;
+        const int prev = atomicAdd(&a.counters[tile], 1);
+        flag[0] = prev == a.nsplit - 1;
+        if (prev == a.nsplit - 1) a.counters[tile] = 0;  // every arrival is in: ready for the next launch
+    }
+    named_barrier_sync(1, NC * 32);
+    if (!flag[0]) return;
+    __threadfence();
+    for (int r = threadIdx.x; r < nvalid; r += NC * 32) {
+        const int rr = row0 + r;
+        const size_t R = ((size_t)b * T + rr / G) * a.Hq + kvh * G + rr % G;
+        float M = -CUDART_INF_F;
+        for (int sp = 0; sp < a.nsplit; ++sp) M = fmaxf(M, __ldcg(&a.part_ml[((size_t)sp * rows_total + R) * 2]));
+        float Lsum = 0.f;
+        for (int sp = 0; sp < a.nsplit; ++sp) {
+            const float m = __ldcg(&a.part_ml[((size_t)sp * rows_total + R) * 2]);
+            const float w = m == -CUDART_INF_F ? 0.f : expf(m - M);
+            wts[r * a.nsplit + sp] = w;
+            Lsum += w * __ldcg(&a.part_ml[((size_t)sp * rows_total + R) * 2 + 1]);
+        }
+        row_l[r] = Lsum;
+        row_m[r] = M;
+    }
+    named_barrier_sync(1, NC * 32);
+    for (int idx = threadIdx.x; idx < nvalid * D; idx += NC * 32) {
+        const int r = idx / D, d = idx % D;
+        const int rr = row0 + r;
+        const size_t R = ((size_t)b * T + rr / G) * a.Hq + kvh * G + rr % G;
+        float O = 0.f;
+        for (int sp = 0; sp < a.nsplit; ++sp)
+            O += wts[r * a.nsplit + sp] * __ldcg(&a.part_o[((size_t)sp * rows_total + R) * D + d]);
+        if (a.out) {
+            a.out[R * D + d] = O / row_l[r];
+        } else {
+            a.res_o[R * D + d] = O;
+            if (d == 0) {
+                a.res_ml[R * 2] = row_m[r];
+                a.res_ml[R * 2 + 1] = row_l[r];
+            }
+        }
+    }
+}
+
+// Bytes of `ring` the epilogue needs: cm, cl, co, the flag word and the split-merge rows
+// (up to 64 splits).
+template <int D, int KG>
+constexpr uint32_t decode_epilogue_bytes() {
+    return KG * 16 * D * 4 + 2 * KG * 16 * 4 + 16 + 32 * 4 + 16 * 64 * 4;
+}
+
+}  // namespace brk

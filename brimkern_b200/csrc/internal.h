@@ -17,6 +17,8 @@ struct brk_ctx {
     int *d_err = nullptr;      // device error word written by bounded waits (brk::DeviceError)
     void *ws = nullptr;        // split-KV workspace
     size_t ws_bytes = 0;
+    void *stage = nullptr;     // fp16 staging of an int8 cache layer for the prefill kernel
+    size_t stage_bytes = 0;
     uint64_t launches = 0;     // kernels launched through this context
 };
 
@@ -31,10 +33,20 @@ struct brk_kv {
     brk_ctx *ctx = nullptr;
     brk_kv_desc desc{};
     int cap = 0;
-    __half *k = nullptr;       // [layer][seq][kv head][cap][D]
+    // BRK_KV_F16: fp16 rows [layer][seq][kv head][cap][D].
+    __half *k = nullptr;
     __half *v = nullptr;
-    CUtensorMap tm_dec_k{}, tm_dec_v{};  // boxes for the decode kernel
-    CUtensorMap tm_pre_k{}, tm_pre_v{};  // boxes for the prefill kernel
+    // BRK_KV_I8: codes biased by +128 as bytes, [layer][seq][kv head][cap][D], and f32 scales
+    // [layer][seq][kv head][2 (K, V)][scale_pitch] (scale_pitch = cap rounded up to 4, so that a
+    // TMA box of scales may start at any 4-aligned key).
+    uint8_t *k8 = nullptr;
+    uint8_t *v8 = nullptr;
+    float *scales = nullptr;
+    int scale_pitch = 0;
+    CUtensorMap tm_dec_k{}, tm_dec_v{};  // boxes for the decode kernel (fp16 rows or int8 codes)
+    CUtensorMap tm_dec_s{};              // int8 mode: [2][keys] scale boxes for the decode kernel
+    CUtensorMap tm_pre_k{}, tm_pre_v{};  // fp16 mode: boxes for the prefill kernel
+    bool q8() const { return desc.dtype == BRK_KV_I8; }
 };
 
 namespace brk {
@@ -42,7 +54,10 @@ namespace brk {
 struct AppendArgs {
     const float *q_in, *k_in, *v_in;
     float *q_out;
-    __half *kc, *vc;
+    __half *kc, *vc;          // fp16 cache, or nullptr in int8 mode
+    uint8_t *kc8, *vc8;       // int8 cache: biased codes, and
+    float *scales;            //   [seg][2][scale_pitch] scales
+    int scale_pitch;
     const double2 *rope;
     int rope_max;
     const float *q_norm, *k_norm;
@@ -93,7 +108,7 @@ struct CombineArgs {
     int n_parts, rows, D;
 };
 
-// Keys per pipeline stage of the decode kernel for a head dim.
+// Keys per pipeline stage of the decode kernel for a head dim (the same for both cache types).
 int decode_stage_keys(int head_dim);
 int prefill_tile_keys();
 
@@ -102,17 +117,37 @@ cudaError_t launch_append(const AppendArgs &a, cudaStream_t s, bool pdl);
 // pdl: launch as a programmatic dependent of the preceding kernel (the append of brk_attn_step).
 cudaError_t launch_decode(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const DecodeArgs &a,
                           int grid_x, int grid_y, int grid_z, cudaStream_t s, bool pdl);
+// Decode over the int8 cache: codes maps as for fp16 (int8 boxes), plus the scale map.
+cudaError_t launch_decode_q8(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const CUtensorMap &tms,
+                             const DecodeArgs &a, int grid_x, int grid_y, int grid_z, cudaStream_t s, bool pdl);
 cudaError_t launch_combine(const CombineArgs &a, cudaStream_t s);
 // Tensor-core prefill (head_dim 64 or 128); maps with prefill_tile_keys()-row boxes.
 cudaError_t launch_prefill(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const PrefillArgs &a,
                            cudaStream_t s);
 // Concurrent CTAs per SM of the decode kernel for a head dim (occupancy query).
-int decode_ctas_per_sm(int head_dim);
+int decode_ctas_per_sm(int head_dim, bool q8);
+int decode_q8_ctas_per_sm(int head_dim);
 
 // kc/vc point at row row0 of kv head 0 of one (layer, sequence) segment; heads are cap rows apart.
 cudaError_t launch_kv_write_rows(__half *kc, __half *vc, const float *k, const float *v, int n_rows, int n_kv_heads,
                                  int head_dim, int cap, cudaStream_t s);
 cudaError_t launch_kv_read_rows(const __half *kc, const __half *vc, uint16_t *k, uint16_t *v, int n_rows,
                                 int n_kv_heads, int head_dim, int cap, cudaStream_t s);
+
+// int8 mode.  kc/vc: codes at row row0 of kv head 0 of one (layer, sequence) segment; sc: that
+// segment's scales ([kv head][2][pitch]) offset by row0.  write_q8 quantises f32 rows
+// (quantize_kv); store_codes writes given codes and scales; read returns codes and scales in the
+// reference's token-major layout.
+cudaError_t launch_kv_write_q8(uint8_t *kc, uint8_t *vc, float *sc, const float *k, const float *v, int n_rows,
+                               int n_kv_heads, int head_dim, int cap, int pitch, cudaStream_t s);
+cudaError_t launch_kv_store_codes(uint8_t *kc, uint8_t *vc, float *sc, const int8_t *k, const float *ks,
+                                  const int8_t *v, const float *vs, int n_rows, int n_kv_heads, int head_dim, int cap,
+                                  int pitch, cudaStream_t s);
+cudaError_t launch_kv_read_q8(const uint8_t *kc, const uint8_t *vc, const float *sc, int8_t *k, float *ks, int8_t *v,
+                              float *vs, int n_rows, int n_kv_heads, int head_dim, int cap, int pitch, cudaStream_t s);
+// Dequantise rows [0, rows) of every (sequence, kv head) of one layer into fp16 staging
+// [B][Hkv][rows][D] (K and V), for the tensor-core prefill kernel.
+cudaError_t launch_kv_dequant(const uint8_t *kc, const uint8_t *vc, const float *sc, __half *k, __half *v, int layer,
+                              int B, int n_kv_heads, int head_dim, int cap, int pitch, int rows, cudaStream_t s);
 
 }  // namespace brk

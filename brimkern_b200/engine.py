@@ -5,7 +5,8 @@ The reference host is TypeScript; no JavaScript runtime exists in this image, so
 is written in Python with the reference's method names and argument meanings:
 
 * readback twins used by selfValidate -- ``attention`` (kernels.ts:610), ``attentionDecode``
-  (:624), ``rope`` (:556), ``ropeFactors`` (:568), ``rmsnorm`` (:428): numpy in, numpy out;
+  (:624), ``quantizeKvReadback`` (:664), ``attentionQ8Kv`` (:681), ``attentionQ8KvDecode``
+  (:694), ``rope`` (:556), ``ropeFactors`` (:568), ``rmsnorm`` (:428): numpy in, numpy out;
 * the resident path -- ``ensureKv`` / ``setKvQuant`` / ``clearKvCache`` (:1760-1806), the
   session check of ``runDecodeGpu`` (:1817-1825), ``recAttention`` (:1626) and the attention
   slice of ``recordLayerKV`` (:1707-1731): device tensors in, device tensors out.
@@ -121,13 +122,16 @@ def llama3_rope_factors(head_dim: int, base: float, factor: float, low_freq_fact
 
 
 class KvCache:
-    """Persistent fp16 KV cache of ``n_layers`` layers x ``batch`` sequences (KvEntry,
-    kernels.ts:93), head-major in HBM."""
+    """Persistent KV cache of ``n_layers`` layers x ``batch`` sequences (KvEntry, kernels.ts:93),
+    head-major in HBM: fp16, or int8 codes + per-(row, kv head) scales (``q8=True``, the
+    reference's setKvQuant mode)."""
 
-    def __init__(self, ctx: Context, n_layers: int, batch: int, n_kv_heads: int, head_dim: int, capacity: int):
+    def __init__(self, ctx: Context, n_layers: int, batch: int, n_kv_heads: int, head_dim: int, capacity: int,
+                 q8: bool = False):
         self.ctx = ctx
         self.n_layers, self.batch, self.n_kv_heads, self.head_dim = n_layers, batch, n_kv_heads, head_dim
-        desc = L.KvDesc(n_layers, batch, n_kv_heads, head_dim, int(capacity), L.BRK_KV_F16)
+        self.q8 = bool(q8)
+        desc = L.KvDesc(n_layers, batch, n_kv_heads, head_dim, int(capacity), L.BRK_KV_I8 if q8 else L.BRK_KV_F16)
         h = ctypes.c_void_p()
         check(L.lib().brk_kv_create(ctx.handle, ctypes.byref(desc), ctypes.byref(h)))
         self.handle = h
@@ -144,9 +148,29 @@ class KvCache:
         check(L.lib().brk_kv_reset(self.handle, _stream_ptr(stream)))
 
     def write_rows(self, layer: int, seq: int, row0: int, k: torch.Tensor, v: torch.Tensor, stream=None) -> None:
+        """f32 rows [n, n_kv_heads, D] stored as fp16, or quantised (quantize_kv) in an int8 cache."""
         n = k.shape[0]
         check(L.lib().brk_kv_write_rows(self.handle, layer, seq, row0, n, _ptr(k.contiguous()), _ptr(v.contiguous()),
                                         _stream_ptr(stream)))
+
+    def write_codes(self, layer: int, seq: int, row0: int, k_codes: torch.Tensor, k_scales: torch.Tensor,
+                    v_codes: torch.Tensor, v_scales: torch.Tensor, stream=None) -> None:
+        """int8 cache: given codes [n, n_kv_heads, D] int8 and scales [n, n_kv_heads] f32."""
+        n = k_codes.shape[0]
+        check(L.lib().brk_kv_write_codes(self.handle, layer, seq, row0, n, _ptr(k_codes.contiguous()),
+                                         _ptr(k_scales.contiguous()), _ptr(v_codes.contiguous()),
+                                         _ptr(v_scales.contiguous()), _stream_ptr(stream)))
+
+    def read_codes(self, layer: int, seq: int, row0: int, n_rows: int, stream=None):
+        """int8 cache: (k_codes, k_scales, v_codes, v_scales) in the reference's layout."""
+        dev = torch.device("cuda", self.ctx.device)
+        kc = torch.empty((n_rows, self.n_kv_heads, self.head_dim), dtype=torch.int8, device=dev)
+        vc = torch.empty_like(kc)
+        ks = torch.empty((n_rows, self.n_kv_heads), dtype=torch.float32, device=dev)
+        vs = torch.empty_like(ks)
+        check(L.lib().brk_kv_read_codes(self.handle, layer, seq, row0, n_rows, _ptr(kc), _ptr(ks), _ptr(vc), _ptr(vs),
+                                        _stream_ptr(stream)))
+        return kc, ks, vc, vs
 
     def read_rows(self, layer: int, seq: int, row0: int, n_rows: int, stream=None):
         """Rows in the reference's token-major layout [n_rows, n_kv_heads, D] as float16 tensors."""
@@ -215,9 +239,7 @@ class AttentionEngine:
     def _attention_readback(self, q, k, v, nTokens, nHeads, nKvHeads, headDim, pastLen, scale, softcap, kernel,
                             window=0):
         kvLen = pastLen + nTokens
-        D = next((d for d in _SUPPORTED_DIMS if d >= headDim), None)
-        if D is None:
-            raise BrkError(L.BRK_ERR_UNSUPPORTED, f"head_dim {headDim} > 256")
+        D = self._padded_dim(headDim)
         sc = float(scale) if scale is not None else 1.0 / math.sqrt(headDim)
 
         def pad(a, rows, heads):
@@ -249,6 +271,64 @@ class AttentionEngine:
         return self._attention_readback(q, k, v, nTokens, nHeads, nKvHeads, headDim, pastLen, scale, softcap,
                                         "decode")
 
+    def quantizeKvReadback(self, src, rows, nKvHeads, headDim):
+        """kernels.ts:664 — quantize_kv of src [rows, nKvHeads, headDim] f32 -> (codes int8
+        [rows*nKvHeads*headDim] (the bytes of the reference's packed Uint32Array), scales f32
+        [rows*nKvHeads])."""
+        D = self._padded_dim(headDim)
+        x = np.zeros((rows, nKvHeads, D), np.float32)
+        x[..., :headDim] = np.asarray(src, np.float32).reshape(rows, nKvHeads, headDim)  # zeros leave amax as is
+        xd = self._dev(x)
+        kv = KvCache(self.ctx, 1, 1, nKvHeads, D, rows, q8=True)
+        kv.write_rows(0, 0, 0, xd, xd)
+        kc, ks, _, _ = kv.read_codes(0, 0, 0, rows)
+        self.ctx.check()
+        kv.close()
+        return kc[..., :headDim].cpu().numpy().ravel(), ks.cpu().numpy().ravel()
+
+    def _attention_q8_readback(self, q, kc, ks, vc, vs, nTokens, nHeads, nKvHeads, headDim, pastLen, scale, softcap,
+                               kernel):
+        kvLen = pastLen + nTokens
+        D = self._padded_dim(headDim)
+        sc = float(scale) if scale is not None else 1.0 / math.sqrt(headDim)
+
+        def codes(c):
+            c = np.ascontiguousarray(c).view(np.int8).reshape(kvLen, nKvHeads, headDim)
+            out = np.zeros((kvLen, nKvHeads, D), np.int8)
+            out[..., :headDim] = c
+            return torch.from_numpy(out).to(self.device)
+
+        qp = np.zeros((nTokens, nHeads, D), np.float32)
+        qp[..., :headDim] = np.asarray(q, np.float32).reshape(nTokens, nHeads, headDim)
+        kv = KvCache(self.ctx, 1, 1, nKvHeads, D, kvLen, q8=True)
+        kv.write_codes(0, 0, 0, codes(kc), self._dev(np.asarray(ks, np.float32).reshape(kvLen, nKvHeads)),
+                       codes(vc), self._dev(np.asarray(vs, np.float32).reshape(kvLen, nKvHeads)))
+        cfg = AttnConfig(nHeads, nKvHeads, D, scale=sc, softcap=softcap)
+        out = torch.empty((nTokens, nHeads, D), dtype=torch.float32, device=self.device)
+        self.recAttention(kv, 0, cfg, self._dev(qp), out, pastLen, kernel=kernel)
+        self.ctx.check()
+        kv.close()
+        return out[..., :headDim].cpu().numpy().ravel()
+
+    def attentionQ8Kv(self, q, kc, ks, vc, vs, nTokens, nHeads, nKvHeads, headDim, pastLen=0, scale=None, softcap=0.0):
+        """kernels.ts:681 — attention over an int8 cache given as codes (int8, or the packed
+        Uint32 words) and per-(row, head) f32 scales."""
+        return self._attention_q8_readback(q, kc, ks, vc, vs, nTokens, nHeads, nKvHeads, headDim, pastLen, scale,
+                                           softcap, "auto")
+
+    def attentionQ8KvDecode(self, q, kc, ks, vc, vs, nTokens, nHeads, nKvHeads, headDim, pastLen=0, scale=None,
+                            softcap=0.0):
+        """kernels.ts:694 — the same through the decode kernel."""
+        return self._attention_q8_readback(q, kc, ks, vc, vs, nTokens, nHeads, nKvHeads, headDim, pastLen, scale,
+                                           softcap, "decode")
+
+    @staticmethod
+    def _padded_dim(headDim: int) -> int:
+        D = next((d for d in _SUPPORTED_DIMS if d >= headDim), None)
+        if D is None:
+            raise BrkError(L.BRK_ERR_UNSUPPORTED, f"head_dim {headDim} > 256")
+        return D
+
     def _q_prologue(self, x, rows, headDim, nHeads, pastLen, rope, gain, eps, onePlus):
         if rows % nHeads:
             raise BrkError(L.BRK_ERR_INVALID, "rows must be a multiple of nHeads")
@@ -278,8 +358,8 @@ class AttentionEngine:
 
     # ---- KV manager (kernels.ts:1749-1806) ----------------------------------------------
     def setKvQuant(self, q8: bool) -> None:
-        if q8:
-            raise BrkError(L.BRK_ERR_UNSUPPORTED, "int8 KV cache is not built in this version (fp16 only)")
+        """kernels.ts:1760 — switch the cache between fp16 and int8 (resets it: layouts differ)."""
+        q8 = bool(q8)
         if self.kvQuant != q8:
             self.kvQuant = q8
             self.resetKvGpu()
@@ -296,12 +376,12 @@ class AttentionEngine:
     def ensureKv(self, n_layers: int, rows: int, batch: int, n_kv_heads: int, head_dim: int) -> KvCache:
         """Cache holding >= rows rows for every layer; grows to max(rows, cap + 1024, 1024)."""
         kv = self.kvGpu
-        if kv is not None and (kv.n_layers, kv.batch, kv.n_kv_heads, kv.head_dim) != (n_layers, batch, n_kv_heads,
-                                                                                      head_dim):
+        if kv is not None and (kv.n_layers, kv.batch, kv.n_kv_heads, kv.head_dim, kv.q8) != (
+                n_layers, batch, n_kv_heads, head_dim, self.kvQuant):
             self.resetKvGpu()
             kv = None
         if kv is None:
-            kv = KvCache(self.ctx, n_layers, batch, n_kv_heads, head_dim, max(rows, 1024))
+            kv = KvCache(self.ctx, n_layers, batch, n_kv_heads, head_dim, max(rows, 1024), q8=self.kvQuant)
             self.kvGpu = kv
         elif kv.capacity < rows:
             kv.grow(rows)

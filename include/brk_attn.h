@@ -42,7 +42,10 @@ enum {
     BRK_ERR_DEVICE = -5       /* a kernel reported a bounded-wait timeout (brk_ctx_check) */
 };
 
-enum { BRK_KV_F16 = 0 };
+/* KV cache element types.  BRK_KV_I8 is the reference's int8 mode (setKvQuant(true),
+ * kernels.ts:1755-1760): symmetric int8 codes with one f32 scale per (row, kv head) for K and for
+ * V (quantize_kv, shaders.ts:1673-1705), half the bytes of fp16. */
+enum { BRK_KV_F16 = 0, BRK_KV_I8 = 1 };
 
 typedef struct brk_ctx brk_ctx;   /* one per GPU: device id, error flag, workspace */
 typedef struct brk_kv brk_kv;     /* persistent KV cache of n_layers layers (KvEntry, kernels.ts:93) */
@@ -54,7 +57,7 @@ typedef struct {
     int n_kv_heads;
     int head_dim;   /* 64, 128 or 256 */
     int capacity;   /* rows per (layer, sequence, kv head); brk_kv_grow enlarges it */
-    int dtype;      /* BRK_KV_F16 */
+    int dtype;      /* BRK_KV_F16 or BRK_KV_I8 */
 } brk_kv_desc;
 
 /* Per-layer attention configuration: LayerCfg's attention fields (kernels.ts:24-56). */
@@ -103,7 +106,10 @@ int brk_llama3_rope_factors(int head_dim, double base, double factor, double low
                             double high_freq_factor, int original_context, float *ff_out);
 
 /* ---- KV cache (ensureKv / resetKvGpu / clearKvCache, kernels.ts:1766-1806) ------------------
- * Stored head-major, [layer][sequence][kv head][capacity][head_dim] fp16, zero-initialised. */
+ * Stored head-major, [layer][sequence][kv head][capacity][head_dim], zero-initialised: fp16, or
+ * for BRK_KV_I8 one byte per code plus per-(row, kv head) K and V scales.  Every attention entry
+ * point below works on both types; the int8 prefill dequantises the layer to fp16 staging held by
+ * the context (so two streams must not run int8 prefill on one context at the same time). */
 int brk_kv_create(brk_ctx *ctx, const brk_kv_desc *desc, brk_kv **out);
 int brk_kv_destroy(brk_kv *kv);
 int brk_kv_capacity(const brk_kv *kv);
@@ -112,19 +118,30 @@ int brk_kv_capacity(const brk_kv *kv);
 int brk_kv_grow(brk_kv *kv, int rows, void *stream);
 /* clearKvCache (kernels.ts:1777): zero every row. */
 int brk_kv_reset(brk_kv *kv, void *stream);
-/* Plain row store, f32 -> fp16 (round to nearest even), no norm or rotation: the f32 copy of
- * kernels.ts:1729-1730 for callers that already hold final K/V.  k, v: [n_rows][n_kv_heads][D]. */
+/* Plain row store, no norm or rotation: the f32 copy of kernels.ts:1729-1730 for callers that
+ * already hold final K/V, f32 -> fp16 (round to nearest even); for an int8 cache the quantize_kv
+ * pass of recQuantizeKv (kernels.ts:1644-1648).  k, v: [n_rows][n_kv_heads][D] f32 (either may
+ * be NULL). */
 int brk_kv_write_rows(brk_kv *kv, int layer, int seq, int row0, int n_rows, const float *k,
                       const float *v, void *stream);
 /* Test hook: copy rows back in the reference's token-major layout as fp16 bit patterns.
- * k_out, v_out: device [n_rows][n_kv_heads][D] uint16. */
+ * k_out, v_out: device [n_rows][n_kv_heads][D] uint16.  fp16 caches only. */
 int brk_kv_read_rows(const brk_kv *kv, int layer, int seq, int row0, int n_rows,
                      uint16_t *k_out, uint16_t *v_out, void *stream);
+/* int8 caches: store given codes and scales (the inputs of the attentionQ8Kv readback twin,
+ * kernels.ts:681), and read them back (quantizeKvReadback, kernels.ts:664), in the reference's
+ * layout: codes [n_rows][n_kv_heads][D] int8, scales [n_rows][n_kv_heads] f32 (K and V pairs may
+ * each be NULL). */
+int brk_kv_write_codes(brk_kv *kv, int layer, int seq, int row0, int n_rows, const int8_t *k_codes,
+                       const float *k_scales, const int8_t *v_codes, const float *v_scales, void *stream);
+int brk_kv_read_codes(const brk_kv *kv, int layer, int seq, int row0, int n_rows, int8_t *k_codes,
+                      float *k_scales, int8_t *v_codes, float *v_scales, void *stream);
 
 /* ---- hot path ----------------------------------------------------------------------------- */
 /* KV append with the q/k prologue fused (kernels.ts:1707-1730): per-head RMSNorm of q and k
  * (if gains are given), NeoX RoPE (if a table is given) at position past_len[b]+t, K and V
- * stored as fp16 at cache row past_len[b]+t-kv_offset; the rotated q is written to q_out f32
+ * stored at cache row past_len[b]+t-kv_offset (fp16, or quantised as quantize_kv does for an
+ * int8 cache, kernels.ts:1721-1725); the rotated q is written to q_out f32
  * [B][T][Hq][D] for the attention call.  With kv == NULL only q is processed (the rope / rmsnorm
  * readback twins, any even head_dim up to 1024).  past_len: HOST [batch]. */
 int brk_attn_append(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, int batch,

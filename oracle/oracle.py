@@ -139,6 +139,15 @@ def quantize_kv(src, rows, n_kv_heads, head_dim, row_offset=0, cap_rows=None):
     return codes, scales
 
 
+def dequantize_kv(codes, scales, rows, n_kv_heads, head_dim):
+    """The dequant closure of the reference's q8 gate (kernels.ts:2577-2588): f32(code * scale)
+    per element, scale per (row, head) -- one rounding of the exact product, as numpy's f32
+    multiply gives."""
+    c = np.asarray(codes, np.int8).reshape(rows, n_kv_heads, head_dim).astype(np.float32)
+    s = np.asarray(scales, np.float32).reshape(rows, n_kv_heads, 1)
+    return (c * s).astype(np.float32).ravel()
+
+
 def attention_batch(q, k, v, batch, seq_stride, n_tokens, n_heads, n_kv_heads, head_dim, past_len,
                     scale=None, softcap=0.0, window=0, threads=0):
     """Multi-core batched attentionCpu (OpenMP over (seq, head)).  Returns (out, threads_used)."""
