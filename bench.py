@@ -618,7 +618,7 @@ def main():
     traffic = read_traffic(workload + ("-q8" if q8 else ""))
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                "kernel": "decode_q8_kernel" if q8 else "decode_attn_kernel",
+                "kernel": "decode_kernel<int8>" if q8 else "decode_kernel<fp16>",
                 "timing": f"CUDA events around each decode launch, {rsteps} steps",
                 "bytes_per_launch": bytes_launch,
                 "avg_launch_ms": round(attn_avg_ms, 5), "frac_of_8TBs": round(achieved / 8000.0, 4)}

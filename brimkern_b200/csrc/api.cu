@@ -87,7 +87,7 @@ int make_cache_map(CUtensorMap *m, const __half *base, uint64_t rows, int head_d
 }
 
 // int8 code rows [rows][head_dim] bytes, box = [box_rows][min(head_dim, 128) B]: 128-byte swizzle,
-// or the 64-byte one for head_dim 64 (the addressing of decode_q8.cu).
+// or the 64-byte one for head_dim 64 (the addressing of the decode kernel, decode.cu).
 int make_code_map(CUtensorMap *m, const uint8_t *base, uint64_t rows, int head_dim, int box_rows) {
     const bool narrow = head_dim < 128;
     return make_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, rows, (uint64_t)head_dim, narrow ? 64u : 128u,
@@ -252,7 +252,8 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
     a.G = G;
     a.layer = layer;
     a.cap = kv->cap;
-    a.mtiles = (n_tokens * G + 15) / 16;
+    const int rt = brk::decode_rows_per_tile();
+    a.mtiles = (n_tokens * G + rt - 1) / rt;
     a.kv_offset = p->kv_offset;
     a.window = p->window > 0 ? p->window : 0;
     a.scale = effective_scale(p);
@@ -316,10 +317,8 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
         a.res_ml = part_ml;
         a.res_o = part_o;
     }
-    cudaError_t e = kv->q8() ? brk::launch_decode_q8(D, kv->tm_dec_k, kv->tm_dec_v, kv->tm_dec_s, a, nsplit,
-                                                     p->n_kv_heads * a.mtiles, batch, stream, pdl)
-                             : brk::launch_decode(D, kv->tm_dec_k, kv->tm_dec_v, a, nsplit, p->n_kv_heads * a.mtiles,
-                                                  batch, stream, pdl);
+    cudaError_t e = brk::launch_decode(kv->q8(), D, kv->tm_dec_k, kv->tm_dec_v, kv->q8() ? kv->tm_dec_s : kv->tm_dec_k,
+                                       a, nsplit, p->n_kv_heads * a.mtiles, batch, stream, pdl);
     if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
     ++ctx->launches;
     return BRK_OK;

@@ -1,98 +1,128 @@
-// Decode attention over the resident fp16 KV cache (replaces attention_decode,
-// shaders.ts:1768-1851, and its dispatch in recAttention, kernels.ts:1626-1641).
+// Decode attention over the resident KV cache, fp16 or int8 (replaces attention_decode and
+// attention_decode_q8kv, shaders.ts:1768-1851 and 1856-1944, and their dispatch in recAttention /
+// recAttentionQ8, kernels.ts:1626-1661).
 //
-// One CTA per (sequence, kv head, row tile, split).  The rows of a CTA are up to 16 (token,
-// q head) pairs of one kv head's query group, so every K/V byte read from HBM serves the whole
-// group (the reference re-reads K/V once per q head).  A producer warp streams the CTA's key
-// range through a ring of shared-memory stages with 2-D TMA loads (128-byte swizzled
-// [keys][64 x fp16] boxes, CTA-local).  Consumer warps come in key groups (four, or two for
-// head_dim 256), each taking 16 keys of every stage; with the head-dim split DS = 2 (head_dim
-// 256) each key group is a warp pair that owns one half of the head dimension and swaps partial
-// QK^T scores through shared memory.  QK^T and PV run on the tensor cores (mma.m16n8k16, fp16 in, fp32 accumulate) with an
-// online softmax per warp (quad shuffles).  The key groups merge their (max, sum, output) in
-// shared memory; with split-KV the last CTA of a (sequence, kv head, row tile) merges the splits.
+// One CTA per (sequence, kv head, tile of 8 query rows, split).  The query rows of a tile are
+// (token, q head) pairs of one kv head's group, so every K/V byte read from HBM serves the whole
+// group.  A producer warp streams the CTA's key range through a shared-memory ring with 2-D TMA
+// loads (CTA-local): fp16 rows as [keys][64 x fp16] boxes, int8 codes as [keys][<=128 B] boxes
+// plus a [2][keys] box of f32 K / V scales.  Consumer warps come in key groups of 16 keys per
+// stage (and, for head_dim 256, pairs that split the head dim and swap partial scores).
+//
+// Keys sit on the M dimension of the tensor-core tiles (mma.m16n8k16, fp16 in, fp32 accumulate)
+// and the 8 query rows on N, so a decode step with a small GQA group wastes at most half of each
+// tile instead of three quarters:
+//   S^T [16 keys x 8 rows] = K [16 x D] Q^T [D x 8]
+//   O^T [D x 8 rows]      += V^T [D x 16 keys] P^T [16 keys x 8 rows]
+// P^T comes from the S^T accumulator fragment with one movmatrix transpose per 8 keys.
+//
+// int8 cache: each code is stored biased by +128 in one byte, so it becomes an exact fp16 value
+// with one byte permute and one fp16x2 subtraction (codes_to_half2).  The K scale is constant over
+// the head dim and factors out of the dot product (shaders.ts:1721-1726): s = scale_k[j] *
+// sum_d q_d code_d; the V scale multiplies the probabilities, p'_j = p_j * scale_v[j], while the
+// row sum keeps p_j.  Lanes read codes as 16-byte words; the head dim is permuted identically in q
+// and K (k-step ks of lane quad qc covers head-dim bytes W qc + 4 ks + 0..3), and a lane's V
+// fragment takes VW bytes at head-dim VW r of four keys, transposed 4 x 4 bytes at a time with
+// byte permutes (output head-dim rows are permuted accordingly and restored at the merge).
 #include "decode_common.cuh"
 
 namespace brk {
 
 namespace {
 
-constexpr int kKeysPerWarp = 16;
+constexpr int kRT = 8;  // query rows per CTA tile (the MMA N dimension)
 
-template <int D>
+template <bool Q8, int D>
 struct DecodeCfg;
 template <>
-struct DecodeCfg<64> {
+struct DecodeCfg<false, 64> {
     static constexpr int kStages = 6, kMinBlocks = 2, kDSplit = 1, kKeyGroups = 4;
 };
 template <>
-struct DecodeCfg<128> {
+struct DecodeCfg<false, 128> {
     static constexpr int kStages = 3, kMinBlocks = 2, kDSplit = 1, kKeyGroups = 4;
 };
-// head_dim 256: two key groups (32-key stages) x two head-dim halves, so that two CTAs fit per SM.
 template <>
-struct DecodeCfg<256> {
+struct DecodeCfg<false, 256> {
     static constexpr int kStages = 3, kMinBlocks = 2, kDSplit = 2, kKeyGroups = 2;
 };
-
-template <int D>
-struct DecodeLayout {
-    static constexpr int kDS = DecodeCfg<D>::kDSplit;
-    static constexpr int kKG = DecodeCfg<D>::kKeyGroups;
-    static constexpr int kStageKeys = kKeysPerWarp * kKG;           // keys per ring stage
-    static constexpr int kConsumers = kKG * kDS;                    // consumer warps
-    static constexpr int kThreads = (kConsumers + 1) * 32;          // + one producer warp
-    static constexpr int kBlocks = D / 64;                          // 128-byte column blocks per row
-    static constexpr uint32_t kBoxBytes = kStageKeys * 128;         // one [keys][64] fp16 box
-    static constexpr uint32_t kTileBytes = kBlocks * kBoxBytes;     // K (or V) of one stage
-    static constexpr uint32_t kStageBytes = 2 * kTileBytes;
-    static constexpr uint32_t kRingBytes = DecodeCfg<D>::kStages * kStageBytes;
-    static constexpr uint32_t kQBytes = kBlocks * 16 * 128;         // 16 rows of q, fp16, swizzled
-    // Score swap of the head-dim halves, [key group][parity][half][lane][8] floats; it reuses
-    // the q staging area once every warp holds its q fragments.
-    static constexpr uint32_t kXBytes = kDS > 1 ? kKG * 2 * 2 * 32 * 8 * 4 : 0;
-    static_assert(kXBytes <= kQBytes, "score swap must fit in the q staging area");
-    static constexpr uint32_t kBarBytes = 2 * DecodeCfg<D>::kStages * 8;
-    static constexpr uint32_t kSmemBytes = 1024 + kRingBytes + kQBytes + kBarBytes;
-    static_assert(decode_epilogue_bytes<D, kKG>() <= kRingBytes, "merge buffers must fit in the ring");
+template <>
+struct DecodeCfg<true, 64> {
+    static constexpr int kStages = 6, kMinBlocks = 3, kDSplit = 1, kKeyGroups = 4;
+};
+template <>
+struct DecodeCfg<true, 128> {
+    static constexpr int kStages = 4, kMinBlocks = 3, kDSplit = 1, kKeyGroups = 4;
+};
+template <>
+struct DecodeCfg<true, 256> {
+    static constexpr int kStages = 4, kMinBlocks = 3, kDSplit = 2, kKeyGroups = 2;
 };
 
-template <int D>
-__global__ void __launch_bounds__(DecodeLayout<D>::kThreads, DecodeCfg<D>::kMinBlocks)
-    decode_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                       const __grid_constant__ DecodeArgs a) {
-    using L = DecodeLayout<D>;
-    constexpr int S = DecodeCfg<D>::kStages;
+template <bool Q8, int D>
+struct DecodeLayout {
+    using C = DecodeCfg<Q8, D>;
+    static constexpr int kDS = C::kDSplit;
+    static constexpr int kKG = C::kKeyGroups;
+    static constexpr int kStageKeys = 16 * kKG;
+    static constexpr int kConsumers = kKG * kDS;
+    static constexpr int kThreads = (kConsumers + 1) * 32;
+    static constexpr int kRowBytes = Q8 ? D : 2 * D;                   // one key row of the cache
+    static constexpr int kBoxCols = Q8 ? (D < 128 ? D : 128) : 128;     // bytes of one box row
+    static constexpr int kBoxElems = Q8 ? kBoxCols : kBoxCols / 2;      // elements of one box row
+    static constexpr int kBoxes = kRowBytes / kBoxCols;
+    static constexpr uint32_t kBoxBytes = kStageKeys * kBoxCols;
+    static constexpr uint32_t kTileBytes = kStageKeys * kRowBytes;      // K (or V) of one stage
+    static constexpr uint32_t kScaleBytes = Q8 ? 2 * kStageKeys * 4 : 0;
+    static constexpr uint32_t kLoadBytes = 2 * kTileBytes + kScaleBytes;
+    static constexpr uint32_t kStageBytes = (kLoadBytes + 1023) / 1024 * 1024;
+    static constexpr uint32_t kRingBytes = C::kStages * kStageBytes;
+    // Score swap of the head-dim halves: [key group][parity][half][lane][4] floats.
+    static constexpr uint32_t kXBytes = kDS > 1 ? kKG * 2 * 2 * 32 * 4 * 4 : 0;
+    static constexpr uint32_t kBarBytes = 2 * C::kStages * 8;
+    static constexpr uint32_t kSmemBytes = 1024 + kRingBytes + kXBytes + kBarBytes;
+    static_assert(decode_epilogue_bytes<D, kKG, kRT>() <= kRingBytes, "merge buffers must fit in the ring");
+};
+
+template <bool Q8, int D>
+__global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D>::kMinBlocks)
+    decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                   const __grid_constant__ CUtensorMap tms, const __grid_constant__ DecodeArgs a) {
+    using L = DecodeLayout<Q8, D>;
+    constexpr int S = DecodeCfg<Q8, D>::kStages;
     constexpr int DS = L::kDS;
     constexpr int NC = L::kConsumers;
     constexpr int KG = L::kKG;
-    constexpr int kStageKeys = L::kStageKeys;
-    constexpr int DH = D / DS;     // head-dim slice of one warp
-    constexpr int KS = DH / 16;    // k-steps of QK^T per warp
-    constexpr int NTO = DH / 8;    // output n-tiles per warp
-    static_assert(DH <= 128, "per-warp head-dim slice");
+    constexpr int SK = L::kStageKeys;
+    constexpr int DH = D / DS;  // head-dim slice of one warp: 64 or 128
+    constexpr int KS = DH / 16; // k-steps of S^T = K Q^T
+    constexpr int MT = DH / 16; // m-tiles (16 head-dim rows) of O^T
+    constexpr int W = DH / 4;   // int8: K bytes of a key row per lane-quad member
+    constexpr int VW = DH / 8;  // int8: V bytes of a key row per lane
+    constexpr int NG = VW / 4;  // int8: V words of a key row per lane
+    static_assert(DH == 64 || DH == 128, "per-warp head-dim slice");
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *ring = smem;
-    uint8_t *qs = ring + L::kRingBytes;
-    float *xbuf = reinterpret_cast<float *>(qs);  // score swap, after the q fragments are loaded
-    uint64_t *full = reinterpret_cast<uint64_t *>(qs + L::kQBytes);
+    float *xbuf = reinterpret_cast<float *>(ring + L::kRingBytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(ring + L::kRingBytes + L::kXBytes);
     uint64_t *empty = full + S;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int split = blockIdx.x;
-    const int kvh = blockIdx.y / a.mtiles, mt = blockIdx.y % a.mtiles;
+    const int kvh = blockIdx.y / a.mtiles, mtile = blockIdx.y % a.mtiles;
     const int b = blockIdx.z;
     const int G = a.G, T = a.T;
     const int nrows = T * G;
-    const int row0 = mt * 16;
+    const int row0 = mtile * kRT;
     const int past = a.past_len[b];
 
-    // Key range of this CTA, in cache rows.
-    const KeyRange kr = decode_key_range(a, past, row0, nrows, split, kStageKeys, 1);
+    // Key range; for int8 a window's first key is rounded down to a multiple of 4 (16-byte scale
+    // boxes) -- the extra keys are below every row's window and masked.
+    const KeyRange kr = decode_key_range(a, past, row0, nrows, split, SK, Q8 ? 4 : 1, kRT);
     const int k_begin = kr.k_begin, k_end = kr.k_end, ntiles = kr.ntiles;
-    const int seg_row = ((a.layer * a.B + b) * a.Hkv + kvh) * a.cap;
+    const int seg = (a.layer * a.B + b) * a.Hkv + kvh;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -101,33 +131,36 @@ __global__ void __launch_bounds__(DecodeLayout<D>::kThreads, DecodeCfg<D>::kMinB
         }
         fence_barrier_init();
     }
-    __syncthreads();  // barrier initialisation visible to every warp
+    __syncthreads();
 
     if (warp == NC) {
-        // ---- producer: one elected lane streams K/V tiles through the ring.
+        // ---- producer: one elected lane streams the stages through the ring.
         if (lane == 0 && ntiles > 0) {
             tma_prefetch_desc(&tmk);
             tma_prefetch_desc(&tmv);
+            if constexpr (Q8) tma_prefetch_desc(&tms);
             int issued = 0;
             bool waited = false;
             // Rows from dep_row on may be written by a preceding kernel (the append, when this
-            // launch is its programmatic dependent): tiles touching them wait for it to finish.
+            // launch is its programmatic dependent): stages touching them wait for it to finish.
             const int dep_row = past - a.kv_offset;
             for (int i = 0; i < ntiles; ++i) {
                 const int s = i % S;
-                if (!waited && k_begin + (i + 1) * kStageKeys > dep_row) {
+                const int key = k_begin + i * SK;
+                if (!waited && key + SK > dep_row) {
                     griddep_wait();
                     waited = true;
                 }
                 if (i >= S && !mbar_wait(&empty[s], ((i / S) - 1) & 1, a.err, kErrSlotTimeout)) break;
-                mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+                mbar_arrive_expect_tx(&full[s], L::kLoadBytes);
                 uint8_t *st = ring + s * L::kStageBytes;
-                const int y = seg_row + k_begin + i * kStageKeys;
+                const int y = seg * a.cap + key;
 #pragma unroll
-                for (int j = 0; j < L::kBlocks; ++j) tma_load_2d(st + j * L::kBoxBytes, &tmk, j * 64, y, &full[s]);
+                for (int j = 0; j < L::kBoxes; ++j) tma_load_2d(st + j * L::kBoxBytes, &tmk, j * L::kBoxElems, y, &full[s]);
 #pragma unroll
-                for (int j = 0; j < L::kBlocks; ++j)
-                    tma_load_2d(st + L::kTileBytes + j * L::kBoxBytes, &tmv, j * 64, y, &full[s]);
+                for (int j = 0; j < L::kBoxes; ++j)
+                    tma_load_2d(st + L::kTileBytes + j * L::kBoxBytes, &tmv, j * L::kBoxElems, y, &full[s]);
+                if constexpr (Q8) tma_load_2d(st + 2 * L::kTileBytes, &tms, key, seg * 2, &full[s]);
                 issued = i + 1;
             }
             // Before leaving, make sure every copy this lane started has landed (bounded).
@@ -137,166 +170,227 @@ __global__ void __launch_bounds__(DecodeLayout<D>::kThreads, DecodeCfg<D>::kMinB
         return;
     }
 
-    // ---- consumers: stage this CTA's 16 q rows as fp16, in the same swizzled layout as the K
-    // boxes (q comes from the preceding append when launched as its dependent).
-    griddep_wait();
-    for (int idx = threadIdx.x; idx < 16 * (D / 8); idx += NC * 32) {
-        const int r = idx / (D / 8), ch = idx % (D / 8);
-        const int rr = row0 + r;
-        float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
-        if (rr < nrows) {
-            const int t = rr / G, h = kvh * G + rr % G;
-            const float *src = a.q + (((size_t)b * T + t) * a.Hq + h) * D + ch * 8;
-            x0 = *reinterpret_cast<const float4 *>(src);
-            x1 = *reinterpret_cast<const float4 *>(src + 4);
-        }
-        uint4 pk;
-        pk.x = pack_half2(x0.x, x0.y);
-        pk.y = pack_half2(x0.z, x0.w);
-        pk.z = pack_half2(x1.x, x1.y);
-        pk.w = pack_half2(x1.z, x1.w);
-        *reinterpret_cast<uint4 *>(qs + (ch >> 3) * 2048 + sw128(r, ch & 7)) = pk;
-    }
-    named_barrier_sync(1, NC * 32);
-
+    griddep_wait();  // q comes from the preceding append when launched as its dependent
     const int kg = warp % KG;  // key group: keys [16 kg, 16 kg + 16) of every stage
     const int dh = warp / KG;  // head-dim slice [DH dh, DH dh + DH)
     const int qr = lane >> 2, qc = lane & 3;
-    uint32_t qf[KS][4];
-#pragma unroll
-    for (int k = 0; k < KS; ++k) {
-        const int ks = dh * KS + k;  // global k-step over D
-        ldsm_x4(smem_addr(qs + (ks >> 2) * 2048 + sw128(lane & 15, (ks & 3) * 2 + (lane >> 4))), qf[k][0], qf[k][1],
-                qf[k][2], qf[k][3]);
-    }
-    if constexpr (DS > 1) named_barrier_sync(1, NC * 32);  // q staging area becomes the score swap
 
-    // Causal / window limits of this lane's two rows (rows rA and rA + 8 of the tile).
-    const int rA = row0 + qr, rB = rA + 8;
-    const int hiA = rA < nrows ? past + rA / G - a.kv_offset : -1;
-    const int hiB = rB < nrows ? past + rB / G - a.kv_offset : -1;
-    const int loA = a.window > 0 ? past + rA / G - a.window + 1 - a.kv_offset : INT_MIN;
-    const int loB = a.window > 0 ? past + rB / G - a.window + 1 - a.kv_offset : INT_MIN;
+    // Q^T fragments (B operand, column qr = query row row0 + qr), fp32 -> fp16 from global memory.
+    uint32_t qf[KS][2];
+    {
+        const int rq = row0 + qr;
+        const float *qrow =
+            rq < nrows ? a.q + (((size_t)b * T + rq / G) * a.Hq + kvh * G + rq % G) * D + dh * DH : nullptr;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            if constexpr (Q8) {
+                const float4 x = qrow ? *reinterpret_cast<const float4 *>(qrow + W * qc + 4 * ks)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+                qf[ks][0] = pack_half2(x.x, x.y);
+                qf[ks][1] = pack_half2(x.z, x.w);
+            } else {
+                const float2 x0 = qrow ? *reinterpret_cast<const float2 *>(qrow + ks * 16 + 2 * qc) : make_float2(0.f, 0.f);
+                const float2 x1 =
+                    qrow ? *reinterpret_cast<const float2 *>(qrow + ks * 16 + 8 + 2 * qc) : make_float2(0.f, 0.f);
+                qf[ks][0] = pack_half2(x0.x, x0.y);
+                qf[ks][1] = pack_half2(x1.x, x1.y);
+            }
+        }
+    }
+
+    // This lane's scores are keys (qr, qr + 8) x rows (2qc, 2qc + 1): causal / window limits.
+    int hi[2], lo[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int r = row0 + 2 * qc + j;
+        hi[j] = r < nrows ? past + r / G - a.kv_offset : -1;
+        lo[j] = a.window > 0 ? past + r / G - a.window + 1 - a.kv_offset : INT_MIN;
+    }
     const bool use_cap = a.softcap > 0.f;
 
-    float o[NTO][4];
+    float o[MT][4];
 #pragma unroll
-    for (int n = 0; n < NTO; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-    float m2[2] = {-CUDART_INF_F, -CUDART_INF_F};  // running max, log2 units
-    float lsum[2] = {0.f, 0.f};                    // this lane's share of the running sum
+    for (int m = 0; m < MT; ++m) o[m][0] = o[m][1] = o[m][2] = o[m][3] = 0.f;
+    float m2[2] = {-CUDART_INF_F, -CUDART_INF_F};  // running max per row, log2 units
+    float lsum[2] = {0.f, 0.f};                    // this lane's share of the running sums
 
     for (int i = 0; i < ntiles; ++i) {
         const int s = i % S;
         if (!mbar_wait(&full[s], (i / S) & 1, a.err, kErrTmaTimeout)) break;
         uint8_t *kt = ring + s * L::kStageBytes;
         uint8_t *vt = kt + L::kTileBytes;
-        const int key0 = k_begin + i * kStageKeys + kg * kKeysPerWarp;
+        const int key0 = k_begin + i * SK + kg * 16;
 
-        // S = Q K^T over this warp's head-dim slice for its 16 keys (two n-tiles of 8 keys).
-        float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-        const int krow = kg * kKeysPerWarp + ((lane >> 4) << 3) + (lane & 7);
+        // ---- S^T = K Q^T for the warp's 16 keys over its head-dim slice.
+        float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+        if constexpr (Q8) {
+            const uint8_t *kb = kt + dh * L::kBoxBytes;
+            const int rA = kg * 16 + qr, rB = rA + 8;
+            uint32_t wa[KS], wb[KS];
+            if constexpr (DH == 128) {
+                const uint4 a0 = *reinterpret_cast<const uint4 *>(kb + sw128(rA, 2 * qc));
+                const uint4 a1 = *reinterpret_cast<const uint4 *>(kb + sw128(rA, 2 * qc + 1));
+                const uint4 b0 = *reinterpret_cast<const uint4 *>(kb + sw128(rB, 2 * qc));
+                const uint4 b1 = *reinterpret_cast<const uint4 *>(kb + sw128(rB, 2 * qc + 1));
+                wa[0] = a0.x, wa[1] = a0.y, wa[2] = a0.z, wa[3] = a0.w, wa[4] = a1.x, wa[5] = a1.y, wa[6] = a1.z;
+                wa[7] = a1.w;
+                wb[0] = b0.x, wb[1] = b0.y, wb[2] = b0.z, wb[3] = b0.w, wb[4] = b1.x, wb[5] = b1.y, wb[6] = b1.z;
+                wb[7] = b1.w;
+            } else {
+                const uint4 a0 = *reinterpret_cast<const uint4 *>(kb + sw64(rA, qc));
+                const uint4 b0 = *reinterpret_cast<const uint4 *>(kb + sw64(rB, qc));
+                wa[0] = a0.x, wa[1] = a0.y, wa[2] = a0.z, wa[3] = a0.w;
+                wb[0] = b0.x, wb[1] = b0.y, wb[2] = b0.z, wb[3] = b0.w;
+            }
 #pragma unroll
-        for (int k = 0; k < KS; ++k) {
-            const int ks = dh * KS + k;
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4(smem_addr(kt + (ks >> 2) * L::kBoxBytes + sw128(krow, (ks & 3) * 2 + ((lane >> 3) & 1))), b0, b1,
-                    b2, b3);
-            mma_16816(sacc[0], qf[k][0], qf[k][1], qf[k][2], qf[k][3], b0, b1);
-            mma_16816(sacc[1], qf[k][0], qf[k][1], qf[k][2], qf[k][3], b2, b3);
+            for (int ks = 0; ks < KS; ++ks)
+                mma_16816(sacc, codes_to_half2(wa[ks], 0x4140u), codes_to_half2(wb[ks], 0x4140u),
+                          codes_to_half2(wa[ks], 0x4342u), codes_to_half2(wb[ks], 0x4342u), qf[ks][0], qf[ks][1]);
+        } else {
+            const int krow = kg * 16 + (lane & 15);
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                const int chunk = dh * (DH / 8) + ks * 2 + (lane >> 4);
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4(smem_addr(kt + (chunk >> 3) * L::kBoxBytes + sw128(krow, chunk & 7)), a0, a1, a2, a3);
+                mma_16816(sacc, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+            }
         }
         if constexpr (DS > 1) {
-            // Swap partial scores with the warp that holds the other half of the head dim
-            // (double-buffered by tile parity, so one pair barrier per tile suffices).
-            float *mine = xbuf + (((kg * 2 + (i & 1)) * 2 + dh) * 32 + lane) * 8;
-            float *theirs = xbuf + (((kg * 2 + (i & 1)) * 2 + (dh ^ 1)) * 32 + lane) * 8;
-            *reinterpret_cast<float4 *>(mine) = make_float4(sacc[0][0], sacc[0][1], sacc[0][2], sacc[0][3]);
-            *reinterpret_cast<float4 *>(mine + 4) = make_float4(sacc[1][0], sacc[1][1], sacc[1][2], sacc[1][3]);
+            // Swap partial scores with the warp holding the other head-dim half (double-buffered by
+            // tile parity: one pair barrier per tile); add in a fixed order so both agree.
+            float *mine = xbuf + (((kg * 2 + (i & 1)) * 2 + dh) * 32 + lane) * 4;
+            const float *theirs = xbuf + (((kg * 2 + (i & 1)) * 2 + (dh ^ 1)) * 32 + lane) * 4;
+            *reinterpret_cast<float4 *>(mine) = make_float4(sacc[0], sacc[1], sacc[2], sacc[3]);
             named_barrier_sync(2 + kg, 64);
-            const float4 t0 = *reinterpret_cast<const float4 *>(theirs);
-            const float4 t1 = *reinterpret_cast<const float4 *>(theirs + 4);
-            // Add in a fixed order (slice 0 + slice 1) so both warps hold identical scores.
-            const float4 lo0 = dh == 0 ? make_float4(sacc[0][0], sacc[0][1], sacc[0][2], sacc[0][3]) : t0;
-            const float4 lo1 = dh == 0 ? make_float4(sacc[1][0], sacc[1][1], sacc[1][2], sacc[1][3]) : t1;
-            const float4 hi0 = dh == 0 ? t0 : make_float4(sacc[0][0], sacc[0][1], sacc[0][2], sacc[0][3]);
-            const float4 hi1 = dh == 0 ? t1 : make_float4(sacc[1][0], sacc[1][1], sacc[1][2], sacc[1][3]);
-            sacc[0][0] = lo0.x + hi0.x, sacc[0][1] = lo0.y + hi0.y, sacc[0][2] = lo0.z + hi0.z;
-            sacc[0][3] = lo0.w + hi0.w;
-            sacc[1][0] = lo1.x + hi1.x, sacc[1][1] = lo1.y + hi1.y, sacc[1][2] = lo1.z + hi1.z;
-            sacc[1][3] = lo1.w + hi1.w;
+            const float4 t = *reinterpret_cast<const float4 *>(theirs);
+            if (dh == 0) {
+                sacc[0] += t.x, sacc[1] += t.y, sacc[2] += t.z, sacc[3] += t.w;
+            } else {
+                sacc[0] = t.x + sacc[0], sacc[1] = t.y + sacc[1], sacc[2] = t.z + sacc[2], sacc[3] = t.w + sacc[3];
+            }
         }
 
-        // Scores -> masked, scaled (log2 units), online softmax per row.
+        // ---- masked, scaled scores (log2 units) and the online softmax per row.
+        float ksc[2] = {1.f, 1.f}, vsc[2] = {1.f, 1.f};
+        if constexpr (Q8) {
+            const float *sc = reinterpret_cast<const float *>(kt + 2 * L::kTileBytes);
+            ksc[0] = sc[kg * 16 + qr];
+            ksc[1] = sc[kg * 16 + qr + 8];
+            vsc[0] = sc[SK + kg * 16 + qr];
+            vsc[1] = sc[SK + kg * 16 + qr + 8];
+        }
         float mx[2] = {-CUDART_INF_F, -CUDART_INF_F};
+        bool valid[4];
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int key = key0 + nt * 8 + 2 * qc + (e & 1);
-                const int hi = e < 2 ? hiA : hiB, lo = e < 2 ? loA : loB;
-                float x = sacc[nt][e];
-                if (use_cap) {
-                    // c*tanh(s/c) (shaders.ts:1490) in log2 units, with tanh(z) = 1 - 2/(1 + e^{2z}):
-                    // one exp2 and one reciprocal; saturates to +-1 for large |z|.
-                    const float e2z = exp2f(x * a.cap_k1);
-                    x = a.cap_k2 * (1.f - 2.f * __frcp_rn(1.f + e2z));
-                } else {
-                    x = x * a.scale_log2;
-                }
-                x = (key >= lo && key <= hi && key < k_end) ? x : -CUDART_INF_F;
-                sacc[nt][e] = x;
-                mx[e >> 1] = fmaxf(mx[e >> 1], x);
+        for (int e = 0; e < 4; ++e) {
+            const int key = key0 + qr + (e >> 1) * 8;
+            const int j = e & 1;  // row 2qc + j
+            float x = sacc[e];
+            if constexpr (Q8) x *= ksc[e >> 1];
+            if (use_cap) {
+                // c*tanh(s/c) (shaders.ts:1490) in log2 units, tanh(z) = 1 - 2/(1 + e^{2z}): one
+                // exp2 and one reciprocal, saturating to +-1 for large |z|.
+                const float e2z = exp2f(x * a.cap_k1);
+                x = a.cap_k2 * (1.f - 2.f * __frcp_rn(1.f + e2z));
+            } else {
+                x *= a.scale_log2;
             }
+            valid[e] = key >= lo[j] && key <= hi[j] && key < k_end;
+            x = valid[e] ? x : -CUDART_INF_F;
+            sacc[e] = x;
+            mx[j] = fmaxf(mx[j], x);
+        }
         float muse[2];
+        bool grew = false;
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-            const float mnew = fmaxf(m2[r], mx[r]);
-            muse[r] = mnew == -CUDART_INF_F ? 0.f : mnew;
-            const float alpha = exp2f(m2[r] - muse[r]);
-            m2[r] = mnew;
-            lsum[r] *= alpha;
+        for (int j = 0; j < 2; ++j) {
+            mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], 4));
+            mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], 8));
+            mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], 16));
+            const float mnew = fmaxf(m2[j], mx[j]);
+            grew |= mnew > m2[j];
+            muse[j] = mnew == -CUDART_INF_F ? 0.f : mnew;
+        }
+        // Rescale the running sums and outputs only when some row's maximum grew.
+        if (__any_sync(0xffffffffu, grew)) {
+            float alpha[2];
 #pragma unroll
-            for (int n = 0; n < NTO; ++n) {
-                o[n][2 * r] *= alpha;
-                o[n][2 * r + 1] *= alpha;
+            for (int j = 0; j < 2; ++j) {
+                alpha[j] = exp2f(m2[j] - muse[j]);
+                lsum[j] *= alpha[j];
+            }
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                o[m][0] *= alpha[0];
+                o[m][1] *= alpha[1];
+                o[m][2] *= alpha[0];
+                o[m][3] *= alpha[1];
             }
         }
-        float p[2][4];
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
+        for (int j = 0; j < 2; ++j) m2[j] = fmaxf(m2[j], mx[j]);
+        float p[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                p[nt][e] = exp2f(sacc[nt][e] - muse[e >> 1]);
-                lsum[e >> 1] += p[nt][e];
-            }
-        const uint32_t pa0 = pack_half2(p[0][0], p[0][1]);
-        const uint32_t pa1 = pack_half2(p[0][2], p[0][3]);
-        const uint32_t pa2 = pack_half2(p[1][0], p[1][1]);
-        const uint32_t pa3 = pack_half2(p[1][2], p[1][3]);
-
-        // Keys past the range end get zero V (in this warp's head-dim slice), so that
-        // 0 * (whatever the tile read there) stays 0.
-        const bool tail = key0 + kKeysPerWarp > k_end;
-        if (tail) {
-            const int first = max(k_end - key0, 0);
-            for (int idx = lane; idx < (kKeysPerWarp - first) * (DH / 8); idx += 32) {
-                const int rl = first + idx / (DH / 8), ch = dh * (DH / 8) + idx % (DH / 8);
-                *reinterpret_cast<uint4 *>(vt + (ch >> 3) * L::kBoxBytes + sw128(kg * kKeysPerWarp + rl, ch & 7)) =
-                    make_uint4(0u, 0u, 0u, 0u);
-            }
-            __syncwarp();
+        for (int e = 0; e < 4; ++e) {
+            p[e] = exp2f(sacc[e] - muse[e & 1]);
+            lsum[e & 1] += p[e];
+            if constexpr (Q8) p[e] = valid[e] ? p[e] * vsc[e >> 1] : 0.f;
         }
+        // P^T fragments -> P fragments (B operand of O^T += V^T P^T): keys 0-7 and 8-15.
+        const uint32_t pb0 = movmatrix_t(pack_half2(p[0], p[1]));
+        const uint32_t pb1 = movmatrix_t(pack_half2(p[2], p[3]));
 
-        // O += P V over this warp's head-dim slice (16 keys), V fragments through ldmatrix.trans.
-        const int vrow = kg * kKeysPerWarp + (((lane >> 3) & 1) << 3) + (lane & 7);
+        // ---- O^T += V^T P^T over the warp's head-dim slice.
+        bool tail = false;
+        if constexpr (Q8) {
+            const uint8_t *vb = vt + dh * L::kBoxBytes;
+            const int vr = kg * 16 + 2 * qc;
+            uint32_t vw[4][NG];
 #pragma unroll
-        for (int np = 0; np < NTO / 2; ++np) {
-            const int chunk = dh * (DH / 8) + np * 2 + (lane >> 4);
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4_t(smem_addr(vt + (chunk >> 3) * L::kBoxBytes + sw128(vrow, chunk & 7)), b0, b1, b2, b3);
-            mma_16816(o[2 * np], pa0, pa1, pa2, pa3, b0, b1);
-            mma_16816(o[2 * np + 1], pa0, pa1, pa2, pa3, b2, b3);
+            for (int k = 0; k < 4; ++k) {
+                const int r = vr + (k & 1) + (k >> 1) * 8;  // keys 2qc, 2qc+1, 2qc+8, 2qc+9
+                if constexpr (DH == 128) {
+                    const uint4 w = *reinterpret_cast<const uint4 *>(vb + sw128(r, qr));
+                    vw[k][0] = w.x, vw[k][1] = w.y, vw[k][2] = w.z, vw[k][3] = w.w;
+                } else {
+                    const uint2 w = *reinterpret_cast<const uint2 *>(vb + sw64(r, qr >> 1) + (qr & 1) * 8);
+                    vw[k][0] = w.x, vw[k][1] = w.y;
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < NG; ++g) {
+                // Pairs (key 2qc, key 2qc+1) / (2qc+8, 2qc+9) of head-dim bytes 4g+t: t = 0, 1 in
+                // lo, t = 2, 3 in hi.  m-tile 2g+u takes bytes 4g+2u (its row qr) and 4g+2u+1 (row qr+8).
+                const uint32_t lo01 = prmt(vw[0][g], vw[1][g], 0x5140u), hi01 = prmt(vw[0][g], vw[1][g], 0x7362u);
+                const uint32_t lo23 = prmt(vw[2][g], vw[3][g], 0x5140u), hi23 = prmt(vw[2][g], vw[3][g], 0x7362u);
+                mma_16816(o[2 * g], codes_to_half2(lo01, 0x4140u), codes_to_half2(lo01, 0x4342u),
+                          codes_to_half2(lo23, 0x4140u), codes_to_half2(lo23, 0x4342u), pb0, pb1);
+                mma_16816(o[2 * g + 1], codes_to_half2(hi01, 0x4140u), codes_to_half2(hi01, 0x4342u),
+                          codes_to_half2(hi23, 0x4140u), codes_to_half2(hi23, 0x4342u), pb0, pb1);
+            }
+        } else {
+            // Keys past the range end get zero V (in this warp's slice), so that 0 * (whatever
+            // the tile holds there) stays 0.
+            tail = key0 + 16 > k_end;
+            if (tail) {
+                const int first = max(k_end - key0, 0);
+                for (int idx = lane; idx < (16 - first) * (DH / 8); idx += 32) {
+                    const int rl = first + idx / (DH / 8), ch = dh * (DH / 8) + idx % (DH / 8);
+                    *reinterpret_cast<uint4 *>(vt + (ch >> 3) * L::kBoxBytes + sw128(kg * 16 + rl, ch & 7)) =
+                        make_uint4(0u, 0u, 0u, 0u);
+                }
+                __syncwarp();
+            }
+            const int j8 = lane >> 3;
+            const int vrow = kg * 16 + (j8 >> 1) * 8 + (lane & 7);
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                const int chunk = dh * (DH / 8) + m * 2 + (j8 & 1);
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4_t(smem_addr(vt + (chunk >> 3) * L::kBoxBytes + sw128(vrow, chunk & 7)), a0, a1, a2, a3);
+                mma_16816(o[m], a0, a1, a2, a3, pb0, pb1);
+            }
         }
         if (tail) fence_proxy_async_smem();  // generic writes before the next TMA into this slot
         __syncwarp();
@@ -305,29 +399,41 @@ __global__ void __launch_bounds__(DecodeLayout<D>::kThreads, DecodeCfg<D>::kMinB
 
     // ---- merge the key groups' (m, l, O) in shared memory (the ring is free now).
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-        lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], 1);
-        lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], 2);
+    for (int j = 0; j < 2; ++j) {
+        lsum[j] += __shfl_xor_sync(0xffffffffu, lsum[j], 4);
+        lsum[j] += __shfl_xor_sync(0xffffffffu, lsum[j], 8);
+        lsum[j] += __shfl_xor_sync(0xffffffffu, lsum[j], 16);
     }
     named_barrier_sync(1, NC * 32);
-    float *cm = reinterpret_cast<float *>(ring);  // [key group][16]
-    float *cl = cm + KG * 16;                     // [key group][16]
-    float *co = cl + KG * 16;                     // [key group][16][D]
-    if (qc == 0 && dh == 0) {
-        cm[kg * 16 + qr] = m2[0];
-        cm[kg * 16 + qr + 8] = m2[1];
-        cl[kg * 16 + qr] = lsum[0];
-        cl[kg * 16 + qr + 8] = lsum[1];
+    float *cm = reinterpret_cast<float *>(ring);  // [key group][kRT]
+    float *cl = cm + KG * kRT;                    // [key group][kRT]
+    float *co = cl + KG * kRT;                    // [key group][kRT][D]
+    if (qr == 0 && dh == 0) {
+        cm[kg * kRT + 2 * qc] = m2[0];
+        cm[kg * kRT + 2 * qc + 1] = m2[1];
+        cl[kg * kRT + 2 * qc] = lsum[0];
+        cl[kg * kRT + 2 * qc + 1] = lsum[1];
     }
+    float *c0 = co + (kg * kRT + 2 * qc) * D;  // row 2qc; row 2qc + 1 is D further
 #pragma unroll
-    for (int n = 0; n < NTO; ++n) {
-        const int d = dh * DH + n * 8 + 2 * qc;
-        *reinterpret_cast<float2 *>(co + (kg * 16 + qr) * D + d) = make_float2(o[n][0], o[n][1]);
-        *reinterpret_cast<float2 *>(co + (kg * 16 + qr + 8) * D + d) = make_float2(o[n][2], o[n][3]);
+    for (int m = 0; m < MT; ++m) {
+        // Head-dim rows of m-tile m held by this lane: dA (fragment row qr), dB (row qr + 8).
+        int dA, dB;
+        if constexpr (Q8) {
+            dA = dh * DH + VW * qr + 4 * (m >> 1) + 2 * (m & 1);
+            dB = dA + 1;
+        } else {
+            dA = dh * DH + m * 16 + qr;
+            dB = dA + 8;
+        }
+        c0[dA] = o[m][0];
+        c0[D + dA] = o[m][1];
+        c0[dB] = o[m][2];
+        c0[D + dB] = o[m][3];
     }
     named_barrier_sync(1, NC * 32);
 
-    decode_epilogue<D, KG, NC>(a, ring, row0, nrows, kvh, mt, b, split);
+    decode_epilogue<D, KG, NC, kRT>(a, ring, row0, nrows, kvh, mtile, b, split);
 }
 
 // Log-sum-exp merge of partials (brk_attn_combine: partials gathered from several GPUs): one
@@ -366,39 +472,39 @@ __global__ void combine_kernel(const __grid_constant__ CombineArgs a) {
     }
 }
 
-template <int D>
-cudaError_t launch_decode_t(const CUtensorMap &tmk, const CUtensorMap &tmv, const DecodeArgs &a, dim3 grid,
-                            cudaStream_t s, bool pdl) {
+template <bool Q8, int D>
+cudaError_t launch_t(const CUtensorMap &tmk, const CUtensorMap &tmv, const CUtensorMap &tms, const DecodeArgs &a,
+                      dim3 grid, cudaStream_t s, bool pdl) {
     static unsigned long long configured = 0;  // one bit per device: the opt-in is per device
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 64 || !(configured & (1ull << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             DecodeLayout<D>::kSmemBytes);
+        cudaError_t e = cudaFuncSetAttribute(decode_kernel<Q8, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             DecodeLayout<Q8, D>::kSmemBytes);
         if (e != cudaSuccess) return e;
         if (dev < 64) configured |= 1ull << dev;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(DecodeLayout<D>::kThreads);
-    cfg.dynamicSmemBytes = DecodeLayout<D>::kSmemBytes;
+    cfg.blockDim = dim3(DecodeLayout<Q8, D>::kThreads);
+    cfg.dynamicSmemBytes = DecodeLayout<Q8, D>::kSmemBytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, decode_attn_kernel<D>, tmk, tmv, a);
+    return cudaLaunchKernelEx(&cfg, decode_kernel<Q8, D>, tmk, tmv, tms, a);
 }
 
-template <int D>
-int ctas_per_sm_t() {
+template <bool Q8, int D>
+int ctas_t() {
     static int n = 0;
     if (n == 0) {
-        cudaFuncSetAttribute(decode_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             DecodeLayout<D>::kSmemBytes);
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_attn_kernel<D>, DecodeLayout<D>::kThreads,
-                                                          DecodeLayout<D>::kSmemBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(decode_kernel<Q8, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             DecodeLayout<Q8, D>::kSmemBytes);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<Q8, D>, DecodeLayout<Q8, D>::kThreads,
+                                                          DecodeLayout<Q8, D>::kSmemBytes) != cudaSuccess ||
             n < 1)
             n = 1;
     }
@@ -407,33 +513,42 @@ int ctas_per_sm_t() {
 
 }  // namespace
 
-int decode_stage_keys(int head_dim) {
-    switch (head_dim) {
-        case 64: return DecodeLayout<64>::kStageKeys;
-        case 128: return DecodeLayout<128>::kStageKeys;
-        case 256: return DecodeLayout<256>::kStageKeys;
-        default: return 64;
-    }
-}
+int decode_rows_per_tile() { return kRT; }
 
 int decode_ctas_per_sm(int head_dim, bool q8) {
-    if (q8) return decode_q8_ctas_per_sm(head_dim);
     switch (head_dim) {
-        case 64: return ctas_per_sm_t<64>();
-        case 128: return ctas_per_sm_t<128>();
-        case 256: return ctas_per_sm_t<256>();
+        case 64: return q8 ? ctas_t<true, 64>() : ctas_t<false, 64>();
+        case 128: return q8 ? ctas_t<true, 128>() : ctas_t<false, 128>();
+        case 256: return q8 ? ctas_t<true, 256>() : ctas_t<false, 256>();
         default: return 1;
     }
 }
 
-cudaError_t launch_decode(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const DecodeArgs &a,
-                          int grid_x, int grid_y, int grid_z, cudaStream_t s, bool pdl) {
+cudaError_t launch_decode(bool q8, int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv,
+                           const CUtensorMap &tms, const DecodeArgs &a, int grid_x, int grid_y, int grid_z,
+                           cudaStream_t s, bool pdl) {
+    static_assert(DecodeLayout<false, 64>::kStageKeys == 64 && DecodeLayout<false, 128>::kStageKeys == 64 &&
+                      DecodeLayout<false, 256>::kStageKeys == 32 && DecodeLayout<true, 64>::kStageKeys == 64 &&
+                      DecodeLayout<true, 128>::kStageKeys == 64 && DecodeLayout<true, 256>::kStageKeys == 32,
+                  "stage keys must match decode_stage_keys()");
     const dim3 grid(grid_x, grid_y, grid_z);
     switch (head_dim) {
-        case 64: return launch_decode_t<64>(tmk, tmv, a, grid, s, pdl);
-        case 128: return launch_decode_t<128>(tmk, tmv, a, grid, s, pdl);
-        case 256: return launch_decode_t<256>(tmk, tmv, a, grid, s, pdl);
+        case 64: return q8 ? launch_t<true, 64>(tmk, tmv, tms, a, grid, s, pdl)
+                           : launch_t<false, 64>(tmk, tmv, tms, a, grid, s, pdl);
+        case 128: return q8 ? launch_t<true, 128>(tmk, tmv, tms, a, grid, s, pdl)
+                            : launch_t<false, 128>(tmk, tmv, tms, a, grid, s, pdl);
+        case 256: return q8 ? launch_t<true, 256>(tmk, tmv, tms, a, grid, s, pdl)
+                            : launch_t<false, 256>(tmk, tmv, tms, a, grid, s, pdl);
         default: return cudaErrorInvalidValue;
+    }
+}
+
+int decode_stage_keys(int head_dim) {
+    switch (head_dim) {
+        case 64: return DecodeLayout<false, 64>::kStageKeys;
+        case 128: return DecodeLayout<false, 128>::kStageKeys;
+        case 256: return DecodeLayout<false, 256>::kStageKeys;
+        default: return 64;
     }
 }
 

@@ -1,6 +1,6 @@
-// Pieces shared by the two decode kernels (fp16 cache: decode.cu, int8 cache: decode_q8.cu):
-// the key range of a CTA and the epilogue that merges the key groups and, with split-KV, the
-// splits (the last CTA of a (sequence, kv head, row tile) merges every split's partial).
+// Pieces of the decode kernel (decode.cu) kept apart from its main loop: the key range of a CTA
+// and the epilogue that merges the key groups and, with split-KV, the splits (the last CTA of a
+// (sequence, kv head, row tile) merges every split's partial).
 #pragma once
 
 #include <math_constants.h>
@@ -20,10 +20,10 @@ struct KeyRange {
 };
 
 __device__ __forceinline__ KeyRange decode_key_range(const DecodeArgs &a, int past, int row0, int nrows, int split,
-                                                     int stage_keys, int align) {
+                                                     int stage_keys, int align, int rows_per_tile) {
     const int G = a.G;
     const int t_lo = row0 / G;
-    const int t_hi = min(row0 + 15, nrows - 1) / G;
+    const int t_hi = min(row0 + rows_per_tile - 1, nrows - 1) / G;
     int kv_hi = past + t_hi + 1 - a.kv_offset;
     if (kv_hi > a.cap) kv_hi = a.cap;
     int kv_lo = 0;
@@ -36,17 +36,18 @@ __device__ __forceinline__ KeyRange decode_key_range(const DecodeArgs &a, int pa
 }
 
 // After every consumer warp has written its key group's running max (log2 units), sum and
-// unnormalised output rows into cm [KG][16], cl [KG][16] and co [KG][16][D] at the start of
-// `ring`: writes this CTA's rows (final output, or its split's partial), then, with split-KV,
-// lets the last CTA of the tile merge all splits.  Called by the NC consumer warps only.
-template <int D, int KG, int NC>
+// unnormalised output rows into cm [KG][RT], cl [KG][RT] and co [KG][RT][D] at the start of
+// `ring` (RT query rows per tile): writes this CTA's rows (final output, or its split's partial),
+// then, with split-KV, lets the last CTA of the tile merge all splits.  Called by the NC
+// consumer warps only.
+template <int D, int KG, int NC, int RT>
 __device__ __forceinline__ void decode_epilogue(const DecodeArgs &a, uint8_t *ring, int row0, int nrows, int kvh,
                                                 int mt, int b, int split) {
     const float *cm = reinterpret_cast<const float *>(ring);
-    const float *cl = cm + KG * 16;
-    const float *co = cl + KG * 16;
+    const float *cl = cm + KG * RT;
+    const float *co = cl + KG * RT;
     const int G = a.G, T = a.T;
-    const int nvalid = min(16, nrows - row0);
+    const int nvalid = min(RT, nrows - row0);
     const int rows_total = a.B * T * a.Hq;
     // (a) This CTA's (m, l, o) per row.  Single split: the final output (or the caller's
     // partial); several splits: this split's partial in the workspace.
@@ -54,14 +55,14 @@ __device__ __forceinline__ void decode_epilogue(const DecodeArgs &a, uint8_t *ri
         const int r = idx / D, d = idx % D;
         float M = -CUDART_INF_F;
 #pragma unroll
-        for (int w = 0; w < KG; ++w) M = fmaxf(M, cm[w * 16 + r]);
+        for (int w = 0; w < KG; ++w) M = fmaxf(M, cm[w * RT + r]);
         float Lsum = 0.f, O = 0.f;
         if (M != -CUDART_INF_F) {
 #pragma unroll
             for (int w = 0; w < KG; ++w) {
-                const float f = exp2f(cm[w * 16 + r] - M);
-                Lsum += cl[w * 16 + r] * f;
-                O += co[(w * 16 + r) * D + d] * f;
+                const float f = exp2f(cm[w * RT + r] - M);
+                Lsum += cl[w * RT + r] * f;
+                O += co[(w * RT + r) * D + d] * f;
             }
         }
         const int rr = row0 + r;
@@ -85,10 +86,10 @@ __device__ __forceinline__ void decode_epilogue(const DecodeArgs &a, uint8_t *ri
     // split's partial (threadfence-reduction pattern: release fence, counter, acquire fence).
     __threadfence();
     named_barrier_sync(1, NC * 32);
-    int *flag = reinterpret_cast<int *>(const_cast<float *>(co) + KG * 16 * D);
-    float *row_l = reinterpret_cast<float *>(flag + 4);  // [16]
-    float *row_m = row_l + 16;                            // [16]
-    float *wts = row_m + 16;                              // [16][nsplit]
+    int *flag = reinterpret_cast<int *>(const_cast<float *>(co) + KG * RT * D);
+    float *row_l = reinterpret_cast<float *>(flag + 4);  // [RT]
+    float *row_m = row_l + RT;                            // [RT]
+    float *wts = row_m + RT;                              // [RT][nsplit]
     if (threadIdx.x == 0) {
         const int tile = (b * a.Hkv + kvh) * a.mtiles + mt;
         const int prev = atomicAdd(&a.counters[tile], 1);
@@ -135,9 +136,9 @@ __device__ __forceinline__ void decode_epilogue(const DecodeArgs &a, uint8_t *ri
 
 // Bytes of `ring` the epilogue needs: cm, cl, co, the flag word and the split-merge rows
 // (up to 64 splits).
-template <int D, int KG>
+template <int D, int KG, int RT>
 constexpr uint32_t decode_epilogue_bytes() {
-    return KG * 16 * D * 4 + 2 * KG * 16 * 4 + 16 + 32 * 4 + 16 * 64 * 4;
+    return KG * RT * D * 4 + 2 * KG * RT * 4 + 16 + 2 * RT * 4 + RT * 64 * 4;
 }
 
 }  // namespace brk

@@ -114,19 +114,20 @@ int prefill_tile_keys();
 
 // pdl: launch so that the next (dependent) decode kernel may start during this one.
 cudaError_t launch_append(const AppendArgs &a, cudaStream_t s, bool pdl);
-// pdl: launch as a programmatic dependent of the preceding kernel (the append of brk_attn_step).
-cudaError_t launch_decode(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const DecodeArgs &a,
-                          int grid_x, int grid_y, int grid_z, cudaStream_t s, bool pdl);
-// Decode over the int8 cache: codes maps as for fp16 (int8 boxes), plus the scale map.
-cudaError_t launch_decode_q8(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const CUtensorMap &tms,
-                             const DecodeArgs &a, int grid_x, int grid_y, int grid_z, cudaStream_t s, bool pdl);
+// Decode kernel for both cache types: tmk / tmv map fp16 rows or int8 codes, tms the int8 scales
+// (ignored for fp16); grid (splits, kv heads x row tiles of decode_rows_per_tile() query rows,
+// sequences).  pdl: launch as a programmatic dependent of the preceding kernel (the append of
+// brk_attn_step).
+cudaError_t launch_decode(bool q8, int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv,
+                          const CUtensorMap &tms, const DecodeArgs &a, int grid_x, int grid_y, int grid_z,
+                          cudaStream_t s, bool pdl);
+int decode_rows_per_tile();
 cudaError_t launch_combine(const CombineArgs &a, cudaStream_t s);
 // Tensor-core prefill (head_dim 64 or 128); maps with prefill_tile_keys()-row boxes.
 cudaError_t launch_prefill(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const PrefillArgs &a,
                            cudaStream_t s);
-// Concurrent CTAs per SM of the decode kernel for a head dim (occupancy query).
+// Concurrent CTAs per SM of the decode kernel for a head dim and cache type (occupancy query).
 int decode_ctas_per_sm(int head_dim, bool q8);
-int decode_q8_ctas_per_sm(int head_dim);
 
 // kc/vc point at row row0 of kv head 0 of one (layer, sequence) segment; heads are cap rows apart.
 cudaError_t launch_kv_write_rows(__half *kc, __half *vc, const float *k, const float *v, int n_rows, int n_kv_heads,
