@@ -113,16 +113,13 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     return d;
 }
 
-// Two int8 KV codes stored biased (u = code + 128, one byte each) -> fp16x2 of the signed codes,
+// Two int8 KV codes stored biased (u = code + 128, one byte each) -> fp16x2 of code + 1152,
 // exactly.  `sel` picks the two bytes of w into bytes 0 and 2 of the fp16 pair (0x4140: bytes
-// 0, 1; 0x4342: bytes 2, 3); bytes 1 and 3 become 0x64, so each half reads 1024 + u (0x64uu is
-// exponent 10 with u in the low mantissa bits), and subtracting 1152 = 1024 + 128 leaves the code.
-__device__ __forceinline__ uint32_t codes_to_half2(uint32_t w, uint32_t sel) {
-    const uint32_t h = prmt(w, 0x64646464u, sel);
-    uint32_t r;
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64806480u));
-    return r;
-}
+// 0, 1; 0x4342: bytes 2, 3); bytes 1 and 3 become 0x64, so each half reads 1024 + u = 1152 + code
+// (0x64uu is exponent 10 with u in the low mantissa bits).  Users subtract kCodeBias * (sum of
+// the other operand) from their dot products instead of 1152 from every code.
+constexpr float kCodeBias = 1152.f;
+__device__ __forceinline__ uint32_t codes_biased_half2(uint32_t w, uint32_t sel) { return prmt(w, 0x64646464u, sel); }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -151,6 +148,13 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
     uint32_t y;
     asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+// Hardware 2^x (MUFU; ~2 ulp, flushes subnormals; 2^-inf = 0), for softmax probabilities.
+__device__ __forceinline__ float ex2_fast(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
 

@@ -16,14 +16,19 @@
 //   O^T [D x 8 rows]      += V^T [D x 16 keys] P^T [16 keys x 8 rows]
 // P^T comes from the S^T accumulator fragment with one movmatrix transpose per 8 keys.
 //
-// int8 cache: each code is stored biased by +128 in one byte, so it becomes an exact fp16 value
-// with one byte permute and one fp16x2 subtraction (codes_to_half2).  The K scale is constant over
-// the head dim and factors out of the dot product (shaders.ts:1721-1726): s = scale_k[j] *
-// sum_d q_d code_d; the V scale multiplies the probabilities, p'_j = p_j * scale_v[j], while the
-// row sum keeps p_j.  Lanes read codes as 16-byte words; the head dim is permuted identically in q
-// and K (k-step ks of lane quad qc covers head-dim bytes W qc + 4 ks + 0..3), and a lane's V
-// fragment takes VW bytes at head-dim VW r of four keys, transposed 4 x 4 bytes at a time with
-// byte permutes (output head-dim rows are permuted accordingly and restored at the merge).
+// int8 cache: each code is stored biased by +128 in one byte, so one byte permute turns two codes
+// into the exact fp16 pair code + 1152 (codes_biased_half2); the bias is removed once per row
+// instead of once per code: 1152 * sum(q) from each raw score, 1152 * sum(p') from each output.
+// The K scale is constant over the head dim and factors out of the dot product
+// (shaders.ts:1721-1726): s = scale_k[j] * sum_d q_d code_d; the V scale multiplies the
+// probabilities, p'_j = p_j * scale_v[j], while the row sum keeps p_j.  Lanes read codes as
+// 16-byte words; the head dim is permuted identically in q and K (k-step ks of lane quad qc covers
+// head-dim bytes W qc + 4 ks + 0..3), and a lane's V fragment takes VW bytes at head-dim VW r of
+// four keys, transposed 4 x 4 bytes at a time with byte permutes (output head-dim rows are
+// permuted accordingly and restored at the merge).
+//
+// Tiles whose keys every row of the tile may attend (all but the causal / window edges and the
+// range end) skip the per-score masks.
 #include "decode_common.cuh"
 
 namespace brk {
@@ -198,6 +203,23 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
         }
     }
 
+    // int8: 1152 * (sum of the fp16 q over this slice) for rows 2qc, 2qc + 1 -- the bias of the
+    // raw scores against biased codes.
+    float qbias[2] = {0.f, 0.f};
+    if constexpr (Q8) {
+        float part = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&qf[ks][0]));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&qf[ks][1]));
+            part += (f0.x + f0.y) + (f1.x + f1.y);
+        }
+        part += __shfl_xor_sync(0xffffffffu, part, 1);
+        part += __shfl_xor_sync(0xffffffffu, part, 2);  // row qr's sum, in every lane of quad qr
+        qbias[0] = kCodeBias * __shfl_sync(0xffffffffu, part, 8 * qc);
+        qbias[1] = kCodeBias * __shfl_sync(0xffffffffu, part, 8 * qc + 4);
+    }
+
     // This lane's scores are keys (qr, qr + 8) x rows (2qc, 2qc + 1): causal / window limits.
     int hi[2], lo[2];
 #pragma unroll
@@ -207,12 +229,17 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
         lo[j] = a.window > 0 ? past + r / G - a.window + 1 - a.kv_offset : INT_MIN;
     }
     const bool use_cap = a.softcap > 0.f;
+    // Keys every valid row of the tile attends: [kin_lo, kin_hi).
+    const int t_first = row0 / G, t_last = (min(row0 + kRT, nrows) - 1) / G;
+    const int kin_hi = min(k_end, past + t_first + 1 - a.kv_offset);
+    const int kin_lo = a.window > 0 ? past + t_last - a.window + 1 - a.kv_offset : INT_MIN;
 
     float o[MT][4];
 #pragma unroll
     for (int m = 0; m < MT; ++m) o[m][0] = o[m][1] = o[m][2] = o[m][3] = 0.f;
     float m2[2] = {-CUDART_INF_F, -CUDART_INF_F};  // running max per row, log2 units
     float lsum[2] = {0.f, 0.f};                    // this lane's share of the running sums
+    float psum[2] = {0.f, 0.f};                    // int8: same for the fp16 p' fed to the tensor cores
 
     for (int i = 0; i < ntiles; ++i) {
         const int s = i % S;
@@ -244,8 +271,11 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
             }
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks)
-                mma_16816(sacc, codes_to_half2(wa[ks], 0x4140u), codes_to_half2(wb[ks], 0x4140u),
-                          codes_to_half2(wa[ks], 0x4342u), codes_to_half2(wb[ks], 0x4342u), qf[ks][0], qf[ks][1]);
+                mma_16816(sacc, codes_biased_half2(wa[ks], 0x4140u), codes_biased_half2(wb[ks], 0x4140u),
+                          codes_biased_half2(wa[ks], 0x4342u), codes_biased_half2(wb[ks], 0x4342u), qf[ks][0],
+                          qf[ks][1]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sacc[e] -= qbias[e & 1];
         } else {
             const int krow = kg * 16 + (lane & 15);
 #pragma unroll
@@ -271,7 +301,7 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
             }
         }
 
-        // ---- masked, scaled scores (log2 units) and the online softmax per row.
+        // ---- scaled scores (log2 units), masked on edge tiles, and the online softmax per row.
         float ksc[2] = {1.f, 1.f}, vsc[2] = {1.f, 1.f};
         if constexpr (Q8) {
             const float *sc = reinterpret_cast<const float *>(kt + 2 * L::kTileBytes);
@@ -280,12 +310,9 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
             vsc[0] = sc[SK + kg * 16 + qr];
             vsc[1] = sc[SK + kg * 16 + qr + 8];
         }
-        float mx[2] = {-CUDART_INF_F, -CUDART_INF_F};
-        bool valid[4];
+        const bool interior = key0 >= kin_lo && key0 + 16 <= kin_hi;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const int key = key0 + qr + (e >> 1) * 8;
-            const int j = e & 1;  // row 2qc + j
             float x = sacc[e];
             if constexpr (Q8) x *= ksc[e >> 1];
             if (use_cap) {
@@ -296,11 +323,19 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
             } else {
                 x *= a.scale_log2;
             }
-            valid[e] = key >= lo[j] && key <= hi[j] && key < k_end;
-            x = valid[e] ? x : -CUDART_INF_F;
             sacc[e] = x;
-            mx[j] = fmaxf(mx[j], x);
         }
+        bool valid[4] = {true, true, true, true};
+        if (!interior) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = key0 + qr + (e >> 1) * 8;
+                const int j = e & 1;  // row 2qc + j
+                valid[e] = key >= lo[j] && key <= hi[j] && key < k_end;
+                sacc[e] = valid[e] ? sacc[e] : -CUDART_INF_F;
+            }
+        }
+        float mx[2] = {fmaxf(sacc[0], sacc[2]), fmaxf(sacc[1], sacc[3])};
         float muse[2];
         bool grew = false;
 #pragma unroll
@@ -317,8 +352,9 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
             float alpha[2];
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                alpha[j] = exp2f(m2[j] - muse[j]);
+                alpha[j] = ex2_fast(m2[j] - muse[j]);
                 lsum[j] *= alpha[j];
+                if constexpr (Q8) psum[j] *= alpha[j];
             }
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
@@ -333,13 +369,21 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
         float p[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            p[e] = exp2f(sacc[e] - muse[e & 1]);
+            p[e] = ex2_fast(sacc[e] - muse[e & 1]);
             lsum[e & 1] += p[e];
             if constexpr (Q8) p[e] = valid[e] ? p[e] * vsc[e >> 1] : 0.f;
         }
+        const uint32_t pt0 = pack_half2(p[0], p[1]), pt1 = pack_half2(p[2], p[3]);
+        if constexpr (Q8) {
+            // The fp16 p' the tensor cores see, per row: the bias 1152 * sum(p') of the outputs.
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&pt0));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&pt1));
+            psum[0] += f0.x + f1.x;
+            psum[1] += f0.y + f1.y;
+        }
         // P^T fragments -> P fragments (B operand of O^T += V^T P^T): keys 0-7 and 8-15.
-        const uint32_t pb0 = movmatrix_t(pack_half2(p[0], p[1]));
-        const uint32_t pb1 = movmatrix_t(pack_half2(p[2], p[3]));
+        const uint32_t pb0 = movmatrix_t(pt0);
+        const uint32_t pb1 = movmatrix_t(pt1);
 
         // ---- O^T += V^T P^T over the warp's head-dim slice.
         bool tail = false;
@@ -364,10 +408,10 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
                 // lo, t = 2, 3 in hi.  m-tile 2g+u takes bytes 4g+2u (its row qr) and 4g+2u+1 (row qr+8).
                 const uint32_t lo01 = prmt(vw[0][g], vw[1][g], 0x5140u), hi01 = prmt(vw[0][g], vw[1][g], 0x7362u);
                 const uint32_t lo23 = prmt(vw[2][g], vw[3][g], 0x5140u), hi23 = prmt(vw[2][g], vw[3][g], 0x7362u);
-                mma_16816(o[2 * g], codes_to_half2(lo01, 0x4140u), codes_to_half2(lo01, 0x4342u),
-                          codes_to_half2(lo23, 0x4140u), codes_to_half2(lo23, 0x4342u), pb0, pb1);
-                mma_16816(o[2 * g + 1], codes_to_half2(hi01, 0x4140u), codes_to_half2(hi01, 0x4342u),
-                          codes_to_half2(hi23, 0x4140u), codes_to_half2(hi23, 0x4342u), pb0, pb1);
+                mma_16816(o[2 * g], codes_biased_half2(lo01, 0x4140u), codes_biased_half2(lo01, 0x4342u),
+                          codes_biased_half2(lo23, 0x4140u), codes_biased_half2(lo23, 0x4342u), pb0, pb1);
+                mma_16816(o[2 * g + 1], codes_biased_half2(hi01, 0x4140u), codes_biased_half2(hi01, 0x4342u),
+                          codes_biased_half2(hi23, 0x4140u), codes_biased_half2(hi23, 0x4342u), pb0, pb1);
             }
         } else {
             // Keys past the range end get zero V (in this warp's slice), so that 0 * (whatever
@@ -403,6 +447,21 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
         lsum[j] += __shfl_xor_sync(0xffffffffu, lsum[j], 4);
         lsum[j] += __shfl_xor_sync(0xffffffffu, lsum[j], 8);
         lsum[j] += __shfl_xor_sync(0xffffffffu, lsum[j], 16);
+        if constexpr (Q8) {
+            psum[j] += __shfl_xor_sync(0xffffffffu, psum[j], 4);
+            psum[j] += __shfl_xor_sync(0xffffffffu, psum[j], 8);
+            psum[j] += __shfl_xor_sync(0xffffffffu, psum[j], 16);
+        }
+    }
+    if constexpr (Q8) {
+        // Remove the code bias: O^T[d][row] -= 1152 * sum of the row's p'.
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            o[m][0] -= kCodeBias * psum[0];
+            o[m][1] -= kCodeBias * psum[1];
+            o[m][2] -= kCodeBias * psum[0];
+            o[m][3] -= kCodeBias * psum[1];
+        }
     }
     named_barrier_sync(1, NC * 32);
     float *cm = reinterpret_cast<float *>(ring);  // [key group][kRT]

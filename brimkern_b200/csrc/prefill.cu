@@ -109,12 +109,6 @@ __device__ __forceinline__ void tc_st32(uint32_t taddr, const uint32_t (&r)[32])
         : "memory");
 }
 
-// Hardware 2^x (MUFU; ~2 ulp, flushes subnormals), for the probabilities.
-__device__ __forceinline__ float ex2_fast(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
 
 // Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
