@@ -10,7 +10,8 @@ import os
 import subprocess
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libbrk_attn.so")
+# The in-tree build; BRK_ATTN_LIB may name another build of the same sources (tuning variants).
+LIB_PATH = os.environ.get("BRK_ATTN_LIB") or os.path.join(HERE, "libbrk_attn.so")
 CSRC = os.path.join(HERE, "csrc")
 
 BRK_OK = 0

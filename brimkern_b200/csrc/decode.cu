@@ -41,15 +41,15 @@ template <bool Q8, int D>
 struct DecodeCfg;
 template <>
 struct DecodeCfg<false, 64> {
-    static constexpr int kStages = 6, kMinBlocks = 2, kDSplit = 1, kKeyGroups = 4;
+    static constexpr int kStages = 4, kMinBlocks = 3, kDSplit = 1, kKeyGroups = 4;
 };
 template <>
 struct DecodeCfg<false, 128> {
-    static constexpr int kStages = 3, kMinBlocks = 2, kDSplit = 1, kKeyGroups = 4;
+    static constexpr int kStages = 2, kMinBlocks = 3, kDSplit = 1, kKeyGroups = 4;
 };
 template <>
 struct DecodeCfg<false, 256> {
-    static constexpr int kStages = 3, kMinBlocks = 2, kDSplit = 2, kKeyGroups = 2;
+    static constexpr int kStages = 2, kMinBlocks = 3, kDSplit = 2, kKeyGroups = 2;
 };
 template <>
 struct DecodeCfg<true, 64> {
@@ -248,8 +248,10 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
         uint8_t *vt = kt + L::kTileBytes;
         const int key0 = k_begin + i * SK + kg * 16;
 
-        // ---- S^T = K Q^T for the warp's 16 keys over its head-dim slice.
-        float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+        // ---- S^T = K Q^T for the warp's 16 keys over its head-dim slice (two accumulators, even
+        // and odd k-steps, to halve the dependent MMA chain).
+        float sacc[4];
+        float sacc2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
         if constexpr (Q8) {
             const uint8_t *kb = kt + dh * L::kBoxBytes;
             const int rA = kg * 16 + qr, rB = rA + 8;
@@ -271,11 +273,11 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
             }
 #pragma unroll
             for (int ks = 0; ks < KS; ++ks)
-                mma_16816(sacc, codes_biased_half2(wa[ks], 0x4140u), codes_biased_half2(wb[ks], 0x4140u),
+                mma_16816(sacc2[ks & 1], codes_biased_half2(wa[ks], 0x4140u), codes_biased_half2(wb[ks], 0x4140u),
                           codes_biased_half2(wa[ks], 0x4342u), codes_biased_half2(wb[ks], 0x4342u), qf[ks][0],
                           qf[ks][1]);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) sacc[e] -= qbias[e & 1];
+            for (int e = 0; e < 4; ++e) sacc[e] = (sacc2[0][e] + sacc2[1][e]) - qbias[e & 1];
         } else {
             const int krow = kg * 16 + (lane & 15);
 #pragma unroll
@@ -283,8 +285,10 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
                 const int chunk = dh * (DH / 8) + ks * 2 + (lane >> 4);
                 uint32_t a0, a1, a2, a3;
                 ldsm_x4(smem_addr(kt + (chunk >> 3) * L::kBoxBytes + sw128(krow, chunk & 7)), a0, a1, a2, a3);
-                mma_16816(sacc, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+                mma_16816(sacc2[ks & 1], a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
             }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sacc[e] = sacc2[0][e] + sacc2[1][e];
         }
         if constexpr (DS > 1) {
             // Swap partial scores with the warp holding the other head-dim half (double-buffered by
