@@ -220,8 +220,10 @@ int choose_splits(const brk_ctx *ctx, int head_dim, bool q8, int units, int span
         const long long ctas = (long long)units * n;
         const long long waves = (ctas + slots - 1) / slots;
         const int keys = ((span + n - 1) / n + tk - 1) / tk * tk;
-        double cost = (double)waves * (keys + 2 * tk);  // + fixed per-CTA cost in key units
-        if (n > 1) cost += 2 * tk;                      // the combine pass
+        // + the fixed cost of a CTA (pipeline ramp, merge epilogue) in key units: measured on B200
+        // it is worth about four stages, so short CTAs in many waves lose to fewer, longer ones.
+        double cost = (double)waves * (keys + 4 * tk);
+        if (n > 1) cost += 4 * tk;  // the split merge
         if (cost < best - 1e-9) {
             best = cost;
             best_n = n;
