@@ -272,8 +272,9 @@ def run_prefill(args, c, workload):
 
 def run_sharded(args, c, workload):
     """Config 5 on N GPUs: the KV sequence is split across ranks (ShardPlan), each rank decodes
-    its slice to (m, l, o) partials, one NCCL all-gather per layer, LSE combine on every rank.
-    Strong scaling: the context (and total KV bytes) is fixed, N GPUs share it."""
+    its slice to (m, l, o) partials that its decode kernel stores straight into every rank's
+    exchange area over NVLink (--sharded-nccl: one NCCL all-gather per layer instead), LSE combine
+    on every rank.  Strong scaling: the context (and total KV bytes) is fixed, N GPUs share it."""
     import datetime
 
     import torch
@@ -296,7 +297,8 @@ def run_sharded(args, c, workload):
     ff = llama3_rope_factors(D, c["base"], *c["ff"]) if c["ff"] else None
     rope = RopeTable(eng.ctx, D, c["base"], ff, Lkv)
     cfg = AttnConfig(Hq, Hkv, D, scale=c["scale"], softcap=c["softcap"], rope=rope)
-    dec = ShardedDecoder(eng, plan, layers, B, Hkv, D, extra=1)
+    fused = not args.sharded_nccl
+    dec = ShardedDecoder(eng, plan, layers, B, Hkv, D, extra=1, fused=fused, max_rows=B * Hq)
     gen = torch.Generator(device=dev)
     gen.manual_seed(3000 + rank)
     rows = plan.hi - plan.lo
@@ -356,7 +358,10 @@ def run_sharded(args, c, workload):
             "scaling": "strong", "vs_baseline": None, "dtype": "f16 KV / f32 accumulate", "data": "synthetic",
             "config": {"workload": workload, "global_batch": B, "kv_len": Lkv, "layers": layers,
                        "heads": f"{Hq}q/{Hkv}kv", "head_dim": D,
-                       "parallelism": f"sequence-sharded x{world}: per-layer NCCL all-gather of (m, l, o) partials",
+                       "parallelism": (f"sequence-sharded x{world}: the decode kernel stores its (m, l, o) partials "
+                                       "into every rank's exchange area over NVLink (CUDA IPC), flag-synchronised "
+                                       "combine" if fused else
+                                       f"sequence-sharded x{world}: per-layer NCCL all-gather of (m, l, o) partials"),
                        "l2": f"no flush: each step streams {bytes_step / 1e9:.1f} GB of KV > L2"},
             "tokens_per_s": round(B / (ms_step * 1e-3), 1),
             "frac_of_measured_hbm_per_gpu": round(value / world / peak, 4),
@@ -524,6 +529,8 @@ def main():
     ap.add_argument("--window", type=int, default=None, help="override the even-layer window (diagnostics)")
     ap.add_argument("--kv", choices=["f16", "q8"], default="f16",
                     help="KV cache type: fp16, or the reference's int8 mode (setKvQuant)")
+    ap.add_argument("--sharded-nccl", action="store_true",
+                    help="llama3.2-1b-long on N>1 GPUs: exchange partials with NCCL all-gathers (baseline)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()

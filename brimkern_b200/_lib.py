@@ -24,6 +24,8 @@ BRK_MAX_BATCH = 512
 BRK_KV_F16 = 0
 BRK_KV_I8 = 1
 BRK_DECODE_STATIC_SCRATCH_BYTES = 8 << 20
+BRK_MAX_PEERS = 8
+BRK_PEER_HANDLE_BYTES = 64
 
 _ERR_NAMES = {BRK_ERR_INVALID: "INVALID", BRK_ERR_CUDA: "CUDA", BRK_ERR_CAPACITY: "CAPACITY",
               BRK_ERR_UNSUPPORTED: "UNSUPPORTED", BRK_ERR_DEVICE: "DEVICE"}
@@ -83,6 +85,13 @@ SIGNATURES = [
     ("brk_attn_prefill_step", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp, _vp, _vp]),
     ("brk_attn_decode_partial", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp, _vp]),
     ("brk_attn_combine", _i, [_vp, _i, _i, _i, _vp, _vp, _sz, _vp, _vp]),
+    ("brk_peer_create", _i, [_vp, _i, _i, _i, _i, _pp]),
+    ("brk_peer_handle", _i, [_vp, _vp, _sz]),
+    ("brk_peer_open", _i, [_vp, _i, _vp, _sz]),
+    ("brk_peer_attach", _i, [_vp, _i, _vp]),
+    ("brk_peer_destroy", _i, [_vp]),
+    ("brk_attn_decode_push", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, ctypes.c_uint32, _vp]),
+    ("brk_attn_combine_peers", _i, [_vp, _vp, _i, ctypes.c_uint32, _d, _vp, _vp]),
 ]
 
 _lib = None

@@ -241,7 +241,8 @@ size_t counters_bytes(int units) { return ((size_t)units * sizeof(int) + 255) / 
 // pdl: the decode kernel is a programmatic dependent of the append launched just before it.
 int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
                const int32_t *past_len, const float *q, float *out, float *part_ml, float *part_o, bool clamp_rows,
-               cudaStream_t stream, void *fixed_ws = nullptr, size_t fixed_bytes = 0, bool pdl = false) {
+               cudaStream_t stream, void *fixed_ws = nullptr, size_t fixed_bytes = 0, bool pdl = false,
+               brk_peer *push = nullptr, uint32_t epoch = 0) {
     const int D = p->head_dim, G = p->n_heads / p->n_kv_heads;
     brk::DecodeArgs a;
     memset(&a, 0, sizeof(a));
@@ -318,6 +319,21 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
         a.out = out;
         a.res_ml = part_ml;
         a.res_o = part_o;
+    }
+    if (push) {
+        // This rank's block (parity epoch & 1, source `rank`) of every rank's exchange area.
+        const int par = (int)(epoch & 1u);
+        a.push_world = push->world;
+        a.epoch = epoch;
+        a.push_tiles = units;
+        a.push_done = push->done;
+        for (int r = 0; r < push->world; ++r) {
+            float *blk = static_cast<float *>(push->peers[r]) + ((size_t)par * push->world + push->rank) * push->stride;
+            a.push_ml[r] = blk;
+            a.push_o[r] = blk + (size_t)rows * 2;
+            a.push_flag[r] = reinterpret_cast<unsigned *>(static_cast<char *>(push->peers[r]) + push->flags_offset) +
+                             par * push->world + push->rank;
+        }
     }
     cudaError_t e = brk::launch_decode(kv->q8(), D, kv->tm_dec_k, kv->tm_dec_v, kv->q8() ? kv->tm_dec_s : kv->tm_dec_k,
                                        a, nsplit, p->n_kv_heads * a.mtiles, batch, stream, pdl);
@@ -932,6 +948,143 @@ int brk_attn_combine(brk_ctx *ctx, int n_parts, int rows, int head_dim, const fl
     c.rows = rows;
     c.D = head_dim;
     cudaError_t e = brk::launch_combine(c, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
+    ++ctx->launches;
+    return BRK_OK;
+}
+
+int brk_peer_create(brk_ctx *ctx, int world, int rank, int max_rows, int head_dim, brk_peer **out) {
+    if (!ctx || !out) return fail(BRK_ERR_INVALID, "null argument");
+    *out = nullptr;
+    if (world < 1 || world > BRK_MAX_PEERS || rank < 0 || rank >= world)
+        return fail(BRK_ERR_INVALID, "rank %d of world %d (1..%d ranks)", rank, world, BRK_MAX_PEERS);
+    if (max_rows < 1 || head_dim < 1) return fail(BRK_ERR_INVALID, "max_rows %d / head_dim %d", max_rows, head_dim);
+    DeviceGuard g(ctx->device);
+    brk_peer *pr = new brk_peer();
+    pr->ctx = ctx;
+    pr->world = world;
+    pr->rank = rank;
+    pr->max_rows = max_rows;
+    pr->head_dim = head_dim;
+    pr->stride = ((size_t)max_rows * (2 + head_dim) + 63) / 64 * 64;  // 256-byte aligned blocks
+    pr->flags_offset = 2 * (size_t)world * pr->stride * sizeof(float);
+    const size_t bytes = pr->flags_offset + 256;
+    cudaError_t e = cudaMalloc(&pr->area, bytes);
+    if (e == cudaSuccess) e = cudaMemset(pr->area, 0, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&pr->done, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(pr->done, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        cudaFree(pr->area);
+        cudaFree(pr->done);
+        delete pr;
+        return cuda_fail(e, "peer exchange area");
+    }
+    pr->peers[rank] = pr->area;
+    *out = pr;
+    return BRK_OK;
+}
+
+int brk_peer_handle(const brk_peer *peer, void *handle, size_t handle_bytes) {
+    if (!peer || !handle) return fail(BRK_ERR_INVALID, "null argument");
+    if (handle_bytes < sizeof(cudaIpcMemHandle_t))
+        return fail(BRK_ERR_INVALID, "handle buffer of %zu bytes (needs %zu)", handle_bytes, sizeof(cudaIpcMemHandle_t));
+    DeviceGuard g(peer->ctx->device);
+    cudaIpcMemHandle_t h;
+    BRK_CUDA(cudaIpcGetMemHandle(&h, peer->area));
+    memcpy(handle, &h, sizeof(h));
+    return BRK_OK;
+}
+
+int brk_peer_open(brk_peer *peer, int peer_rank, const void *handle, size_t handle_bytes) {
+    if (!peer || !handle) return fail(BRK_ERR_INVALID, "null argument");
+    if (peer_rank < 0 || peer_rank >= peer->world || peer_rank == peer->rank)
+        return fail(BRK_ERR_INVALID, "peer rank %d (world %d, own rank %d)", peer_rank, peer->world, peer->rank);
+    if (handle_bytes < sizeof(cudaIpcMemHandle_t)) return fail(BRK_ERR_INVALID, "short handle");
+    if (peer->peers[peer_rank]) return fail(BRK_ERR_INVALID, "peer rank %d is already mapped", peer_rank);
+    DeviceGuard g(peer->ctx->device);
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    void *ptr = nullptr;
+    BRK_CUDA(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+    peer->peers[peer_rank] = ptr;
+    peer->opened[peer_rank] = true;
+    return BRK_OK;
+}
+
+int brk_peer_attach(brk_peer *peer, int peer_rank, const brk_peer *other) {
+    if (!peer || !other) return fail(BRK_ERR_INVALID, "null argument");
+    if (peer_rank < 0 || peer_rank >= peer->world || peer_rank == peer->rank || other->rank != peer_rank ||
+        other->world != peer->world || other->max_rows != peer->max_rows || other->head_dim != peer->head_dim)
+        return fail(BRK_ERR_INVALID, "attaching rank %d: areas of different shapes or ranks", peer_rank);
+    if (peer->peers[peer_rank]) return fail(BRK_ERR_INVALID, "peer rank %d is already mapped", peer_rank);
+    if (other->ctx->device != peer->ctx->device) {
+        DeviceGuard g(peer->ctx->device);
+        cudaError_t e = cudaDeviceEnablePeerAccess(other->ctx->device, 0);
+        if (e == cudaErrorPeerAccessAlreadyEnabled) {
+            cudaGetLastError();
+        } else if (e != cudaSuccess) {
+            return cuda_fail(e, "enabling peer access");
+        }
+    }
+    peer->peers[peer_rank] = other->area;
+    return BRK_OK;
+}
+
+int brk_peer_destroy(brk_peer *peer) {
+    if (!peer) return BRK_OK;
+    DeviceGuard g(peer->ctx->device);
+    cudaDeviceSynchronize();
+    for (int r = 0; r < peer->world; ++r)
+        if (peer->opened[r]) cudaIpcCloseMemHandle(peer->peers[r]);
+    cudaFree(peer->area);
+    cudaFree(peer->done);
+    delete peer;
+    return BRK_OK;
+}
+
+int brk_attn_decode_push(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch,
+                         int n_tokens, const int32_t *past_len, const float *q, brk_peer *peer, uint32_t epoch,
+                         void *stream) {
+    int rc = check_call(ctx, kv, layer, p, batch, n_tokens, past_len);
+    if (rc) return rc;
+    if (!q || !peer) return fail(BRK_ERR_INVALID, "null q or peer area");
+    if (peer->ctx != ctx) return fail(BRK_ERR_INVALID, "peer area belongs to another context");
+    if (epoch == 0) return fail(BRK_ERR_INVALID, "epoch 0 is reserved (flags start at 0)");
+    const long long rows = (long long)batch * n_tokens * p->n_heads;
+    if (rows > peer->max_rows || p->head_dim != peer->head_dim)
+        return fail(BRK_ERR_INVALID, "%lld rows of head_dim %d exceed the peer area (%d rows of %d)", rows, p->head_dim,
+                    peer->max_rows, peer->head_dim);
+    for (int r = 0; r < peer->world; ++r)
+        if (!peer->peers[r]) return fail(BRK_ERR_INVALID, "rank %d's area is not mapped (brk_peer_open)", r);
+    DeviceGuard g(ctx->device);
+    return run_decode(ctx, kv, layer, p, batch, n_tokens, past_len, q, nullptr, nullptr, nullptr, true,
+                      static_cast<cudaStream_t>(stream), nullptr, 0, false, peer, epoch);
+}
+
+int brk_attn_combine_peers(brk_ctx *ctx, brk_peer *peer, int rows, uint32_t epoch, double timeout_s, float *out,
+                           void *stream) {
+    if (!ctx || !peer || !out) return fail(BRK_ERR_INVALID, "null argument");
+    if (peer->ctx != ctx) return fail(BRK_ERR_INVALID, "peer area belongs to another context");
+    if (rows < 0 || rows > peer->max_rows) return fail(BRK_ERR_INVALID, "rows %d outside [0, %d]", rows, peer->max_rows);
+    if (epoch == 0) return fail(BRK_ERR_INVALID, "epoch 0 is reserved (flags start at 0)");
+    if (!(timeout_s > 0.0) || timeout_s > 60.0) return fail(BRK_ERR_INVALID, "timeout %g s outside (0, 60]", timeout_s);
+    DeviceGuard g(ctx->device);
+    const int par = (int)(epoch & 1u);
+    float *base = static_cast<float *>(peer->area) + (size_t)par * peer->world * peer->stride;
+    brk::CombineArgs c;
+    c.part_ml = base;
+    c.part_o = base + (size_t)rows * 2;
+    c.stride_ml = c.stride_o = peer->stride;
+    c.out = out;
+    c.out_ml = nullptr;
+    c.out_o = nullptr;
+    c.n_parts = peer->world;
+    c.rows = rows;
+    c.D = peer->head_dim;
+    const unsigned *flags =
+        reinterpret_cast<const unsigned *>(static_cast<const char *>(peer->area) + peer->flags_offset) + par * peer->world;
+    cudaError_t e = brk::launch_combine_peers(c, flags, peer->world, epoch, (unsigned long long)(timeout_s * 1e9),
+                                              ctx->d_err, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
     ++ctx->launches;
     return BRK_OK;

@@ -21,6 +21,7 @@ enum DeviceError : int {
     kErrTmaTimeout = 1,   // a consumer waited too long for a TMA tile
     kErrSlotTimeout = 2,  // the producer waited too long for a free ring slot
     kErrMmaTimeout = 3,   // a tcgen05 commit never arrived
+    kErrPeerTimeout = 4,  // a rank's partials never arrived (sequence-sharded combine)
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
@@ -170,6 +171,17 @@ __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wa
 // Lets the next programmatic-dependent grid in the stream be scheduled.
 __device__ __forceinline__ void griddep_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// System-scope release store / acquire load of a 32-bit flag (the flag may live in another GPU's
+// memory mapped into this process).
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {

@@ -499,11 +499,9 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
     decode_epilogue<D, KG, NC, kRT>(a, ring, row0, nrows, kvh, mtile, b, split);
 }
 
-// Log-sum-exp merge of partials (brk_attn_combine: partials gathered from several GPUs): one
-// warp per row; the row's maximum and sum are reduced across the lanes first.
-__global__ void combine_kernel(const __grid_constant__ CombineArgs a) {
-    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (row >= a.rows) return;
+// Log-sum-exp merge of one row's partials by one warp (brk_attn_combine: partials gathered from
+// several GPUs); the row's maximum and sum are reduced across the lanes first.
+__device__ __forceinline__ void combine_row(const CombineArgs &a, int row, int lane) {
     float M = -CUDART_INF_F;
     for (int p = lane; p < a.n_parts; p += 32) M = fmaxf(M, a.part_ml[(size_t)p * a.stride_ml + (size_t)row * 2]);
 #pragma unroll
@@ -533,6 +531,39 @@ __global__ void combine_kernel(const __grid_constant__ CombineArgs a) {
             }
         }
     }
+}
+
+__global__ void combine_kernel(const __grid_constant__ CombineArgs a) {
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (row < a.rows) combine_row(a, row, lane);
+}
+
+// The combine of a sequence-sharded decode over peer memory: one thread per block waits until
+// every rank's flag holds `epoch` (each rank's decode launch stores it after its last partial
+// landed here), bounded by wait_ns; on timeout the context's error word records
+// kErrPeerTimeout and the block writes nothing.
+__global__ void combine_peers_kernel(const __grid_constant__ CombineArgs a, const unsigned *flags, int world,
+                                     unsigned epoch, unsigned long long wait_ns, int *err) {
+    __shared__ int ready;
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const unsigned long long t0 = global_timer_ns();
+        for (int p = 0; p < world && ok; ++p) {
+            uint32_t polls = 0;
+            while (ld_acquire_sys(flags + p) != epoch) {
+                if ((++polls & 63u) == 0 && (global_timer_ns() - t0 > wait_ns || polls >= kWaitPolls)) {
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        if (!ok && err) atomicCAS(err, 0, kErrPeerTimeout);
+        ready = ok;
+    }
+    __syncthreads();
+    if (!ready) return;
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (row < a.rows) combine_row(a, row, lane);
 }
 
 template <bool Q8, int D>
@@ -613,6 +644,15 @@ int decode_stage_keys(int head_dim) {
         case 256: return DecodeLayout<false, 256>::kStageKeys;
         default: return 64;
     }
+}
+
+cudaError_t launch_combine_peers(const CombineArgs &a, const unsigned *flags, int world, unsigned epoch,
+                                 unsigned long long wait_ns, int *err, cudaStream_t s) {
+    if (a.rows == 0) return cudaSuccess;
+    const int threads = 256;
+    const long long blocks = ((long long)a.rows * 32 + threads - 1) / threads;
+    combine_peers_kernel<<<(unsigned)blocks, threads, 0, s>>>(a, flags, world, epoch, wait_ns, err);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_combine(const CombineArgs &a, cudaStream_t s) {

@@ -35,6 +35,35 @@ __device__ __forceinline__ KeyRange decode_key_range(const DecodeArgs &a, int pa
     return r;
 }
 
+// Push mode: element d of row R's final partial (m in natural-log units) to every rank.
+template <int D>
+__device__ __forceinline__ void push_partial(const DecodeArgs &a, size_t R, int d, float o, float m, float l) {
+    for (int p = 0; p < a.push_world; ++p) {
+        a.push_o[p][R * D + d] = o;
+        if (d == 0) {
+            a.push_ml[p][R * 2] = m;
+            a.push_ml[p][R * 2 + 1] = l;
+        }
+    }
+}
+
+// Push mode: after a tile's rows went out, count the tile; the launch's last tile publishes the
+// epoch to every rank.  Each writer fences its remote stores at system scope before the count, so
+// the flag (a system-scope release) is ordered after every tile's data.
+template <int NC>
+__device__ __forceinline__ void push_finish(const DecodeArgs &a) {
+    __threadfence_system();
+    named_barrier_sync(1, NC * 32);
+    if (threadIdx.x == 0) {
+        const int prev = atomicAdd(a.push_done, 1);
+        if (prev == a.push_tiles - 1) {
+            *a.push_done = 0;  // every tile is in: ready for the next launch
+            __threadfence_system();
+            for (int p = 0; p < a.push_world; ++p) st_release_sys(a.push_flag[p], a.epoch);
+        }
+    }
+}
+
 // After every consumer warp has written its key group's running max (log2 units), sum and
 // unnormalised output rows into cm [KG][RT], cl [KG][RT] and co [KG][RT][D] at the start of
 // `ring` (RT query rows per tile): writes this CTA's rows (final output, or its split's partial),
@@ -70,6 +99,8 @@ __device__ __forceinline__ void decode_epilogue(const DecodeArgs &a, uint8_t *ri
         const size_t R = ((size_t)b * T + t) * a.Hq + h;
         if (a.nsplit == 1 && a.out) {
             a.out[R * D + d] = O / Lsum;
+        } else if (a.nsplit == 1 && a.push_world) {
+            push_partial<D>(a, R, d, O, M == -CUDART_INF_F ? -CUDART_INF_F : M * kLn2, Lsum);
         } else {
             const size_t PR = (size_t)split * rows_total + R;
             a.part_o[PR * D + d] = O;
@@ -80,7 +111,10 @@ __device__ __forceinline__ void decode_epilogue(const DecodeArgs &a, uint8_t *ri
         }
     }
     griddep_launch_dependents();
-    if (a.nsplit == 1) return;
+    if (a.nsplit == 1) {
+        if (a.push_world) push_finish<NC>(a);
+        return;
+    }
 
     // (b) Split-KV: the last CTA to finish for this (sequence, kv head, row tile) merges every
     // split's partial (threadfence-reduction pattern: release fence, counter, acquire fence).
@@ -124,6 +158,8 @@ __device__ __forceinline__ void decode_epilogue(const DecodeArgs &a, uint8_t *ri
             O += wts[r * a.nsplit + sp] * __ldcg(&a.part_o[((size_t)sp * rows_total + R) * D + d]);
         if (a.out) {
             a.out[R * D + d] = O / row_l[r];
+        } else if (a.push_world) {
+            push_partial<D>(a, R, d, O, row_m[r], row_l[r]);
         } else {
             a.res_o[R * D + d] = O;
             if (d == 0) {
@@ -132,6 +168,7 @@ __device__ __forceinline__ void decode_epilogue(const DecodeArgs &a, uint8_t *ri
             }
         }
     }
+    if (a.push_world) push_finish<NC>(a);
 }
 
 // Bytes of `ring` the epilogue needs: cm, cl, co, the flag word and the split-merge rows

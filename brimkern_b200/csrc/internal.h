@@ -22,6 +22,21 @@ struct brk_ctx {
     uint64_t launches = 0;     // kernels launched through this context
 };
 
+// This rank's exchange area for sequence-sharded decode over peer memory (brk_attn_decode_push /
+// brk_attn_combine_peers): [2 parities][world sources][stride floats] of packed partials
+// [rows*2 | rows*D], then [2 parities][world] uint32 epoch flags.  peers[p] is rank p's area as
+// seen from this device (own area included), mapped through CUDA IPC or attached in-process.
+struct brk_peer {
+    brk_ctx *ctx = nullptr;
+    int world = 0, rank = 0, max_rows = 0, head_dim = 0;
+    size_t stride = 0;          // floats per (parity, source) block
+    size_t flags_offset = 0;    // bytes from the area base to the flags
+    void *area = nullptr;
+    void *peers[8] = {};
+    bool opened[8] = {};        // mapped with cudaIpcOpenMemHandle (closed on destroy)
+    int *done = nullptr;        // tiles of this rank's current push launch that have finished
+};
+
 struct brk_rope {
     brk_ctx *ctx = nullptr;
     int head_dim = 0;
@@ -82,6 +97,16 @@ struct DecodeArgs {
     float scale, scale_log2, softcap;
     float cap_k1;           // softcap: 2 * scale * log2(e) / softcap  (exp2 argument of e^{2z})
     float cap_k2;           // softcap: softcap * log2(e)              (score in log2 units)
+    // Push mode (push_world > 0, partial mode only): the final partial of every row goes to
+    // push_ml[p] / push_o[p] on each of the push_world ranks; the last tile of the launch to
+    // finish then stores `epoch` into push_flag[p] on every rank (system-scope release).
+    int push_world;
+    unsigned epoch;
+    int push_tiles;         // tiles of this launch (B * Hkv * mtiles)
+    int *push_done;         // finished-tile counter, zero between launches
+    float *push_ml[8];
+    float *push_o[8];
+    unsigned *push_flag[8];
     int past_len[BRK_MAX_BATCH];
 };
 
@@ -123,6 +148,9 @@ cudaError_t launch_decode(bool q8, int head_dim, const CUtensorMap &tmk, const C
                           cudaStream_t s, bool pdl);
 int decode_rows_per_tile();
 cudaError_t launch_combine(const CombineArgs &a, cudaStream_t s);
+// Combine after a bounded wait (wait_ns) until flags[p] == epoch for every p < world.
+cudaError_t launch_combine_peers(const CombineArgs &a, const unsigned *flags, int world, unsigned epoch,
+                                 unsigned long long wait_ns, int *err, cudaStream_t s);
 // Tensor-core prefill (head_dim 64 or 128); maps with prefill_tile_keys()-row boxes.
 cudaError_t launch_prefill(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const PrefillArgs &a,
                            cudaStream_t s);

@@ -192,6 +192,41 @@ class KvCache:
             pass
 
 
+class PeerArea:
+    """This rank's exchange area for sequence-sharded decode over peer memory (brk_peer): the
+    other ranks' decode kernels store their partials here, and this rank's kernels store into
+    theirs (mapped with CUDA IPC handles, or attached in-process)."""
+
+    def __init__(self, ctx: Context, world: int, rank: int, max_rows: int, head_dim: int):
+        self.ctx, self.world, self.rank = ctx, int(world), int(rank)
+        h = ctypes.c_void_p()
+        check(L.lib().brk_peer_create(ctx.handle, self.world, self.rank, int(max_rows), int(head_dim), ctypes.byref(h)))
+        self.handle = h
+
+    def ipc_handle(self) -> bytes:
+        buf = (ctypes.c_char * L.BRK_PEER_HANDLE_BYTES)()
+        check(L.lib().brk_peer_handle(self.handle, buf, L.BRK_PEER_HANDLE_BYTES))
+        return bytes(buf)
+
+    def open(self, peer_rank: int, handle: bytes) -> None:
+        buf = (ctypes.c_char * len(handle)).from_buffer_copy(handle)
+        check(L.lib().brk_peer_open(self.handle, int(peer_rank), buf, len(handle)))
+
+    def attach(self, peer_rank: int, other: "PeerArea") -> None:
+        check(L.lib().brk_peer_attach(self.handle, int(peer_rank), other.handle))
+
+    def close(self):
+        if self.handle:
+            L.lib().brk_peer_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 @dataclass
 class AttnConfig:
     """LayerCfg's attention fields (kernels.ts:24-56) plus the extensions of this build."""
@@ -494,6 +529,23 @@ class AttentionEngine:
         pos = _positions(past_len, B)
         check(L.lib().brk_attn_decode_partial(self.ctx.handle, kv.handle, layer, ctypes.byref(p), B, T, pos, _ptr(q),
                                               _ptr(part_ml), _ptr(part_o), _stream_ptr(stream)))
+
+    def decodePush(self, kv: KvCache, layer: int, cfg: AttnConfig, q: torch.Tensor, peer: PeerArea, epoch: int,
+                   past_len, stream=None) -> None:
+        """Split-KV partial of this cache's rows, stored into every rank's exchange area."""
+        B = kv.batch
+        T = q.numel() // (B * cfg.n_heads * cfg.head_dim)
+        p = cfg.params()
+        pos = _positions(past_len, B)
+        check(L.lib().brk_attn_decode_push(self.ctx.handle, kv.handle, layer, ctypes.byref(p), B, T, pos, _ptr(q),
+                                           peer.handle, int(epoch), _stream_ptr(stream)))
+
+    def combinePeers(self, peer: PeerArea, rows: int, epoch: int, out: torch.Tensor, timeout_s: float = 2.0,
+                     stream=None) -> torch.Tensor:
+        """Waits for every rank's partials of `epoch`, then their log-sum-exp combine -> out."""
+        check(L.lib().brk_attn_combine_peers(self.ctx.handle, peer.handle, int(rows), int(epoch), float(timeout_s),
+                                             _ptr(out), _stream_ptr(stream)))
+        return out
 
     def combine(self, n_parts: int, rows: int, head_dim: int, part_ml: torch.Tensor, part_o: torch.Tensor,
                 out: torch.Tensor, stream=None, part_stride: int = 0) -> torch.Tensor:

@@ -5,9 +5,13 @@ Each rank owns a contiguous range of positions [lo, hi) of every (layer, sequenc
 keeps only those rows.  Per layer and step:
   1. every rank rotates q (replicated), and the rank owning the new position appends its K/V;
   2. every rank computes split-KV partials (max m, sum l, unnormalised o) over its rows;
-  3. one all-gather of the packed partials [rows*2 | rows*D] (NCCL over NVLink between GPUs);
+  3. the partials [rows*2 | rows*D] reach every rank;
   4. every rank merges the N partials with the log-sum-exp combine.
-The only communication is step 3 (B * Hq * (D + 2) * 4 bytes per rank per layer).
+The only communication is step 3 (B * Hq * (D + 2) * 4 bytes per rank per layer).  Two forms:
+  - fused (``fused=True``, what bench.py runs): the decode kernel itself stores its partials into every rank's exchange
+    area through NVLink (CUDA IPC mappings, brk_attn_decode_push) and publishes an epoch flag;
+    the combine kernel waits for all flags (brk_attn_combine_peers).  No collective launch.
+  - nccl: decode_partial, an NCCL all-gather, then the combine (the library-collective baseline).
 """
 from __future__ import annotations
 
@@ -67,12 +71,28 @@ class ShardedDecoder:
     """One rank's part of a sequence-sharded decode over a context of `context` positions."""
 
     def __init__(self, engine, plan: ShardPlan, n_layers: int, batch: int, n_kv_heads: int, head_dim: int,
-                 extra: int = 1, group=None):
-        from .engine import KvCache
+                 extra: int = 1, group=None, fused: bool = False, max_rows: int = 0):
+        """fused=True needs max_rows (>= batch * n_tokens * n_heads of every step) and, with
+        several ranks, an initialised process group: the ranks exchange IPC handles here (a
+        collective) and must call close() together."""
+        from .engine import KvCache, PeerArea
         self.engine, self.plan, self.group = engine, plan, group
         self.batch, self.head_dim = batch, head_dim
         self.kv = KvCache(engine.ctx, n_layers, batch, n_kv_heads, head_dim, max(1, plan.capacity(extra)))
         self._bufs = {}
+        self.fused = bool(fused)
+        self.peer = None
+        self.epoch = 0
+        if self.fused:
+            if max_rows < 1:
+                raise ValueError("fused sharded decode needs max_rows")
+            self.peer = PeerArea(engine.ctx, plan.world, plan.rank, max_rows, head_dim)
+            if plan.world > 1:
+                handles = [None] * plan.world
+                dist.all_gather_object(handles, self.peer.ipc_handle(), group=group)
+                for r, h in enumerate(handles):
+                    if r != plan.rank:
+                        self.peer.open(r, h)
 
     def _buffers(self, rows: int, dev):
         key = rows
@@ -95,6 +115,10 @@ class ShardedDecoder:
         self.engine.appendKv(self.kv, layer, shard_cfg, q_in, k_in if owns else None, v_in if owns else None, q_work,
                              pos, stream)
         rows = B * cfg.n_heads
+        if self.fused:
+            self.epoch += 1
+            self.engine.decodePush(self.kv, layer, shard_cfg, q_work, self.peer, self.epoch, pos, stream)
+            return self.engine.combinePeers(self.peer, rows, self.epoch, out, stream=stream)
         part, gathered = self._buffers(rows, q_in.device)
         self.engine.decodePartial(self.kv, layer, shard_cfg, q_work, part[:rows * 2], part[rows * 2:], pos, stream)
         gather_partials(part, p.world, self.group, gathered)
@@ -104,4 +128,11 @@ class ShardedDecoder:
         return out
 
     def close(self):
+        """Collective in fused mode: no rank unmaps its area while another may still store to it."""
+        if self.peer is not None:
+            torch.cuda.synchronize(self.kv.ctx.device)
+            if self.plan.world > 1:
+                dist.barrier(group=self.group)
+            self.peer.close()
+            self.peer = None
         self.kv.close()

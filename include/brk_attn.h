@@ -223,6 +223,38 @@ int brk_attn_decode_partial(brk_ctx *ctx, const brk_kv *kv, int layer,
 int brk_attn_combine(brk_ctx *ctx, int n_parts, int rows, int head_dim, const float *part_ml,
                      const float *part_o, size_t part_stride, float *out, void *stream);
 
+/* ---- sequence-sharded decode over peer memory (extension, no reference counterpart) ---------
+ * The fused form of decode_partial + all-gather + combine for one process per GPU: each rank's
+ * decode kernel stores its final partials straight into every rank's exchange area (plain
+ * stores through NVLink into memory mapped with CUDA IPC) and publishes an epoch flag there;
+ * each rank's combine waits for every rank's flag, then merges.
+ *   - The exchange area holds two epochs (parity epoch & 1).  Every rank makes the same calls with
+ *     the same epochs (1, 2, 3, ... one per layer step), decode_push(e) then combine_peers(e) on
+ *     one stream; then no rank can overwrite data another rank has yet to combine.
+ *   - A rank whose partials do not arrive within timeout_s makes the combine write nothing and
+ *     record a device error (brk_ctx_check -> BRK_ERR_DEVICE); recreate the areas after that.
+ *   - Destroy an area only after every rank has finished its last combine (a host barrier). */
+#define BRK_MAX_PEERS 8
+#define BRK_PEER_HANDLE_BYTES 64
+typedef struct brk_peer brk_peer;
+/* This rank's exchange area for `world` ranks of up to max_rows rows (B * n_tokens * n_heads). */
+int brk_peer_create(brk_ctx *ctx, int world, int rank, int max_rows, int head_dim, brk_peer **out);
+/* The area's IPC handle (BRK_PEER_HANDLE_BYTES opaque bytes) for the other ranks' brk_peer_open. */
+int brk_peer_handle(const brk_peer *peer, void *handle, size_t handle_bytes);
+int brk_peer_open(brk_peer *peer, int peer_rank, const void *handle, size_t handle_bytes);
+/* In-process form of brk_peer_open: rank peer_rank's area `other` (same device, or a device with
+ * peer access). */
+int brk_peer_attach(brk_peer *peer, int peer_rank, const brk_peer *other);
+int brk_peer_destroy(brk_peer *peer);
+/* brk_attn_decode_partial over this rank's cache rows, pushed into every rank's area. */
+int brk_attn_decode_push(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p,
+                         int batch, int n_tokens, const int32_t *past_len, const float *q,
+                         brk_peer *peer, uint32_t epoch, void *stream);
+/* Waits (at most timeout_s) for every rank's partials of `epoch`, then out [rows][head_dim] =
+ * their log-sum-exp combine. */
+int brk_attn_combine_peers(brk_ctx *ctx, brk_peer *peer, int rows, uint32_t epoch, double timeout_s,
+                           float *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

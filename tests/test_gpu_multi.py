@@ -1,6 +1,8 @@
-"""Sequence-sharded decode on 2+ GPUs (NCCL over NVLink): each rank holds a slice of the KV
-positions, decodes it to partials, all-gathers them and merges; the result must match the oracle
-over the whole context.  Skipped with fewer than 2 visible GPUs."""
+"""Sequence-sharded decode on 2+ GPUs: each rank holds a slice of the KV positions and decodes it
+to partials, which reach every rank either through an NCCL all-gather or, fused, through the
+decode kernel's own stores into the other ranks' exchange areas (CUDA IPC over NVLink); every
+rank merges them.  The result must match the oracle over the whole context (north-star
+tolerance).  Skipped with fewer than 2 visible GPUs."""
 import os
 import socket
 
@@ -26,7 +28,7 @@ def _inputs(context, B, Hq, Hkv, D):
     return q, k, v
 
 
-def _rank(rank, world, port, context, B, Hq, Hkv, D, path):
+def _rank(rank, world, port, context, B, Hq, Hkv, D, path, fused):
     import datetime
 
     import torch
@@ -44,7 +46,7 @@ def _rank(rank, world, port, context, B, Hq, Hkv, D, path):
         q, k, v = _inputs(context, B, Hq, Hkv, D)
         eng = AttentionEngine(rank)
         plan = ShardPlan(context, world, rank)
-        dec = ShardedDecoder(eng, plan, 1, B, Hkv, D, extra=1)
+        dec = ShardedDecoder(eng, plan, 1, B, Hkv, D, extra=1, fused=fused, max_rows=B * Hq)
         for b in range(B):
             dec.kv.write_rows(0, b, 0, torch.from_numpy(k[b, plan.lo:plan.hi]).to(dev),
                               torch.from_numpy(v[b, plan.lo:plan.hi]).to(dev))
@@ -52,8 +54,10 @@ def _rank(rank, world, port, context, B, Hq, Hkv, D, path):
         q_work = torch.empty((B, 1, Hq, D), dtype=torch.float32, device=dev)
         out = torch.empty((B, 1, Hq, D), dtype=torch.float32, device=dev)
         # The new token (position `context`) brings its own K/V; no rope table: q passes through.
-        dec.step(0, cfg, torch.from_numpy(q).to(dev), torch.from_numpy(k[:, context:context + 1]).contiguous().to(dev),
-                 torch.from_numpy(v[:, context:context + 1]).contiguous().to(dev), context, q_work, out)
+        # Two steps over the same token: the second one uses the other parity of the areas.
+        for _ in range(2):
+            dec.step(0, cfg, torch.from_numpy(q).to(dev), torch.from_numpy(k[:, context:context + 1]).contiguous().to(dev),
+                     torch.from_numpy(v[:, context:context + 1]).contiguous().to(dev), context, q_work, out)
         eng.ctx.check()
         if rank == 0:
             np.save(path, out.cpu().numpy())
@@ -64,8 +68,9 @@ def _rank(rank, world, port, context, B, Hq, Hkv, D, path):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("fused", [False, True])
 @pytest.mark.parametrize("world", [2])
-def test_sequence_sharded_decode_nccl(tmp_path, world):
+def test_sequence_sharded_decode(tmp_path, world, fused):
     torch = pytest.importorskip("torch")
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
@@ -75,7 +80,7 @@ def test_sequence_sharded_decode_nccl(tmp_path, world):
     context, B, Hq, Hkv, D = 4095, 2, 8, 2, 64
     path = str(tmp_path / "out.npy")
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    mp.start_processes(_rank, args=(world, _free_port(), context, B, Hq, Hkv, D, path), nprocs=world,
+    mp.start_processes(_rank, args=(world, _free_port(), context, B, Hq, Hkv, D, path, fused), nprocs=world,
                        start_method="spawn")
     got = np.load(path)
     q, k, v = _inputs(context, B, Hq, Hkv, D)
