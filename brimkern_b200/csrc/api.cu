@@ -809,8 +809,11 @@ int ensure_stage(brk_ctx *ctx, size_t bytes) {
 }
 
 // The tensor-core prefill launch: q rotated (q) or raw with the prologue fused (q_raw).
+// clamp_rows: positions may run past the cache capacity (the kernel attends rows below it), for
+// the non-causal path whose rows all sit at the last key.
 int prefill_impl(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
-                 const int32_t *past_len, const float *q, const float *q_raw, float *out, void *stream) {
+                 const int32_t *past_len, const float *q, const float *q_raw, float *out, void *stream,
+                 bool clamp_rows = false) {
     int rc = check_call(ctx, kv, layer, p, batch, n_tokens, past_len);
     if (rc) return rc;
     if ((!q && !q_raw) || !out) return fail(BRK_ERR_INVALID, "null q or out");
@@ -827,7 +830,7 @@ int prefill_impl(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_param
     brk::PrefillArgs a;
     memset(&a, 0, sizeof(a));
     for (int b = 0; b < batch; ++b) {
-        if (past_len[b] + n_tokens - p->kv_offset > kv->cap)
+        if (!clamp_rows && past_len[b] + n_tokens - p->kv_offset > kv->cap)
             return fail(BRK_ERR_CAPACITY, "sequence %d needs %d cache rows, capacity is %d (grow the cache)", b,
                         past_len[b] + n_tokens - p->kv_offset, kv->cap);
         a.past_len[b] = past_len[b];
@@ -950,6 +953,64 @@ int brk_attn_combine(brk_ctx *ctx, int n_parts, int rows, int head_dim, const fl
     cudaError_t e = brk::launch_combine(c, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "combine kernel launch");
     ++ctx->launches;
+    return BRK_OK;
+}
+
+int brk_attn_full(brk_ctx *ctx, const brk_attn_params *p, int batch, int n_tokens, int kv_len, const float *q,
+                  const float *k, const float *v, float *out, void *stream) {
+    if (!ctx || !p || !q || !k || !v || !out) return fail(BRK_ERR_INVALID, "null argument");
+    if (p->n_heads < 1 || p->n_kv_heads < 1 || p->n_heads % p->n_kv_heads)
+        return fail(BRK_ERR_INVALID, "n_heads %d is not a multiple of n_kv_heads %d", p->n_heads, p->n_kv_heads);
+    if (p->head_dim < 1 || p->head_dim > 256)
+        return fail(BRK_ERR_UNSUPPORTED, "non-causal attention covers head_dim 1..256 (got %d)", p->head_dim);
+    if (p->rope || p->q_norm || p->k_norm || p->window > 0 || p->kv_offset)
+        return fail(BRK_ERR_INVALID, "non-causal attention takes no rope, norm gains, window or kv_offset");
+    if (batch < 1 || batch > BRK_MAX_BATCH || n_tokens < 1 || kv_len < 1)
+        return fail(BRK_ERR_INVALID, "batch %d / n_tokens %d / kv_len %d out of range", batch, n_tokens, kv_len);
+    if ((long long)batch * p->n_kv_heads * kv_len >= (1ll << 31) ||
+        (long long)batch * n_tokens * p->n_heads >= (1ll << 31))
+        return fail(BRK_ERR_CAPACITY, "rows beyond 2^31");
+    DeviceGuard g(ctx->device);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int D = p->head_dim, Dp = D <= 64 ? 64 : D <= 128 ? 128 : 256;
+    const int G = p->n_heads / p->n_kv_heads;
+    const size_t kv_elems = (size_t)batch * p->n_kv_heads * kv_len * Dp;
+    const size_t q_elems = D == Dp ? 0 : (size_t)batch * n_tokens * p->n_heads * Dp;
+    int rc = ensure_stage(ctx, kv_elems * 2 * sizeof(__half) + q_elems * 2 * sizeof(float) + 256);
+    if (rc) return rc;
+    __half *sk = static_cast<__half *>(ctx->stage), *sv = sk + kv_elems;
+    float *qp = const_cast<float *>(q), *op = out;
+    if (q_elems) {
+        qp = reinterpret_cast<float *>(reinterpret_cast<uintptr_t>(sv + kv_elems + 127) & ~uintptr_t(127));
+        op = qp + q_elems;
+    }
+    cudaError_t e = brk::launch_stage_kv(k, v, sk, sv, batch, kv_len, p->n_kv_heads, D, Dp, st);
+    if (e == cudaSuccess && q_elems)
+        e = brk::launch_pad_rows(q, qp, (long long)batch * n_tokens * p->n_heads, D, Dp, st);
+    if (e != cudaSuccess) return cuda_fail(e, "non-causal staging launch");
+    ctx->launches += q_elems ? 2 : 1;
+    // The staged rows as a one-layer cache whose every query sits at its last key.
+    brk_kv view;
+    view.ctx = ctx;
+    view.desc = brk_kv_desc{1, batch, p->n_kv_heads, Dp, kv_len, BRK_KV_F16};
+    view.cap = kv_len;
+    view.k = sk;
+    view.v = sv;
+    if ((rc = kv_build_maps(&view))) return rc;
+    brk_attn_params pp = *p;
+    pp.head_dim = Dp;
+    pp.scale = effective_scale(p);  // 1/sqrt of the caller's head_dim, not the padded one
+    std::vector<int32_t> past(batch, kv_len - 1);
+    if ((Dp == 64 || Dp == 128) && (long long)n_tokens * G > 64)
+        rc = prefill_impl(ctx, &view, 0, &pp, batch, n_tokens, past.data(), qp, nullptr, op, stream, true);
+    else
+        rc = run_decode(ctx, &view, 0, &pp, batch, n_tokens, past.data(), qp, op, nullptr, nullptr, true, st);
+    if (rc) return rc;
+    if (q_elems) {
+        e = cudaMemcpy2DAsync(out, (size_t)D * sizeof(float), op, (size_t)Dp * sizeof(float), (size_t)D * sizeof(float),
+                              (size_t)batch * n_tokens * p->n_heads, cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) return cuda_fail(e, "non-causal output copy");
+    }
     return BRK_OK;
 }
 

@@ -179,4 +179,10 @@ cudaError_t launch_kv_read_q8(const uint8_t *kc, const uint8_t *vc, const float 
 cudaError_t launch_kv_dequant(const uint8_t *kc, const uint8_t *vc, const float *sc, __half *k, __half *v, int layer,
                               int B, int n_kv_heads, int head_dim, int cap, int pitch, int rows, cudaStream_t s);
 
+// Non-causal attention staging (full.cu): token-major f32 [B][L][H][D] K/V -> head-major fp16
+// [B][H][L][Dp] (zero-padded head dim), and f32 rows [rows][D] -> [rows][Dp] zero-padded.
+cudaError_t launch_stage_kv(const float *k, const float *v, __half *ks, __half *vs, int B, int L, int H, int D, int Dp,
+                            cudaStream_t s);
+cudaError_t launch_pad_rows(const float *src, float *dst, long long rows, int D, int Dp, cudaStream_t s);
+
 }  // namespace brk

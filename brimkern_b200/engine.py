@@ -6,7 +6,8 @@ is written in Python with the reference's method names and argument meanings:
 
 * readback twins used by selfValidate -- ``attention`` (kernels.ts:610), ``attentionDecode``
   (:624), ``quantizeKvReadback`` (:664), ``attentionQ8Kv`` (:681), ``attentionQ8KvDecode``
-  (:694), ``rope`` (:556), ``ropeFactors`` (:568), ``rmsnorm`` (:428): numpy in, numpy out;
+  (:694), ``attentionFull`` (:639), ``attentionFullWg`` (:652), ``rope`` (:556), ``ropeFactors``
+  (:568), ``rmsnorm`` (:428): numpy in, numpy out;
 * the resident path -- ``ensureKv`` / ``setKvQuant`` / ``clearKvCache`` (:1760-1806), the
   session check of ``runDecodeGpu`` (:1817-1825), ``recAttention`` (:1626) and the attention
   slice of ``recordLayerKV`` (:1707-1731): device tensors in, device tensors out.
@@ -259,6 +260,7 @@ class AttentionEngine:
         # ?attndecode=0 kill switch (kernels.ts:181-215) -> BRK_ATTN_DECODE=0.
         self.attnDecodeOk = os.environ.get("BRK_ATTN_DECODE", "1") != "0"
         self.kvGpu: Optional[KvCache] = None
+        self.lfm2KvGpu: dict = {}  # LFM2 attention layer -> its own cache (kernels.ts:1990)
         self.kvSession = ""
         self.kvQuant = False
 
@@ -320,6 +322,34 @@ class AttentionEngine:
         self.ctx.check()
         kv.close()
         return kc[..., :headDim].cpu().numpy().ravel(), ks.cpu().numpy().ravel()
+
+    def attentionFull(self, q, k, v, nTokens, nHeads, nKvHeads, headDim, kvLen, scale=None, softcap=0.0):
+        """kernels.ts:639 — non-causal attention: every query attends all kvLen keys
+        (q [nTokens, nHeads, headDim], k / v [kvLen, nKvHeads, headDim] f32)."""
+        qd = self._dev(np.asarray(q, np.float32).reshape(1, nTokens, nHeads, headDim))
+        kd = self._dev(np.asarray(k, np.float32).reshape(1, kvLen, nKvHeads, headDim))
+        vd = self._dev(np.asarray(v, np.float32).reshape(1, kvLen, nKvHeads, headDim))
+        out = torch.empty_like(qd)
+        cfg = AttnConfig(nHeads, nKvHeads, headDim, scale=scale, softcap=softcap)
+        self.recAttentionFull(cfg, qd, kd, vd, out)
+        self.ctx.check()
+        return self._host(out)
+
+    def attentionFullWg(self, q, k, v, nTokens, nHeads, nKvHeads, headDim, kvLen, scale=None, softcap=0.0):
+        """kernels.ts:652 — the reference's workgroup-per-(token, head) variant of attentionFull;
+        here the same operator (one kernel choice per shape)."""
+        return self.attentionFull(q, k, v, nTokens, nHeads, nKvHeads, headDim, kvLen, scale, softcap)
+
+    def recAttentionFull(self, cfg: "AttnConfig", q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
+                         stream=None) -> torch.Tensor:
+        """recAttentionFull (kernels.ts:1277): q [B, T, Hq, D], k / v [B, kvLen, Hkv, D] f32 device
+        tensors -> out [B, T, Hq, D]."""
+        B, T = q.shape[0], q.shape[1]
+        kv_len = k.shape[1]
+        p = cfg.params()
+        check(L.lib().brk_attn_full(self.ctx.handle, ctypes.byref(p), B, T, kv_len, _ptr(q.contiguous()),
+                                    _ptr(k.contiguous()), _ptr(v.contiguous()), _ptr(out), _stream_ptr(stream)))
+        return out
 
     def _attention_q8_readback(self, q, kc, ks, vc, vs, nTokens, nHeads, nKvHeads, headDim, pastLen, scale, softcap,
                                kernel):
@@ -403,6 +433,9 @@ class AttentionEngine:
         if self.kvGpu is not None:
             self.kvGpu.close()
         self.kvGpu = None
+        for kv in self.lfm2KvGpu.values():
+            kv.close()
+        self.lfm2KvGpu = {}
         self.kvSession = ""
 
     def clearKvCache(self) -> None:
@@ -421,6 +454,40 @@ class AttentionEngine:
         elif kv.capacity < rows:
             kv.grow(rows)
         return kv
+
+    # ---- LFM2 attention layers (kernels.ts:1990-2003, 2029-2111; lfm2Model.ts:320-333) --------
+    def ensureLfm2Kv(self, layer: int, rows: int, n_kv_heads: int, head_dim: int, batch: int = 1) -> KvCache:
+        """ensureLfm2Kv (kernels.ts:1990): one cache per LFM2 attention layer (its conv layers
+        keep no K/V), grown with ensureKv's rule max(rows, cap + 1024, 1024)."""
+        kv = self.lfm2KvGpu.get(layer)
+        if kv is not None and (kv.batch, kv.n_kv_heads, kv.head_dim, kv.q8) != (batch, n_kv_heads, head_dim,
+                                                                              self.kvQuant):
+            kv.close()
+            kv = None
+        if kv is None:
+            kv = KvCache(self.ctx, 1, batch, n_kv_heads, head_dim, max(rows, 1024), q8=self.kvQuant)
+            self.lfm2KvGpu[layer] = kv
+        elif kv.capacity < rows:
+            kv.grow(rows)
+        return kv
+
+    LFM2_PREFILL_CHUNK = 128  # lfm2Model.ts:320
+
+    def lfm2Attention(self, layer: int, cfg: AttnConfig, q_in: torch.Tensor, k_in: torch.Tensor, v_in: torch.Tensor,
+                      past_len, chunk: Optional[int] = None, stream=None) -> torch.Tensor:
+        """The attention slice of an LFM2 attention layer in recordLfm2 (kernels.ts:2055-2067):
+        per-head QK-norm and RoPE of the q / k projections, K/V appended to the layer's cache at
+        pastLen, causal attention over it.  q_in [B, T, Hq, D], k_in / v_in [B, T, Hkv, D] f32;
+        a prompt is prefilled in chunks of PREFILL_CHUNK tokens (lfm2Model.ts:320-333), a decode
+        token goes through the fused append + decode step."""
+        B, T = q_in.shape[0], q_in.shape[1]
+        base = [int(past_len)] * B if np.isscalar(past_len) else [int(x) for x in past_len]
+        kv = self.ensureLfm2Kv(layer, max(base) + T, cfg.n_kv_heads, cfg.head_dim, B)
+        G = cfg.n_heads // cfg.n_kv_heads
+        if T * G <= 64 and self.attnDecodeOk:
+            return self.attentionLayer(kv, 0, cfg, q_in, k_in, v_in, base, stream=stream)
+        return self.prefillChunked(kv, 0, cfg, q_in, k_in, v_in, base, chunk=chunk or self.LFM2_PREFILL_CHUNK,
+                                   stream=stream)
 
     def session(self, session_id: str, past_len) -> None:
         """runDecodeGpu's session rule (kernels.ts:1817-1825): a new session id or pastLen 0

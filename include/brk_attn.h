@@ -207,6 +207,16 @@ int brk_attn_prefill_step(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_pa
                           int batch, int n_tokens, const int32_t *past_len, const float *q_in,
                           const float *k_in, const float *v_in, float *out, void *stream);
 
+/* Non-causal attention (attention_full / attention_full_wg, shaders.ts:1530-1667, dispatched by
+ * recAttentionFull, kernels.ts:1277-1290; UNet / ViT self- and cross-attention): every query
+ * attends all kv_len keys, kv_len independent of n_tokens.  q [B][n_tokens][n_heads][head_dim],
+ * k / v [B][kv_len][n_kv_heads][head_dim], out [B][n_tokens][n_heads][head_dim] f32; head_dim
+ * 1..256.  K/V are staged as fp16 in the context (so two streams must not run this on one
+ * context at the same time).  p->scale (<= 0: 1/sqrt(head_dim)) and p->softcap apply; rope,
+ * norm gains, window and kv_offset must be unset. */
+int brk_attn_full(brk_ctx *ctx, const brk_attn_params *p, int batch, int n_tokens, int kv_len,
+                  const float *q, const float *k, const float *v, float *out, void *stream);
+
 /* Split-KV partial over this cache's rows (extension, no reference counterpart; used to shard
  * a long context across GPUs): per row R = (b*T + t)*Hq + h, part_ml[2R] = max score m (natural
  * log units, -inf if no key), part_ml[2R+1] = sum l of exp(s - m), part_o[R*D..] = sum of

@@ -191,6 +191,49 @@ void brk_oracle_combine(const double *m, const double *l, const double *o, int n
     }
 }
 
+/* Non-causal attention (attention_full, shaders.ts:1530-1570) as the reference's own gate computes
+ * it (kernels.ts:3168-3177): per (head, query) the score s_j = f32(dot * scale) with the dot in
+ * double, mx = max s_j, s_j = f32(exp(s_j - mx)), sum in double, o = f32(sum_j (s_j / sum) v_j)
+ * accumulated in double.  Every query attends all kv_len keys.  Extensions that reduce to the gate
+ * in its case (n_kv_heads == n_heads, no softcap): GQA (kvh = floor(h / group)) and the softcap
+ * c * tanh(s / c) of attentionCpu (kernels.ts:3469) applied before the f32 store. */
+void brk_oracle_attention_full(const float *q, const float *k, const float *v, int n_tokens,
+                               int n_heads, int n_kv_heads, int head_dim, int kv_len,
+                               double scale, double softcap, float *o) {
+    scale = default_scale(scale, head_dim);
+    double group = (double)n_heads / (double)n_kv_heads;
+    float *s = (float *)malloc(sizeof(float) * (size_t)(kv_len > 0 ? kv_len : 1));
+    double *acc = (double *)malloc(sizeof(double) * (size_t)head_dim);
+    for (int h = 0; h < n_heads; h++)
+        for (int t = 0; t < n_tokens; t++) {
+            int kvh = (int)floor((double)h / group);
+            const float *qr = q + ((long long)t * n_heads + h) * head_dim;
+            float mx = -INFINITY;
+            for (int j = 0; j < kv_len; j++) {
+                const float *kr = k + ((long long)j * n_kv_heads + kvh) * head_dim;
+                double d2 = 0;
+                for (int e = 0; e < head_dim; e++) d2 += (double)qr[e] * (double)kr[e];
+                s[j] = (float)cap_score(d2 * scale, softcap);
+                if (s[j] > mx) mx = s[j];
+            }
+            double sum = 0;
+            for (int j = 0; j < kv_len; j++) {
+                s[j] = (float)exp((double)s[j] - (double)mx);
+                sum += (double)s[j];
+            }
+            for (int e = 0; e < head_dim; e++) {
+                double a = 0;
+                for (int j = 0; j < kv_len; j++)
+                    a += ((double)s[j] / sum) * (double)v[((long long)j * n_kv_heads + kvh) * head_dim + e];
+                acc[e] = a;
+            }
+            float *orow = o + ((long long)t * n_heads + h) * head_dim;
+            for (int e = 0; e < head_dim; e++) orow[e] = (float)acc[e];
+        }
+    free(acc);
+    free(s);
+}
+
 /* quantize_kv shader (shaders.ts:1673-1705), in the shader's own f32 arithmetic:
  * amax over the head's D values, scale = amax == 0 ? 1e-8 : amax/127, inv = 1/scale,
  * code = clamp(round(x*inv), -127, 127) with WGSL round() = round-half-to-even (rintf). */

@@ -62,6 +62,11 @@ void brk_oracle_attention_partial(const float *q, const float *k, const float *v
 void brk_oracle_combine(const double *m, const double *l, const double *o, int n_parts,
                         int rows, int head_dim, float *out);
 
+/* Non-causal attention as the attention_full gate computes it (kernels.ts:3168-3177). */
+void brk_oracle_attention_full(const float *q, const float *k, const float *v, int n_tokens,
+                               int n_heads, int n_kv_heads, int head_dim, int kv_len,
+                               double scale, double softcap, float *o);
+
 /* int8 KV quantisation — quantize_kv shader, shaders.ts:1673-1705 (symmetric amax/127,
  * per-(row, head) f32 scale, WGSL round() = round-half-to-even, clamp +-127), in the
  * shader's f32 arithmetic, written at row offset row_offset.

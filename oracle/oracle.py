@@ -45,6 +45,8 @@ def lib():
         L.brk_oracle_attention_partial.argtypes = ([_f32p, _f32p, _f32p] + [ctypes.c_int] * 5 + [ctypes.c_double, ctypes.c_double]
                                                    + [ctypes.c_int] * 3 + [_f64p, _f64p, _f64p])
         L.brk_oracle_combine.argtypes = [_f64p, _f64p, _f64p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p]
+        L.brk_oracle_attention_full.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_double, _f32p]
         L.brk_oracle_quantize_kv.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _i8p, _f32p]
         L.brk_oracle_attention_batch.argtypes = ([_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_longlong] + [ctypes.c_int] * 4
                                                  + [_i32p, ctypes.c_double, ctypes.c_double, ctypes.c_int, ctypes.c_int, _f32p])
@@ -126,6 +128,18 @@ def combine(m, l, o, n_parts, rows, head_dim):
     out = np.zeros(rows * head_dim, np.float32)
     lib().brk_oracle_combine(mp, lp, op, n_parts, rows, head_dim, out.ctypes.data_as(_f32p))
     return out
+
+
+def attention_full(q, k, v, n_tokens, n_heads, n_kv_heads, head_dim, kv_len, scale=None, softcap=0.0):
+    """Non-causal attention of the attention_full gate (kernels.ts:3168-3177)."""
+    q, qp = _f32(q)
+    k, kp = _f32(k)
+    v, vp = _f32(v)
+    o = np.zeros(n_tokens * n_heads * head_dim, np.float32)
+    lib().brk_oracle_attention_full(qp, kp, vp, n_tokens, n_heads, n_kv_heads, head_dim, kv_len,
+                                    math.nan if scale is None else float(scale), float(softcap or 0.0),
+                                    o.ctypes.data_as(_f32p))
+    return o
 
 
 def quantize_kv(src, rows, n_kv_heads, head_dim, row_offset=0, cap_rows=None):

@@ -5,11 +5,13 @@ Run here, where the reference is mounted (default ``/root/reference``, or ``$BRK
     python tests/golden/gen_golden.py
 
 It extracts ``attentionCpu``, ``ropeCpu``, ``ropeFactorsCpu`` and ``rmsnormCpu`` verbatim from
-``src/lib/webgpu/kernels.ts`` (lines 3395-3495), runs them through ``jsmini`` (a JS-subset
-interpreter with JS number semantics; no JavaScript engine exists in this image) on seeded
-inputs, and writes ``golden.npz`` + ``golden.json`` next to this file.  The cases replay the
-reference's own selfValidate shapes (kernels.ts:2519-2535, 2556-2568, 2611-2640), the
-QK-norm shape of the Qwen3 gate (kernels.ts:2676-2688) and the config-1 decode shape.
+``src/lib/webgpu/kernels.ts`` (lines 3395-3495), and the inline reference loop of the
+attention_full gate (kernels.ts:3171-3177, wrapped in a function that declares its inputs), runs
+them through ``jsmini`` (a JS-subset interpreter with JS number semantics; no JavaScript engine
+exists in this image) on seeded inputs, and writes ``golden.npz`` + ``golden.json`` next to this
+file.  The cases replay the reference's own selfValidate shapes (kernels.ts:2519-2535, 2556-2568,
+2611-2640, 3168-3201), the QK-norm shape of the Qwen3 gate (kernels.ts:2676-2688) and the
+config-1 decode shape.
 The fixtures are committed; tests read them without the reference.
 """
 from __future__ import annotations
@@ -85,7 +87,30 @@ def cases():
     att("att_prefill_past0", 7, 4, 2, 16, 0, dist=normal)
     # config 1: Qwen2.5-0.5B decode, positions 0..1023 + 1 new token, N(0,1), scale 1/8 (default)
     att("att_config1_qwen05_past1024", 1, 14, 2, 64, 1024, dist=normal)
+
+    # --- non-causal attention_full gates (kernels.ts:3168-3201): the cross-attention shape, then
+    # the UNet shapes of the workgroup-kernel gate (partial tile, CLIP text length, head_dim 160).
+    def full(name, nT, kvL, nH, hd, dist=uniform):
+        out.append(dict(name=name, fn="attentionFullGate", n_tokens=nT, kv_len=kvL, n_heads=nH, head_dim=hd,
+                        q=dist(rng, nT * nH * hd), k=dist(rng, kvL * nH * hd), v=dist(rng, kvL * nH * hd)))
+
+    full("full_gate_cross", 3, 5, 2, 4)
+    full("full_sdturbo_self", 70, 70, 5, 64)
+    full("full_clip_cross", 16, 77, 5, 64)
+    full("full_sdxs_hd160", 9, 9, 8, 160)
     return out
+
+
+def extract_full_gate(src: str) -> str:
+    """The attention_full gate's reference loop (kernels.ts:3171-3177), verbatim, inside a function
+    that declares the names it uses (the gate's own declarations at kernels.ts:3170)."""
+    marker = src.index("// attention_full: NON-causal")
+    start = src.index("for (let h = 0; h < nH; h++) for (let t = 0; t < nT; t++) {", marker)
+    end = src.index("if (!closeRel(await this.attentionFull(aq, ak, av", start)
+    body = src[start:end].rstrip()
+    return ("function attentionFullGate(aq, ak, av, nT, kvL, nH, hd2) {\n"
+            "const dd = nH * hd2, sc = 1 / Math.sqrt(hd2);\n"
+            "const aref = new Float32Array(nT * dd);\n" + body + "\nreturn aref;\n}")
 
 
 def run_case(interp, c):
@@ -103,6 +128,9 @@ def run_case(interp, c):
             if c["one_plus"] is not None:
                 args.append(bool(c["one_plus"]))
         r = interp.call(fn, *args)
+    elif fn == "attentionFullGate":
+        r = interp.call(fn, jsmini.F32Array(c["q"]), jsmini.F32Array(c["k"]), jsmini.F32Array(c["v"]),
+                        float(c["n_tokens"]), float(c["kv_len"]), float(c["n_heads"]), float(c["head_dim"]))
     elif fn == "attentionCpu":
         args = [jsmini.F32Array(c["q"]), jsmini.F32Array(c["k"]), jsmini.F32Array(c["v"]), float(c["n_tokens"]),
                 float(c["n_heads"]), float(c["n_kv_heads"]), float(c["head_dim"]), float(c["past_len"])]
@@ -121,6 +149,7 @@ def main():
     interp = jsmini.Interpreter()
     for f in FUNCS:
         interp.load(jsmini.extract_function(src, f))
+    interp.load(extract_full_gate(src))
     arrays, manifest = {}, []
     for c in cases():
         t0 = time.time()
@@ -134,7 +163,7 @@ def main():
         print(f"{c['name']:34s} {out.size:7d} values  {time.time() - t0:6.1f}s", flush=True)
     np.savez_compressed(os.path.join(HERE, "golden.npz"), **arrays)
     with open(os.path.join(HERE, "golden.json"), "w") as fh:
-        json.dump({"source": "src/lib/webgpu/kernels.ts:3395-3495 executed by tests/golden/jsmini.py",
+        json.dump({"source": "src/lib/webgpu/kernels.ts:3395-3495 and 3171-3177 executed by tests/golden/jsmini.py",
                    "cases": manifest}, fh, indent=1)
 
 

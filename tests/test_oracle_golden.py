@@ -1,6 +1,7 @@
 """Pin the C oracle to the reference: bit-exact against fixtures made by executing the
 reference's own attentionCpu / ropeCpu / ropeFactorsCpu / rmsnormCpu source
-(src/lib/webgpu/kernels.ts:3395-3495) with tests/golden/jsmini.py."""
+(src/lib/webgpu/kernels.ts:3395-3495) and the attention_full gate's reference loop
+(kernels.ts:3171-3177) with tests/golden/jsmini.py."""
 import math
 
 import numpy as np
@@ -18,14 +19,17 @@ def _run(c, a):
     if fn == "rmsnormCpu":
         eps = 1e-5 if c["eps"] is None else c["eps"]  # kernels.ts:3395 default eps
         return O.rmsnorm(a["x"], a["w"], c["rows"], c["dim"], eps, bool(c["one_plus"]))
+    if fn == "attentionFullGate":
+        return O.attention_full(a["q"], a["k"], a["v"], c["n_tokens"], c["n_heads"], c["n_heads"], c["head_dim"],
+                                c["kv_len"])
     return O.attention(a["q"], a["k"], a["v"], c["n_tokens"], c["n_heads"], c["n_kv_heads"], c["head_dim"],
                        c["past_len"], c["scale"], c["softcap"] or 0.0)
 
 
 def test_golden_cases_present(golden):
-    assert len(golden) >= 19
+    assert len(golden) >= 23
     fns = {c["fn"] for c, _ in golden.values()}
-    assert fns == {"ropeCpu", "ropeFactorsCpu", "rmsnormCpu", "attentionCpu"}
+    assert fns == {"ropeCpu", "ropeFactorsCpu", "rmsnormCpu", "attentionCpu", "attentionFullGate"}
 
 
 @pytest.mark.parametrize("name", [
@@ -33,7 +37,7 @@ def test_golden_cases_present(golden):
     "rope_llama_pos131071", "rmsnorm_qk_small", "rmsnorm_qk_hd128", "rmsnorm_oneplus", "rmsnorm_default_eps",
     "att_gqa_plain", "att_gqa_softcap", "att_decode_qwen05_past300", "att_decode_qwen05_nt10_past173",
     "att_decode_softcap_hd8", "att_decode_hd128_past70", "att_decode_hd256_gemma", "att_prefill_past0",
-    "att_config1_qwen05_past1024",
+    "att_config1_qwen05_past1024", "full_gate_cross", "full_sdturbo_self", "full_clip_cross", "full_sdxs_hd160",
 ])
 def test_oracle_bit_exact_vs_reference(golden, name):
     c, a = golden[name]
