@@ -136,6 +136,158 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32) append_kernel(const __grid
     }
 }
 
+// Row-block form of the same append for head_dim 64 / 128 / 256: ROWS head rows per block of 256
+// threads.  The rows are staged in shared memory with coalesced loads (padded stride D + 1, so
+// that one thread walking one row and its neighbours walking theirs hit distinct banks); one
+// thread per row then runs the ordered double sum of squares, all threads apply the norm and the
+// rotation element by element (coalesced gains, table and stores), and an int8 cache quantises
+// each K / V row from its final f32 values.  Same operations in the same order as append_kernel,
+// so the outputs are the same bits.
+template <int D, int ROWS>
+__global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant__ AppendArgs a) {
+    griddep_launch_dependents();
+    griddep_wait();
+    constexpr int kStride = D + 1;
+    constexpr int H2 = D / 2;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    double *inv_s = reinterpret_cast<double *>(smem_raw);                 // [ROWS]
+    int4 *meta = reinterpret_cast<int4 *>(smem_raw + ROWS * sizeof(double));  // [ROWS] kind, bt, head, pos
+    float *xs = reinterpret_cast<float *>(smem_raw + ROWS * (sizeof(double) + sizeof(int4)));  // [ROWS][D+1]
+    const int per_tok = a.Hq + 2 * a.Hkv;
+    const long long total = (long long)a.B * a.T * per_tok;
+    const long long row0 = (long long)blockIdx.x * ROWS;
+    const int nrow = (int)min((long long)ROWS, total - row0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // Row descriptors: kind 0 = q, 1 = k, 2 = v, -1 = nothing to do (no q_out / no k, v inputs).
+    if (threadIdx.x < nrow) {
+        const long long row = row0 + threadIdx.x;
+        const int bt = (int)(row / per_tok), kind_h = (int)(row % per_tok);
+        int kind, h;
+        if (kind_h < a.Hq) {
+            kind = a.q_out ? 0 : -1;
+            h = kind_h;
+        } else if (kind_h < a.Hq + a.Hkv) {
+            kind = a.k_in ? 1 : -1;
+            h = kind_h - a.Hq;
+        } else {
+            kind = a.v_in ? 2 : -1;
+            h = kind_h - a.Hq - a.Hkv;
+        }
+        meta[threadIdx.x] = make_int4(kind, bt, h, a.past_len[bt / a.T] + bt % a.T);
+    }
+    __syncthreads();
+    auto source = [&](int4 m) -> const float * {
+        return m.x == 0 ? a.q_in + ((size_t)m.y * a.Hq + m.z) * D
+                        : (m.x == 1 ? a.k_in : a.v_in) + ((size_t)m.y * a.Hkv + m.z) * D;
+    };
+    // 1. Coalesced loads: one warp per row at a time.
+    for (int lr = warp; lr < nrow; lr += 8) {
+        const int4 m = meta[lr];
+        if (m.x < 0) continue;
+        const float4 *src = reinterpret_cast<const float4 *>(source(m));
+        for (int c = lane; c < D / 4; c += 32) {
+            const float4 x = src[c];
+            float *dst = xs + lr * kStride + 4 * c;
+            dst[0] = x.x, dst[1] = x.y, dst[2] = x.z, dst[3] = x.w;
+        }
+    }
+    __syncthreads();
+    // 2. rmsnormCpu's ordered sum (kernels.ts:3395), one thread per row: inv = 1/sqrt(ss/D + eps).
+    if (threadIdx.x < nrow) {
+        const int4 m = meta[threadIdx.x];
+        const float *gain = m.x == 0 ? a.q_norm : m.x == 1 ? a.k_norm : nullptr;
+        double inv = 0.0;
+        if (m.x >= 0 && gain) {
+            const float *x = xs + threadIdx.x * kStride;
+            double ss = 0.0;
+#pragma unroll 16
+            for (int d = 0; d < D; ++d) ss = __dadd_rn(ss, __dmul_rn((double)x[d], (double)x[d]));
+            inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)D), a.eps)));
+        }
+        inv_s[threadIdx.x] = inv;
+    }
+    __syncthreads();
+    // 3. Norm and rotation (ropeCpu kernels.ts:3445) per element pair (i, i + D/2), and the stores:
+    // one warp per row, lane l always owning pairs i = l + 32u, so that its gains are converted
+    // once per block and a row's addresses once per row.
+    constexpr int NP = H2 / 32;  // pairs per lane
+    const bool q8 = a.kc == nullptr && a.kc8 != nullptr;
+    double gq[NP][2], gk[NP][2];
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+        const int i = lane + 32 * u;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const double wq = a.q_norm ? (double)a.q_norm[i + e * H2] : 0.0;
+            const double wk = a.k_norm ? (double)a.k_norm[i + e * H2] : 0.0;
+            gq[u][e] = a.one_plus ? __dadd_rn(1.0, wq) : wq;
+            gk[u][e] = a.one_plus ? __dadd_rn(1.0, wk) : wk;
+        }
+    }
+    for (int lr = warp; lr < nrow; lr += 8) {
+        const int4 m = meta[lr];
+        if (m.x < 0) continue;
+        float *xr = xs + lr * kStride;
+        const bool norm = m.x == 0 ? a.q_norm != nullptr : m.x == 1 && a.k_norm != nullptr;
+        const double inv = inv_s[lr];
+        const bool rotate = a.rope && m.x < 2;
+        const double2 *cs = rotate ? a.rope + (size_t)m.w * H2 : nullptr;
+        float *qdst = nullptr;
+        __half *cdst = nullptr;
+        if (m.x == 0) {
+            qdst = a.q_out + ((size_t)m.y * a.Hq + m.z) * D;
+        } else if (!q8) {
+            const size_t crow =
+                ((size_t)(a.layer * a.B + m.y / a.T) * a.Hkv + m.z) * a.cap + (size_t)(m.w - a.kv_offset);
+            cdst = (m.x == 1 ? a.kc : a.vc) + crow * D;
+        }
+#pragma unroll
+        for (int u = 0; u < NP; ++u) {
+            const int i = lane + 32 * u;
+            double y0 = xr[i], y1 = xr[i + H2];
+            if (norm) {
+                const double g0 = m.x == 0 ? gq[u][0] : gk[u][0], g1 = m.x == 0 ? gq[u][1] : gk[u][1];
+                y0 = (double)(float)__dmul_rn(__dmul_rn(y0, inv), g0);
+                y1 = (double)(float)__dmul_rn(__dmul_rn(y1, inv), g1);
+            }
+            float o0 = (float)y0, o1 = (float)y1;
+            if (rotate) {
+                const double2 e = cs[i];
+                o0 = (float)__dsub_rn(__dmul_rn(y0, e.x), __dmul_rn(y1, e.y));
+                o1 = (float)__dadd_rn(__dmul_rn(y1, e.x), __dmul_rn(y0, e.y));
+            }
+            if (qdst) {
+                qdst[i] = o0;
+                qdst[i + H2] = o1;
+            } else if (cdst) {
+                cdst[i] = __float2half_rn(o0);
+                cdst[i + H2] = __float2half_rn(o1);
+            } else {
+                xr[i] = o0;  // int8: quantised below from the final row
+                xr[i + H2] = o1;
+            }
+        }
+    }
+    if (q8) {
+        __syncthreads();
+        for (int lr = warp; lr < nrow; lr += 8) {
+            const int4 m = meta[lr];
+            if (m.x < 1) continue;
+            const int b = m.y / a.T;
+            const size_t seg = (size_t)(a.layer * a.B + b) * a.Hkv + m.z;
+            const size_t r = (size_t)(m.w - a.kv_offset);
+            quantize_row_warp(xs + lr * kStride, D, (m.x == 1 ? a.kc8 : a.vc8) + (seg * a.cap + r) * D,
+                              a.scales + (seg * 2 + (m.x == 1 ? 0 : 1)) * a.scale_pitch + r, lane);
+        }
+    }
+}
+
+template <int D, int ROWS>
+constexpr size_t append_block_smem() {
+    return ROWS * (sizeof(double) + sizeof(int4)) + (size_t)ROWS * (D + 1) * sizeof(float);
+}
+
 // Plain f32 -> fp16 row store into one (layer, sequence) segment: rows [row0, row0+n) of every
 // kv head.  kc/vc point at row row0 of kv head 0 of the segment; heads are `cap` rows apart.
 __global__ void kv_write_rows_kernel(__half *kc, __half *vc, const float *k, const float *v, int n_rows, int Hkv,
@@ -166,6 +318,13 @@ __global__ void kv_read_rows_kernel(const __half *kc, const __half *vc, uint16_t
 
 }  // namespace
 
+template <int D, int ROWS>
+cudaError_t launch_block(cudaLaunchConfig_t cfg, const AppendArgs &a, long long rows) {
+    cfg.gridDim = dim3((unsigned)((rows + ROWS - 1) / ROWS));
+    cfg.dynamicSmemBytes = append_block_smem<D, ROWS>();
+    return cudaLaunchKernelEx(&cfg, append_block_kernel<D, ROWS>, a);
+}
+
 cudaError_t launch_append(const AppendArgs &a, cudaStream_t s, bool pdl) {
     const long long rows = (long long)a.B * a.T * (a.Hq + 2 * a.Hkv);
     if (rows == 0) return cudaSuccess;
@@ -179,11 +338,20 @@ cudaError_t launch_append(const AppendArgs &a, cudaStream_t s, bool pdl) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
+    // Head dims 64 / 128 / 256: row blocks (large appends: 8 KB of rows per block; decode-sized
+    // ones: 16 rows per block, so that the rows spread over the SMs).
+    const bool big = rows >= 148LL * 2 * (8192 / (a.D > 0 ? a.D : 1));
+    cfg.blockDim = dim3(256);
     switch (a.D) {
-        case 64: return cudaLaunchKernelEx(&cfg, append_kernel<64>, a);
-        case 128: return cudaLaunchKernelEx(&cfg, append_kernel<128>, a);
-        case 256: return cudaLaunchKernelEx(&cfg, append_kernel<256>, a);
-        default: return cudaLaunchKernelEx(&cfg, append_kernel<0>, a);
+        case 64:
+            return big ? launch_block<64, 128>(cfg, a, rows) : launch_block<64, 16>(cfg, a, rows);
+        case 128:
+            return big ? launch_block<128, 64>(cfg, a, rows) : launch_block<128, 16>(cfg, a, rows);
+        case 256:
+            return big ? launch_block<256, 32>(cfg, a, rows) : launch_block<256, 16>(cfg, a, rows);
+        default:
+            cfg.blockDim = dim3(kRowsPerBlock * 32);
+            return cudaLaunchKernelEx(&cfg, append_kernel<0>, a);
     }
 }
 

@@ -259,14 +259,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_commit(&bars[kBarODone + s]);
                 return true;
             };
+            // S_s(j+1) only needs the softmax to have read S_s(j) (SFree), not its P: issuing both
+            // streams' next QK^T before their PV lets it run under the softmax of tile j.
             if (ok) ok = issue_s(0, 0) && (ns < 2 || issue_s(1, 0));
             for (int j = 0; ok && j < nk; ++j) {
-                if (!issue_pv(0, j)) break;
-                if (j + 1 < nk && !issue_s(0, j + 1)) break;
-                if (ns == 2) {
-                    if (!issue_pv(1, j)) break;
-                    if (j + 1 < nk && !issue_s(1, j + 1)) break;
+                if (j + 1 < nk) {
+                    if (!issue_s(0, j + 1)) break;
+                    if (ns == 2 && !issue_s(1, j + 1)) break;
                 }
+                if (!issue_pv(0, j)) break;
+                if (ns == 2 && !issue_pv(1, j)) break;
                 tc_commit(&bars[kBarKvEmpty + j % kStages]);
             }
             // Every MMA this thread issued must finish before TMEM is released.
@@ -439,35 +441,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                     m_used = mt;
                 }
                 const float m_eff = m_used == -CUDART_INF_F ? 0.f : m_used;
-                // P_s (fp16) into shared memory once PV_s(j-1) no longer reads it.
+                // P_s as packed fp16 in registers first, so that the exponentials overlap the
+                // tensor core's PV_s(j-1); only the stores wait for it to stop reading P_s.
+                float rsum = 0.f;
+                uint32_t pk[32];
+#pragma unroll
+                for (int u = 0; u < 32; ++u) {
+                    float p0, p1;
+                    if constexpr (CAP) {
+                        p0 = v[2 * u] == -CUDART_INF_F ? 0.f : ex2_fast(score_log2<CAP>(v[2 * u], a) - m_eff);
+                        p1 = v[2 * u + 1] == -CUDART_INF_F ? 0.f : ex2_fast(score_log2<CAP>(v[2 * u + 1], a) - m_eff);
+                    } else {
+                        p0 = ex2_fast(fmaf(v[2 * u], a.scale_log2, -m_eff));
+                        p1 = ex2_fast(fmaf(v[2 * u + 1], a.scale_log2, -m_eff));
+                    }
+                    rsum += p0 + p1;
+                    pk[u] = pack_half2(p0, p1);
+                }
                 if (j >= 1 && !waited_o) {
                     if (!mbar_wait(&bars[kBarODone + s], (j - 1) & 1, a.err, kErrMmaTimeout)) {
                         ok = false;
                         break;
                     }
                 }
-                float rsum = 0.f;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    uint32_t pk[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        float p0, p1;
-                        if constexpr (CAP) {
-                            p0 = v[c * 8 + 2 * u] == -CUDART_INF_F ? 0.f
-                                                                    : ex2_fast(score_log2<CAP>(v[c * 8 + 2 * u], a) - m_eff);
-                            p1 = v[c * 8 + 2 * u + 1] == -CUDART_INF_F
-                                     ? 0.f
-                                     : ex2_fast(score_log2<CAP>(v[c * 8 + 2 * u + 1], a) - m_eff);
-                        } else {
-                            p0 = ex2_fast(fmaf(v[c * 8 + 2 * u], a.scale_log2, -m_eff));
-                            p1 = ex2_fast(fmaf(v[c * 8 + 2 * u + 1], a.scale_log2, -m_eff));
-                        }
-                        rsum += p0 + p1;
-                        pk[u] = pack_half2(p0, p1);
-                    }
-                    *reinterpret_cast<uint4 *>(sp + sw128(r, c)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                }
+                for (int c = 0; c < 8; ++c)
+                    *reinterpret_cast<uint4 *>(sp + sw128(r, c)) =
+                        make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
                 // Keys past the range end: zero their V rows so that 0 * (stale data) stays 0
                 // (one warpgroup does it; PV of both streams waits for both P_s arrivals).
                 if (s == 0 && kbase + kTK > khi && r < kTK && kbase + r >= khi) {
