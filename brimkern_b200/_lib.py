@@ -86,6 +86,8 @@ SIGNATURES = [
     ("brk_attn_full", _i, [_vp, _PARAMS, _i, _i, _i, _vp, _vp, _vp, _vp, _vp]),
     ("brk_attn_decode_partial", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp, _vp]),
     ("brk_attn_combine", _i, [_vp, _i, _i, _i, _vp, _vp, _sz, _vp, _vp]),
+    ("brk_proj_qkv", _i, [_vp, _i, _i, _i, _i, _vp, _vp, _d, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    ("brk_proj_out", _i, [_vp, _i, _i, _i, _vp, _vp, _vp, _d, _i, _vp, _vp, _vp]),
     ("brk_peer_create", _i, [_vp, _i, _i, _i, _i, _pp]),
     ("brk_peer_handle", _i, [_vp, _vp, _sz]),
     ("brk_peer_open", _i, [_vp, _i, _vp, _sz]),

@@ -410,6 +410,7 @@ int brk_ctx_destroy(brk_ctx *ctx) {
     cudaFree(ctx->d_err);
     cudaFree(ctx->ws);
     cudaFree(ctx->stage);
+    cudaFree(ctx->act);
     delete ctx;
     return BRK_OK;
 }
@@ -1011,6 +1012,112 @@ int brk_attn_full(brk_ctx *ctx, const brk_attn_params *p, int batch, int n_token
                               (size_t)batch * n_tokens * p->n_heads, cudaMemcpyDeviceToDevice, st);
         if (e != cudaSuccess) return cuda_fail(e, "non-causal output copy");
     }
+    return BRK_OK;
+}
+
+namespace {
+// fp16 weight matrix [n][k] (K-major), boxes [nt][64].
+int make_weight_map(CUtensorMap *m, const uint16_t *w, int n, int k, int nt) {
+    return make_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w, (uint64_t)n, (uint64_t)k, 64u, (uint32_t)nt,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int ensure_act(brk_ctx *ctx, size_t bytes) {
+    if (bytes <= ctx->act_bytes) return BRK_OK;
+    BRK_CUDA(cudaDeviceSynchronize());  // queued kernels may still read the old buffer
+    cudaFree(ctx->act);
+    ctx->act = nullptr;
+    ctx->act_bytes = 0;
+    BRK_CUDA(cudaMalloc(&ctx->act, bytes));
+    ctx->act_bytes = bytes;
+    return BRK_OK;
+}
+
+// Casts `rows` x K activations to fp16 (RMSNorm fused when gain is given) and runs the GEMM over
+// up to three weight matrices.
+int run_proj(brk_ctx *ctx, int rows, int K, const float *x, const float *gain, double eps, int one_plus, int nmat,
+             const int *n, const uint16_t *const *w, float *const *out, const float *const *bias,
+             const float *residual, cudaStream_t st) {
+    int nt = brk::proj_tile_cols(rows);
+    for (int i = 0; i < nmat; ++i)
+        if (n[i] % nt) nt = 32;
+    for (int i = 0; i < nmat; ++i)
+        if (n[i] < 32 || n[i] % 32)
+            return fail(BRK_ERR_UNSUPPORTED, "projection widths must be multiples of 32 (got %d)", n[i]);
+    int rc = ensure_act(ctx, (size_t)rows * K * sizeof(__half));
+    if (rc) return rc;
+    __half *act = static_cast<__half *>(ctx->act);
+    cudaError_t e = brk::launch_norm_cast(x, gain, (float)eps, one_plus, act, rows, K, st);
+    if (e != cudaSuccess) return cuda_fail(e, "activation cast launch");
+    ++ctx->launches;
+    CUtensorMap ta, tw[3];
+    if ((rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, act, (uint64_t)rows, (uint64_t)K, 64u, 128u,
+                       CU_TENSOR_MAP_SWIZZLE_128B)))
+        return rc;
+    brk::ProjArgs a;
+    memset(&a, 0, sizeof(a));
+    a.M = rows;
+    a.K = K;
+    a.nmat = nmat;
+    a.residual = residual;
+    a.err = ctx->d_err;
+    int end = 0;
+    for (int i = 0; i < 3; ++i) {
+        const int j = i < nmat ? i : 0;
+        if ((rc = make_weight_map(&tw[i], w[j], n[j], K, nt))) return rc;
+        if (i < nmat) {
+            end += n[i];
+            a.n_end[i] = end;
+            a.out[i] = out[i];
+            a.bias[i] = bias[i];
+        }
+    }
+    e = brk::launch_proj_gemm(nt, ta, tw, a, st);
+    if (e != cudaSuccess) return cuda_fail(e, "projection GEMM launch");
+    ++ctx->launches;
+    return BRK_OK;
+}
+
+int check_proj(const brk_ctx *ctx, int rows, int K, const float *x, const void *out) {
+    if (!ctx || !x || !out) return fail(BRK_ERR_INVALID, "null argument");
+    if (rows < 1 || K < 8 || K % 8) return fail(BRK_ERR_INVALID, "rows %d / input width %d (a multiple of 8)", rows, K);
+    if ((long long)rows * K >= (1ll << 31)) return fail(BRK_ERR_CAPACITY, "rows * width beyond 2^31");
+    return BRK_OK;
+}
+}  // namespace
+
+int brk_proj_qkv(brk_ctx *ctx, int rows, int d_model, int q_dim, int kv_dim, const float *x, const float *attn_norm,
+                 double eps, int norm_one_plus, const uint16_t *wq, const uint16_t *wk, const uint16_t *wv,
+                 const float *bq, const float *bk, const float *bv, float *q, float *k, float *v, void *stream) {
+    int rc = check_proj(ctx, rows, d_model, x, q);
+    if (rc) return rc;
+    if (!wq || !wk || !wv || !k || !v) return fail(BRK_ERR_INVALID, "null weight or output");
+    DeviceGuard g(ctx->device);
+    const int n[3] = {q_dim, kv_dim, kv_dim};
+    const uint16_t *w[3] = {wq, wk, wv};
+    float *out[3] = {q, k, v};
+    const float *bias[3] = {bq, bk, bv};
+    return run_proj(ctx, rows, d_model, x, attn_norm, eps, norm_one_plus, 3, n, w, out, bias, nullptr,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int brk_proj_out(brk_ctx *ctx, int rows, int q_dim, int d_model, const float *attn, const uint16_t *wo,
+                 const float *post_norm, double eps, int norm_one_plus, const float *x, float *h, void *stream) {
+    int rc = check_proj(ctx, rows, q_dim, attn, h);
+    if (rc) return rc;
+    if (!wo || !x) return fail(BRK_ERR_INVALID, "null weight or residual");
+    if (d_model % 4) return fail(BRK_ERR_INVALID, "d_model %d must be a multiple of 4", d_model);
+    DeviceGuard g(ctx->device);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int n[1] = {d_model};
+    const uint16_t *w[1] = {wo};
+    float *out[1] = {h};
+    const float *bias[1] = {nullptr};
+    rc = run_proj(ctx, rows, q_dim, attn, nullptr, 0.0, 0, 1, n, w, out, bias, post_norm ? nullptr : x, st);
+    if (rc || !post_norm) return rc;
+    cudaError_t e = brk::launch_post_norm_residual(h, x, post_norm, (float)eps, norm_one_plus, rows, d_model, st);
+    if (e != cudaSuccess) return cuda_fail(e, "post-norm launch");
+    ++ctx->launches;
     return BRK_OK;
 }
 

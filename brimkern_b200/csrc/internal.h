@@ -19,6 +19,8 @@ struct brk_ctx {
     size_t ws_bytes = 0;
     void *stage = nullptr;     // fp16 staging of an int8 cache layer for the prefill kernel
     size_t stage_bytes = 0;
+    void *act = nullptr;       // fp16 activations of the projection GEMMs
+    size_t act_bytes = 0;
     uint64_t launches = 0;     // kernels launched through this context
 };
 
@@ -125,6 +127,18 @@ struct PrefillArgs {
     int past_len[BRK_MAX_BATCH];
 };
 
+// Projection GEMM (proj.cu): out[i] [M][n_i] = A [M][K] . W_i^T (+ bias_i) (+ residual for
+// matrix 0), for up to three weight matrices W_i [n_i][K] concatenated along the output columns
+// (n_end: cumulative ends).
+struct ProjArgs {
+    int M, K, nmat;
+    int n_end[3];
+    float *out[3];
+    const float *bias[3];
+    const float *residual;
+    int *err;
+};
+
 struct CombineArgs {
     const float *part_ml, *part_o;
     size_t stride_ml, stride_o;  // floats between consecutive parts
@@ -178,6 +192,14 @@ cudaError_t launch_kv_read_q8(const uint8_t *kc, const uint8_t *vc, const float 
 // [B][Hkv][rows][D] (K and V), for the tensor-core prefill kernel.
 cudaError_t launch_kv_dequant(const uint8_t *kc, const uint8_t *vc, const float *sc, __half *k, __half *v, int layer,
                               int B, int n_kv_heads, int head_dim, int cap, int pitch, int rows, cudaStream_t s);
+
+// Projections (proj.cu).  proj_tile_cols: output columns per CTA for M rows (32 or 128).
+int proj_tile_cols(int rows);
+cudaError_t launch_norm_cast(const float *x, const float *gain, float eps, int one_plus, __half *out, int rows, int K,
+                             cudaStream_t s);
+cudaError_t launch_post_norm_residual(float *h, const float *x, const float *gain, float eps, int one_plus, int rows,
+                                      int n, cudaStream_t s);
+cudaError_t launch_proj_gemm(int nt, const CUtensorMap &ta, const CUtensorMap *tw, const ProjArgs &a, cudaStream_t s);
 
 // Non-causal attention staging (full.cu): token-major f32 [B][L][H][D] K/V -> head-major fp16
 // [B][H][L][Dp] (zero-padded head dim), and f32 rows [rows][D] -> [rows][Dp] zero-padded.

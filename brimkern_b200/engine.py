@@ -597,6 +597,29 @@ class AttentionEngine:
         check(L.lib().brk_attn_decode_partial(self.ctx.handle, kv.handle, layer, ctypes.byref(p), B, T, pos, _ptr(q),
                                               _ptr(part_ml), _ptr(part_o), _stream_ptr(stream)))
 
+    # ---- the projections either side of the operator (recordLayerKV, kernels.ts:1700-1736) -----
+    def projQkv(self, x: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor, wv: torch.Tensor,
+                q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, attn_norm: Optional[torch.Tensor] = None,
+                eps: float = 1e-6, one_plus: bool = False, bq=None, bk=None, bv=None, stream=None):
+        """n1 = rmsnorm(x, attn_norm); q / k / v = n1 W^T (+ bias).  x [rows, d] f32, weights
+        [n, d] fp16, outputs [rows, n] f32."""
+        rows, d = x.shape[0], x.shape[-1]
+        check(L.lib().brk_proj_qkv(self.ctx.handle, rows, d, wq.shape[0], wk.shape[0], _ptr(x.contiguous()),
+                                   _ptr(attn_norm), float(eps), int(bool(one_plus)), _ptr(wq.contiguous()),
+                                   _ptr(wk.contiguous()), _ptr(wv.contiguous()), _ptr(bq), _ptr(bk), _ptr(bv), _ptr(q),
+                                   _ptr(k), _ptr(v), _stream_ptr(stream)))
+        return q, k, v
+
+    def projOut(self, attn: torch.Tensor, wo: torch.Tensor, x: torch.Tensor, h: torch.Tensor,
+                post_norm: Optional[torch.Tensor] = None, eps: float = 1e-6, one_plus: bool = False, stream=None):
+        """h = x + attn Wo^T (Gemma-2: x + rmsnorm(attn Wo^T, post_norm)).  attn [rows, q_dim],
+        wo [d, q_dim] fp16, x / h [rows, d] f32."""
+        rows, q_dim = attn.shape[0], attn.shape[-1]
+        check(L.lib().brk_proj_out(self.ctx.handle, rows, q_dim, wo.shape[0], _ptr(attn.contiguous()),
+                                   _ptr(wo.contiguous()), _ptr(post_norm), float(eps), int(bool(one_plus)),
+                                   _ptr(x.contiguous()), _ptr(h), _stream_ptr(stream)))
+        return h
+
     def decodePush(self, kv: KvCache, layer: int, cfg: AttnConfig, q: torch.Tensor, peer: PeerArea, epoch: int,
                    past_len, stream=None) -> None:
         """Split-KV partial of this cache's rows, stored into every rank's exchange area."""

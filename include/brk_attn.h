@@ -233,6 +233,25 @@ int brk_attn_decode_partial(brk_ctx *ctx, const brk_kv *kv, int layer,
 int brk_attn_combine(brk_ctx *ctx, int n_parts, int rows, int head_dim, const float *part_ml,
                      const float *part_o, size_t part_stride, float *out, void *stream);
 
+/* ---- the projections either side of the operator (recordLayerKV, kernels.ts:1700-1736) -------
+ * The layer-input RMSNorm with the q / k / v projections that feed brk_attn_append / step, and
+ * the output projection with the residual add that consumes the attention output, as tensor-core
+ * GEMMs.  Weights are the engine's fp16 matrices [n][k] (matmul_t_f16w: C = A W^T), passed as
+ * raw fp16 bits; activations are f32 [rows][width] (rows = batch * n_tokens) and are cast to
+ * fp16 for the tensor cores.  Widths: d_model / q_dim multiples of 8 as inputs, projection
+ * outputs multiples of 32.
+ *   brk_proj_qkv: n1 = rmsnorm(x, attn_norm) (attn_norm NULL: no norm), q = n1 wq^T (+ bq), k, v
+ *   likewise (biases may be NULL).
+ *   brk_proj_out: h = x + o where o = attn wo^T, or rmsnorm(o, post_norm) when post_norm is given
+ *   (Gemma-2's post-attention norm).  h may not alias x. */
+int brk_proj_qkv(brk_ctx *ctx, int rows, int d_model, int q_dim, int kv_dim, const float *x,
+                 const float *attn_norm, double eps, int norm_one_plus, const uint16_t *wq,
+                 const uint16_t *wk, const uint16_t *wv, const float *bq, const float *bk,
+                 const float *bv, float *q, float *k, float *v, void *stream);
+int brk_proj_out(brk_ctx *ctx, int rows, int q_dim, int d_model, const float *attn, const uint16_t *wo,
+                 const float *post_norm, double eps, int norm_one_plus, const float *x, float *h,
+                 void *stream);
+
 /* ---- sequence-sharded decode over peer memory (extension, no reference counterpart) ---------
  * The fused form of decode_partial + all-gather + combine for one process per GPU: each rank's
  * decode kernel stores its final partials straight into every rank's exchange area (plain

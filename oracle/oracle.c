@@ -234,6 +234,18 @@ void brk_oracle_attention_full(const float *q, const float *k, const float *v, i
     free(s);
 }
 
+/* matmulCpu (kernels.ts:3384-3392) in the GPU's weight layout (matmul_t, shaders.ts:28-43):
+ * o[r][c] = f32(sum_i a[r][i] * w[c][i]) with the sum in double, w [n][k]. */
+void brk_oracle_matmul_t(const float *a, const float *w, int m, int k, int n, float *o) {
+    for (int r = 0; r < m; r++)
+        for (int c = 0; c < n; c++) {
+            double s = 0;
+            const float *ar = a + (long long)r * k, *wr = w + (long long)c * k;
+            for (int i = 0; i < k; i++) s += (double)ar[i] * (double)wr[i];
+            o[(long long)r * n + c] = (float)s;
+        }
+}
+
 /* quantize_kv shader (shaders.ts:1673-1705), in the shader's own f32 arithmetic:
  * amax over the head's D values, scale = amax == 0 ? 1e-8 : amax/127, inv = 1/scale,
  * code = clamp(round(x*inv), -127, 127) with WGSL round() = round-half-to-even (rintf). */

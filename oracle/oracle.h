@@ -62,6 +62,9 @@ void brk_oracle_attention_partial(const float *q, const float *k, const float *v
 void brk_oracle_combine(const double *m, const double *l, const double *o, int n_parts,
                         int rows, int head_dim, float *out);
 
+/* matmulCpu (kernels.ts:3384) with [n][k] weights (matmul_t): o = a w^T, double sums. */
+void brk_oracle_matmul_t(const float *a, const float *w, int m, int k, int n, float *o);
+
 /* Non-causal attention as the attention_full gate computes it (kernels.ts:3168-3177). */
 void brk_oracle_attention_full(const float *q, const float *k, const float *v, int n_tokens,
                                int n_heads, int n_kv_heads, int head_dim, int kv_len,

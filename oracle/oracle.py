@@ -45,6 +45,7 @@ def lib():
         L.brk_oracle_attention_partial.argtypes = ([_f32p, _f32p, _f32p] + [ctypes.c_int] * 5 + [ctypes.c_double, ctypes.c_double]
                                                    + [ctypes.c_int] * 3 + [_f64p, _f64p, _f64p])
         L.brk_oracle_combine.argtypes = [_f64p, _f64p, _f64p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p]
+        L.brk_oracle_matmul_t.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p]
         L.brk_oracle_attention_full.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                 ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_double, _f32p]
         L.brk_oracle_quantize_kv.argtypes = [_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _i8p, _f32p]
@@ -128,6 +129,15 @@ def combine(m, l, o, n_parts, rows, head_dim):
     out = np.zeros(rows * head_dim, np.float32)
     lib().brk_oracle_combine(mp, lp, op, n_parts, rows, head_dim, out.ctypes.data_as(_f32p))
     return out
+
+
+def matmul_t(a, w, m, k, n):
+    """matmulCpu (kernels.ts:3384) with [n][k] weights: a [m][k] . w^T, double sums."""
+    a, ap = _f32(a)
+    w, wp = _f32(w)
+    o = np.zeros(m * n, np.float32)
+    lib().brk_oracle_matmul_t(ap, wp, m, k, n, o.ctypes.data_as(_f32p))
+    return o
 
 
 def attention_full(q, k, v, n_tokens, n_heads, n_kv_heads, head_dim, kv_len, scale=None, softcap=0.0):
