@@ -35,16 +35,16 @@ sys.path.insert(0, ROOT)
 CONFIGS = {
     # BASELINE config 2 at batch 64 (the north-star target shape).
     "qwen3-4b": dict(layers=36, Hq=32, Hkv=8, D=128, L=4096, base=1e6, qk_norm=True, batch=64, scale=None,
-                     softcap=0.0, window_even=0, ff=None),
+                     softcap=0.0, window_even=0, ff=None, d_model=2560),
     # BASELINE config 4.
     "gemma2-2b": dict(layers=26, Hq=8, Hkv=4, D=256, L=8192, base=1e4, qk_norm=False, batch=32, scale=1 / 16,
-                      softcap=50.0, window_even=4096, ff=None),
+                      softcap=50.0, window_even=4096, ff=None, d_model=2304),
     # 2048-token prompt in 512-token chunks on the tensor-core prefill kernel.
     "qwen3-4b-prefill": dict(layers=36, Hq=32, Hkv=8, D=128, L=2048, chunk=512, base=1e6, qk_norm=True, batch=4,
                              scale=None, softcap=0.0, window_even=0, ff=None, prefill=True),
     # BASELINE config 5 on one GPU (the long-context shape; sequence sharding is the multi-GPU form).
     "llama3.2-1b-long": dict(layers=16, Hq=32, Hkv=8, D=64, L=131072, base=5e5, qk_norm=False, batch=8, scale=None,
-                             softcap=0.0, window_even=0, ff=(32.0, 1.0, 4.0, 8192)),
+                             softcap=0.0, window_even=0, ff=(32.0, 1.0, 4.0, 8192), d_model=2048),
 }
 
 
@@ -60,6 +60,12 @@ def kv_bytes_per_step(c, batch):
             keys = min(keys, c["window_even"])
         total += batch * keys * c["Hkv"] * row_bytes * 2
     return total
+
+
+def weight_bytes_per_step(c):
+    """fp16 q/k/v and output projection weights of every layer (read once per decode step)."""
+    d, qd, kvd = c["d_model"], c["Hq"] * c["D"], c["Hkv"] * c["D"]
+    return c["layers"] * (qd + 2 * kvd + qd) * d * 2
 
 
 def prefill_flops(c, batch):
@@ -488,6 +494,212 @@ def cpu_reference_sample(c, batch, target_s, threads=0, seed=7):
     return gbs, used, desc
 
 
+def cpu_slice_sample(c, target_s, pool=8, seed=11):
+    """CPU attention slice (oracle rmsnormCpu + matmulCpu + attentionCpu + matmulCpu) of one layer
+    for `pool` sequences, repeated for about target_s seconds.  Returns (GB/s, threads, desc) with
+    the bytes counted as the fp16 weights of the layer plus the fp16 KV of those sequences."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(seed)
+    d, Hq, Hkv, D, keys = c["d_model"], c["Hq"], c["Hkv"], c["D"], c["L"]
+    qd, kvd = Hq * D, Hkv * D
+    w_qkv = (rng.standard_normal((qd + 2 * kvd, d), dtype=np.float32) / np.sqrt(d)).astype(np.float32)
+    w_o = (rng.standard_normal((d, qd), dtype=np.float32) / np.sqrt(qd)).astype(np.float32)
+    g = np.ones(d, np.float32)
+    x = rng.standard_normal((pool, d), dtype=np.float32)
+    k = rng.standard_normal(pool * keys * kvd, dtype=np.float32)
+    v = rng.standard_normal(pool * keys * kvd, dtype=np.float32)
+    stride = keys * kvd
+
+    def once():
+        n1 = O.rmsnorm(x.ravel(), g, pool, d, 1e-6)
+        qkv = O.matmul_t(n1, w_qkv, pool, d, qd + 2 * kvd).reshape(pool, -1)
+        q = np.ascontiguousarray(qkv[:, :qd]).ravel()
+        att, used = O.attention_batch(q, k, v, pool, stride, 1, Hq, Hkv, D, [keys - 1] * pool, c["scale"],
+                                      c["softcap"], 0, 0)
+        O.matmul_t(att, w_o, pool, qd, d)
+        return used
+
+    t0 = time.perf_counter()
+    used = once()
+    reps = max(1, int(target_s / max(time.perf_counter() - t0, 1e-3)))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        once()
+    dt = time.perf_counter() - t0
+    units = reps
+    byts = units * ((qd + 2 * kvd + qd) * d * 2 + pool * keys * kvd * 2 * 2)
+    desc = (f"{units} single-layer slices of {pool} sequences at KV length {keys}: rmsnormCpu + matmulCpu "
+            f"(double sums, one thread) + attentionCpu ({used} threads) + matmulCpu, {dt:.1f} s; bytes counted as "
+            f"the fp16 weights of the layer + the fp16 KV of those sequences")
+    return byts / dt / 1e9, used, desc
+
+
+def run_slice(args, c, workload):
+    """The attention slice of a decode step (recordLayerKV, kernels.ts:1700-1736): per layer,
+    RMSNorm + q/k/v projections, QK-norm + RoPE + append + decode attention, output projection +
+    residual.  value = (fp16 weights + KV) bytes per step / step time."""
+    import torch
+
+    from brimkern_b200.engine import AttentionEngine, AttnConfig, KvCache, RopeTable, llama3_rope_factors
+
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("--slice runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, Lkv, layers = args.batch, c["L"], c["layers"]
+    Hq, Hkv, D, d = c["Hq"], c["Hkv"], c["D"], c["d_model"]
+    qd, kvd = Hq * D, Hkv * D
+    eng = AttentionEngine(0)
+    ff = llama3_rope_factors(D, c["base"], *c["ff"]) if c["ff"] else None
+    rope = RopeTable(eng.ctx, D, c["base"], ff, Lkv)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3000)
+    qn = kn = None
+    if c["qk_norm"]:
+        qn = (1 + 0.02 * torch.randn(D, generator=gen, device=dev)).float()
+        kn = (1 + 0.02 * torch.randn(D, generator=gen, device=dev)).float()
+    cfgs = [AttnConfig(Hq, Hkv, D, scale=c["scale"], softcap=c["softcap"],
+                       window=c["window_even"] if (c["window_even"] and l % 2 == 0) else 0, q_norm=qn, k_norm=kn,
+                       rope=rope) for l in range(layers)]
+
+    def w(n, k):
+        return (torch.randn((n, k), generator=gen, device=dev) / k ** 0.5).half()
+
+    wq = [w(qd, d) for _ in range(layers)]
+    wk = [w(kvd, d) for _ in range(layers)]
+    wv = [w(kvd, d) for _ in range(layers)]
+    wo = [w(d, qd) for _ in range(layers)]
+    g1 = [(1 + 0.02 * torch.randn(d, generator=gen, device=dev)).float() for _ in range(layers)]
+    kv = KvCache(eng.ctx, layers, B, Hkv, D, Lkv)
+    tmp_k = torch.empty((Lkv, Hkv, D), dtype=torch.float32, device=dev)
+    tmp_v = torch.empty_like(tmp_k)
+    for layer in range(layers):
+        for b in range(B):
+            tmp_k.normal_(generator=gen)
+            tmp_v.normal_(generator=gen)
+            kv.write_rows(layer, b, 0, tmp_k, tmp_v)
+    del tmp_k, tmp_v
+    past = [Lkv - 1] * B
+    x = torch.randn((layers, B, d), generator=gen, device=dev)
+    h = torch.empty_like(x)
+    q = torch.empty((B, qd), device=dev)
+    k = torch.empty((B, kvd), device=dev)
+    v = torch.empty_like(k)
+    q_work = torch.empty((B, 1, Hq, D), device=dev)
+    att = torch.empty((B, 1, Hq, D), device=dev)
+    eng.ctx.reserve(64 << 20)
+    stream = torch.cuda.current_stream()
+
+    def layer_slice(layer, xi, hi, ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        eng.projQkv(xi, wq[layer], wk[layer], wv[layer], q, k, v, attn_norm=g1[layer], eps=1e-6)
+        if ev is None:
+            eng.attentionLayer(kv, layer, cfgs[layer], q.view(B, 1, Hq, D), k.view(B, 1, Hkv, D),
+                               v.view(B, 1, Hkv, D), past, q_work, att)
+        else:
+            ev[1].record(stream)
+            eng.appendKv(kv, layer, cfgs[layer], q.view(B, 1, Hq, D), k.view(B, 1, Hkv, D), v.view(B, 1, Hkv, D),
+                         q_work, past)
+            ev[2].record(stream)
+            eng.recAttention(kv, layer, cfgs[layer], q_work, att, past)
+            ev[3].record(stream)
+        eng.projOut(att.view(B, qd), wo[layer], xi, hi)
+        if ev is not None:
+            ev[4].record(stream)
+
+    def step(ev=None):
+        for layer in range(layers):
+            layer_slice(layer, x[layer], h[layer], None if ev is None else ev[layer])
+
+    for _ in range(args.warmup):
+        step()
+    eng.ctx.check()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(0)
+    sampler.start()
+    time.sleep(0.3)
+    n0 = eng.ctx.launches
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = eng.ctx.launches - n0
+    clocks = sampler.stop()
+    eng.ctx.check()
+    ms_step = e0.elapsed_time(e1) / args.steps
+    rsteps = max(2, min(args.steps, 5))
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(layers)] for _ in range(rsteps)]
+    for si in range(rsteps):
+        step(ev[si])
+    torch.cuda.synchronize()
+    eng.ctx.check()
+    n = rsteps * layers
+    proj_ms = sum(e[0].elapsed_time(e[1]) + e[3].elapsed_time(e[4]) for es in ev for e in es) / n
+    attn_ms = sum(e[2].elapsed_time(e[3]) for es in ev for e in es) / n
+    wbytes = weight_bytes_per_step(c)
+    kbytes = kv_bytes_per_step(c, B)
+    value = (wbytes + kbytes) / (ms_step * 1e-3) / 1e9
+    peak, peak_kind = load_peak()
+    wl = wbytes / layers
+    proj_ach = wl / (proj_ms * 1e-3) / 1e9
+    attn_ach = kbytes / layers / (attn_ms * 1e-3) / 1e9
+    e2e = None
+    if not args.no_e2e:
+        hx = x.cpu().pin_memory()
+        hh = torch.empty(h.shape, dtype=torch.float32, pin_memory=True)
+        dx, dh = torch.empty_like(x), torch.empty_like(h)
+        pipe = CopyPipeline(dev, layers)
+
+        def e2e_step():
+            pipe.run(stream, layers, lambda l: dx[l].copy_(hx[l], non_blocking=True),
+                     lambda l: layer_slice(l, dx[l], dh[l]), lambda l: hh[l].copy_(dh[l], non_blocking=True))
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        e_step = f0.elapsed_time(f1) / args.steps
+        e2e = {"value": round((wbytes + kbytes) / (e_step * 1e-3) / 1e9, 2), "unit": "GB/s",
+               "h2d_bytes_per_step": int(hx.numel() * 4), "d2h_bytes_per_step": int(hh.numel() * 4),
+               "ms_per_step": round(e_step, 4), "tokens_per_s": round(B / (e_step * 1e-3), 1)}
+        eng.ctx.check()
+    cpu = None
+    if not args.no_cpu:
+        gbs, used, desc = cpu_slice_sample(c, 10.0)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": used, "kind": "port", "sample": desc}
+    line = {
+        "metric": "decode attention-slice GB/s (weights + KV)", "value": round(value, 2), "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 weights + f16 KV / f32 accumulate", "data": "synthetic (random-init weights)",
+        "config": {"workload": workload + "-slice", "global_batch": B, "kv_len": Lkv, "layers": layers,
+                   "d_model": d, "heads": f"{Hq}q/{Hkv}kv", "head_dim": D, "parallelism": "single GPU",
+                   "l2": f"no flush: each step streams {(wbytes + kbytes) / 1e9:.1f} GB > 126 MB L2"},
+        "tokens_per_s": round(B / (ms_step * 1e-3), 1),
+        "roofline": {"bound": "hbm", "achieved": round(proj_ach, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(proj_ach / peak, 4), "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "projections (norm_cast + proj_kernel, q/k/v and output)",
+                     "timing": f"CUDA events around projQkv and projOut, {rsteps} steps",
+                     "bytes_per_layer": wl, "proj_ms_per_layer": round(proj_ms, 5),
+                     "attention_ms_per_layer": round(attn_ms, 5), "attention_achieved_gbs": round(attn_ach, 1)},
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    eng.close()
+    return 0
+
+
 def run_reference(args, c, workload):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -531,6 +743,9 @@ def main():
                     help="KV cache type: fp16, or the reference's int8 mode (setKvQuant)")
     ap.add_argument("--sharded-nccl", action="store_true",
                     help="llama3.2-1b-long on N>1 GPUs: exchange partials with NCCL all-gathers (baseline)")
+    ap.add_argument("--slice", action="store_true",
+                    help="decode workloads: the whole attention slice (RMSNorm + q/k/v projections, attention, "
+                         "output projection + residual) on one GPU")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
@@ -551,6 +766,8 @@ def main():
         return run_reference(args, c, workload)
     if c.get("prefill"):
         return run_prefill(args, c, workload)
+    if args.slice:
+        return run_slice(args, c, workload)
     if workload == "llama3.2-1b-long" and int(os.environ.get("WORLD_SIZE", "1")) > 1:
         return run_sharded(args, c, workload)
 

@@ -1038,20 +1038,17 @@ int ensure_act(brk_ctx *ctx, size_t bytes) {
 int run_proj(brk_ctx *ctx, int rows, int K, const float *x, const float *gain, double eps, int one_plus, int nmat,
              const int *n, const uint16_t *const *w, float *const *out, const float *const *bias,
              const float *residual, cudaStream_t st) {
-    int nt = brk::proj_tile_cols(rows);
+    const int ntok = brk::proj_token_tile(rows);
     for (int i = 0; i < nmat; ++i)
-        if (n[i] % nt) nt = 32;
-    for (int i = 0; i < nmat; ++i)
-        if (n[i] < 32 || n[i] % 32)
-            return fail(BRK_ERR_UNSUPPORTED, "projection widths must be multiples of 32 (got %d)", n[i]);
+        if (n[i] < 1) return fail(BRK_ERR_INVALID, "projection width %d", n[i]);
     int rc = ensure_act(ctx, (size_t)rows * K * sizeof(__half));
     if (rc) return rc;
     __half *act = static_cast<__half *>(ctx->act);
     cudaError_t e = brk::launch_norm_cast(x, gain, (float)eps, one_plus, act, rows, K, st);
     if (e != cudaSuccess) return cuda_fail(e, "activation cast launch");
     ++ctx->launches;
-    CUtensorMap ta, tw[3];
-    if ((rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, act, (uint64_t)rows, (uint64_t)K, 64u, 128u,
+    CUtensorMap tx, tw[3];
+    if ((rc = make_map(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, act, (uint64_t)rows, (uint64_t)K, 64u, (uint32_t)ntok,
                        CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
     brk::ProjArgs a;
@@ -1064,15 +1061,16 @@ int run_proj(brk_ctx *ctx, int rows, int K, const float *x, const float *gain, d
     int end = 0;
     for (int i = 0; i < 3; ++i) {
         const int j = i < nmat ? i : 0;
-        if ((rc = make_weight_map(&tw[i], w[j], n[j], K, nt))) return rc;
+        if ((rc = make_weight_map(&tw[i], w[j], n[j], K, 128))) return rc;
         if (i < nmat) {
-            end += n[i];
-            a.n_end[i] = end;
+            end += (n[i] + 127) / 128;
+            a.tile_end[i] = end;
+            a.n[i] = n[i];
             a.out[i] = out[i];
             a.bias[i] = bias[i];
         }
     }
-    e = brk::launch_proj_gemm(nt, ta, tw, a, st);
+    e = brk::launch_proj(ntok, tx, tw, a, ctx->num_sms, st);
     if (e != cudaSuccess) return cuda_fail(e, "projection GEMM launch");
     ++ctx->launches;
     return BRK_OK;

@@ -132,10 +132,12 @@ struct PrefillArgs {
 // (n_end: cumulative ends).
 struct ProjArgs {
     int M, K, nmat;
-    int n_end[3];
-    float *out[3];
-    const float *bias[3];
-    const float *residual;
+    int tile_end[3];          // cumulative 128-feature tiles per weight matrix
+    int n[3];                 // output features of each matrix
+    float *out[3];            // [M][n[i]] f32
+    const float *bias[3];     // [n[i]] or null
+    const float *residual;    // [M][n[0]] added to matrix 0 (or null)
+    int kps;                  // k steps (of 64) per split, set by the launcher
     int *err;
 };
 
@@ -193,13 +195,14 @@ cudaError_t launch_kv_read_q8(const uint8_t *kc, const uint8_t *vc, const float 
 cudaError_t launch_kv_dequant(const uint8_t *kc, const uint8_t *vc, const float *sc, __half *k, __half *v, int layer,
                               int B, int n_kv_heads, int head_dim, int cap, int pitch, int rows, cudaStream_t s);
 
-// Projections (proj.cu).  proj_tile_cols: output columns per CTA for M rows (32 or 128).
-int proj_tile_cols(int rows);
+// Projections (proj.cu).  proj_token_tile: tokens per CTA (the MMA N) for M rows: 32..256.
+int proj_token_tile(int rows);
 cudaError_t launch_norm_cast(const float *x, const float *gain, float eps, int one_plus, __half *out, int rows, int K,
                              cudaStream_t s);
 cudaError_t launch_post_norm_residual(float *h, const float *x, const float *gain, float eps, int one_plus, int rows,
                                       int n, cudaStream_t s);
-cudaError_t launch_proj_gemm(int nt, const CUtensorMap &ta, const CUtensorMap *tw, const ProjArgs &a, cudaStream_t s);
+cudaError_t launch_proj(int ntok, const CUtensorMap &tx, const CUtensorMap *tw, const ProjArgs &a, int sms,
+                        cudaStream_t s);
 
 // Non-causal attention staging (full.cu): token-major f32 [B][L][H][D] K/V -> head-major fp16
 // [B][H][L][Dp] (zero-padded head dim), and f32 rows [rows][D] -> [rows][Dp] zero-padded.
