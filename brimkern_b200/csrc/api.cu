@@ -1040,14 +1040,11 @@ int run_proj(brk_ctx *ctx, int rows, int K, const float *x, const float *gain, d
              const float *residual, cudaStream_t st) {
     const int ntok = brk::proj_token_tile(rows);
     for (int i = 0; i < nmat; ++i)
-        if (n[i] < 1) return fail(BRK_ERR_INVALID, "projection width %d", n[i]);
+        if (n[i] < 4 || n[i] % 4) return fail(BRK_ERR_INVALID, "projection width %d (a multiple of 4)", n[i]);
     int rc = ensure_act(ctx, (size_t)rows * K * sizeof(__half));
     if (rc) return rc;
     __half *act = static_cast<__half *>(ctx->act);
-    cudaError_t e = brk::launch_norm_cast(x, gain, (float)eps, one_plus, act, rows, K, st);
-    if (e != cudaSuccess) return cuda_fail(e, "activation cast launch");
-    ++ctx->launches;
-    CUtensorMap tx, tw[3];
+    CUtensorMap tx, tw[3], to[3];
     if ((rc = make_map(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, act, (uint64_t)rows, (uint64_t)K, 64u, (uint32_t)ntok,
                        CU_TENSOR_MAP_SWIZZLE_128B)))
         return rc;
@@ -1062,6 +1059,10 @@ int run_proj(brk_ctx *ctx, int rows, int K, const float *x, const float *gain, d
     for (int i = 0; i < 3; ++i) {
         const int j = i < nmat ? i : 0;
         if ((rc = make_weight_map(&tw[i], w[j], n[j], K, 128))) return rc;
+        // Output [rows][n] f32, box [32 tokens][128 features], no swizzle (the staging layout).
+        if ((rc = make_map(&to[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, out[j], (uint64_t)rows, (uint64_t)n[j], 128u, 32u,
+                           CU_TENSOR_MAP_SWIZZLE_NONE)))
+            return rc;
         if (i < nmat) {
             end += (n[i] + 127) / 128;
             a.tile_end[i] = end;
@@ -1070,7 +1071,11 @@ int run_proj(brk_ctx *ctx, int rows, int K, const float *x, const float *gain, d
             a.bias[i] = bias[i];
         }
     }
-    e = brk::launch_proj(ntok, tx, tw, a, ctx->num_sms, st);
+    brk::proj_plan(a, ntok, ctx->num_sms);
+    cudaError_t e = brk::launch_norm_cast(x, gain, (float)eps, one_plus, act, rows, K, a, st);
+    if (e != cudaSuccess) return cuda_fail(e, "activation cast launch");
+    ++ctx->launches;
+    e = brk::launch_proj(ntok, tx, tw, to, a, st);
     if (e != cudaSuccess) return cuda_fail(e, "projection GEMM launch");
     ++ctx->launches;
     return BRK_OK;

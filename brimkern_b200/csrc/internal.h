@@ -137,7 +137,7 @@ struct ProjArgs {
     float *out[3];            // [M][n[i]] f32
     const float *bias[3];     // [n[i]] or null
     const float *residual;    // [M][n[0]] added to matrix 0 (or null)
-    int kps;                  // k steps (of 64) per split, set by the launcher
+    int splits, kps;          // split-K factor and k steps (of 64) per split (proj_plan)
     int *err;
 };
 
@@ -195,14 +195,16 @@ cudaError_t launch_kv_read_q8(const uint8_t *kc, const uint8_t *vc, const float 
 cudaError_t launch_kv_dequant(const uint8_t *kc, const uint8_t *vc, const float *sc, __half *k, __half *v, int layer,
                               int B, int n_kv_heads, int head_dim, int cap, int pitch, int rows, cudaStream_t s);
 
-// Projections (proj.cu).  proj_token_tile: tokens per CTA (the MMA N) for M rows: 32..256.
+// Projections (proj.cu).  proj_token_tile: tokens per CTA (the MMA N) for M rows: 32..256;
+// proj_plan sets a.splits / a.kps; launch_norm_cast also pre-fills the outputs when a.splits > 1.
 int proj_token_tile(int rows);
+void proj_plan(ProjArgs &a, int ntok, int sms);
 cudaError_t launch_norm_cast(const float *x, const float *gain, float eps, int one_plus, __half *out, int rows, int K,
-                             cudaStream_t s);
+                             const ProjArgs &a, cudaStream_t s);
 cudaError_t launch_post_norm_residual(float *h, const float *x, const float *gain, float eps, int one_plus, int rows,
                                       int n, cudaStream_t s);
-cudaError_t launch_proj(int ntok, const CUtensorMap &tx, const CUtensorMap *tw, const ProjArgs &a, int sms,
-                        cudaStream_t s);
+cudaError_t launch_proj(int ntok, const CUtensorMap &tx, const CUtensorMap *tw, const CUtensorMap *to,
+                        const ProjArgs &a, cudaStream_t s);
 
 // Non-causal attention staging (full.cu): token-major f32 [B][L][H][D] K/V -> head-major fp16
 // [B][H][L][Dp] (zero-padded head dim), and f32 rows [rows][D] -> [rows][Dp] zero-padded.

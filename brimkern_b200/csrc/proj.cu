@@ -9,17 +9,21 @@
 //   - the weight rows are the MMA's M (128 output features per CTA, TMEM lane = feature) and the
 //     tokens its N (32..256 per CTA, TMEM column = token), so a decode step with a few dozen tokens
 //     wastes no MMA rows and every CTA streams 16 KB of weights per 64-wide k step;
-//   - when the output tiles cannot fill the SMs (decode), K is split over a thread-block cluster of
-//     up to 8 CTAs along z; each CTA parks its partial in its own shared memory and then sums one
-//     slice of the tokens over all the cluster's partials through distributed shared memory, in
-//     split order (deterministic, no global workspace, no atomics);
+//   - when the output tiles cannot fill the SMs (decode), K is split over up to 8 CTAs along z;
+//     the activation-cast kernel first fills the outputs with the bias (or the residual), and every
+//     split adds its partial with a TMA reduce-add (cp.reduce.async.bulk.tensor ... .add, f32 in
+//     L2).  The order of those adds is not fixed, so split-K results may differ in the last bit
+//     from run to run; with one split the epilogue stores with a plain TMA store;
 //   - warp 4 streams [128 features][64 k] weight boxes and [tokens][64 k] activation boxes
 //     through a TMA ring (128-byte swizzle, CTA-local loads); the weight loads of the first ring
 //     are issued before griddepcontrol.wait, so they overlap the kernel that produced the
 //     activations (programmatic dependent launch);
 //   - warp 5 issues tcgen05.mma (M 128, N tokens, K 16; fp16 in, fp32 in TMEM) and commits each
-//     stage back to the producer; warps 0-3 (thread r <-> feature r) drain TMEM with tcgen05.ld and
-//     store f32 outputs plus bias and residual, 32 consecutive features per warp store.
+//     stage back to the producer; warps 0-3 (thread r <-> feature r) drain TMEM with tcgen05.ld
+//     32 tokens at a time into a [32 tokens][128 features] f32 staging tile (double-buffered in the
+//     idle ring) that one thread hands to the TMA engine.
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 #include "tcgen05.cuh"
@@ -46,27 +50,29 @@ struct ProjLayout {
     static constexpr int kCtasPerSm = NTOK <= 64 ? 2 : 1;  // resident CTAs per SM the ring allows
     static constexpr uint32_t kBarOff = kStages * kStageBytes;
     static constexpr uint32_t kSmemBytes = 1024 + kBarOff + (2 * kStages + 1) * 8 + 16;
-    // The split-K partial [NTOK][128] f32 reuses the ring once the MMAs are done.
-    static_assert(NTOK * kFM * 4 <= kBarOff, "partial does not fit the ring");
+    // Two [32 tokens][128 features] f32 staging tiles reuse the ring once the MMAs are done.
+    static constexpr uint32_t kOutTile = 32 * kFM * 4;
+    static_assert(2 * kOutTile <= kBarOff, "staging tiles do not fit the ring");
 };
 
-// Cluster barrier without release semantics: orders nothing, only waits for every thread of the
-// cluster (so pending global stores are not drained first).
-__device__ __forceinline__ void cluster_sync_relaxed() {
-    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+// TMA store / reduce-add of a shared-memory box into the tensor at (x, y), in this thread's bulk
+// group.  x * 4 bytes must be a multiple of 16.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_addr(src)), "r"(x), "r"(y)
+                 : "memory");
 }
-
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const void *src, int x, int y) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_addr(src)), "r"(x), "r"(y)
+                 : "memory");
 }
-
-// Generic address of the same shared-memory location in cluster CTA `rank` (plain loads then
-// read that CTA's shared memory over the cluster's distributed shared memory).
-__device__ __forceinline__ const float *map_cluster_ptr(const float *p, uint32_t rank) {
-    uint64_t r;
-    asm volatile("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
-    return reinterpret_cast<const float *>(r);
-}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most one of this thread's bulk groups still reads shared memory.
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 constexpr int kRowThreads = 128;  // threads per row of the norm kernels
 
@@ -84,10 +90,12 @@ __device__ __forceinline__ float block_row_sum(float v, float *red) {
 
 // One block per row: out = fp16(x * inv * g) with inv = 1/sqrt(mean(x^2) + eps) (rmsnorm shader,
 // shaders.ts:580-598), or a plain fp16 cast when gain is null.  The loads of a pass are unrolled
-// so that they are in flight together.
+// so that they are in flight together.  With split-K the block also fills the row of every output
+// with its bias (or the residual row, or zero) for the GEMM's reduce-adds.
 __global__ void __launch_bounds__(kRowThreads) norm_cast_kernel(const float *__restrict__ x,
                                                                 const float *__restrict__ gain, float eps,
-                                                                int one_plus, __half *__restrict__ out, int K) {
+                                                                int one_plus, __half *__restrict__ out, int K,
+                                                                const __grid_constant__ ProjArgs pa, int fill) {
     griddep_launch_dependents();  // the GEMM may start streaming weights meanwhile
     __shared__ float red[kRowThreads / 32];
     const int row = blockIdx.x;
@@ -115,6 +123,17 @@ __global__ void __launch_bounds__(kRowThreads) norm_cast_kernel(const float *__r
             v.w *= inv * (one_plus ? 1.f + g.w : g.w);
         }
         dst[c] = make_uint2(pack_half2(v.x, v.y), pack_half2(v.z, v.w));
+    }
+    if (fill) {
+        for (int i = 0; i < pa.nmat; ++i) {
+            float4 *o = reinterpret_cast<float4 *>(pa.out[i] + (size_t)row * pa.n[i]);
+            const float4 *b = reinterpret_cast<const float4 *>(pa.bias[i]);
+            const float4 *r = i == 0 && pa.residual ? reinterpret_cast<const float4 *>(pa.residual + (size_t)row * pa.n[0])
+                                                    : nullptr;
+#pragma unroll 4
+            for (int c = threadIdx.x; c < pa.n[i] / 4; c += kRowThreads)
+                o[c] = r ? r[c] : b ? b[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
     }
 }
 
@@ -148,7 +167,8 @@ template <int NTOK>
 __global__ void __launch_bounds__(kPThreads, 1)
     proj_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw0,
                 const __grid_constant__ CUtensorMap tw1, const __grid_constant__ CUtensorMap tw2,
-                const __grid_constant__ ProjArgs a) {
+                const __grid_constant__ CUtensorMap to0, const __grid_constant__ CUtensorMap to1,
+                const __grid_constant__ CUtensorMap to2, const __grid_constant__ ProjArgs a) {
     using L = ProjLayout<NTOK>;
     constexpr int S = L::kStages;
     extern __shared__ uint8_t smem_raw[];
@@ -165,6 +185,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     const int f0 = (tile - (mi ? a.tile_end[mi - 1] : 0)) * kFM;   // first feature inside matrix mi
     const int ncols = a.n[mi];
     const CUtensorMap *tw = mi == 0 ? &tw0 : mi == 1 ? &tw1 : &tw2;
+    const CUtensorMap *to = mi == 0 ? &to0 : mi == 1 ? &to1 : &to2;
     const int m0 = blockIdx.y * NTOK;
     const int split = blockIdx.z, splits = gridDim.z;
     const int nk = (a.K + L::kStepK - 1) / L::kStepK;
@@ -197,7 +218,6 @@ __global__ void __launch_bounds__(kPThreads, 1)
         tmem = *tmem_slot;
     }
 
-    bool ok = true;
     if (warp == kPProducer) {
         if (lane == 0) {
             tma_prefetch_desc(&tx);
@@ -254,96 +274,52 @@ __global__ void __launch_bounds__(kPThreads, 1)
         __syncwarp();
     }
 
-    // Epilogue: thread r of warps 0-3 owns feature f0 + r (TMEM lane r).  Every load of a group
-    // of tokens is issued before the first of its stores, so the latencies overlap.
-    const int r = warp * 32 + lane;
-    const int feat = f0 + r;
-    const bool epi = warp < 4;
-    const int ntok = min(NTOK, a.M - m0);
-    float *__restrict__ out = a.out[mi] + (size_t)m0 * ncols + feat;
-    const float *__restrict__ res = a.residual && mi == 0 ? a.residual + (size_t)m0 * ncols + feat : nullptr;
-    const int per = (ntok + splits - 1) / splits;   // split-K: tokens [t0, t1) are reduced here
-    const int t0 = split * per, t1 = min(ntok, t0 + per);
-    float bias = 0.f;
-    if (epi) {
+    // Epilogue: thread r of warps 0-3 owns feature f0 + r (TMEM lane r).  Per 32 tokens: TMEM ->
+    // registers (+ bias + residual with one split) -> staging tile -> one TMA store / reduce-add.
+    if (warp < 4) {
+        const int r = warp * 32 + lane;
+        const int feat = f0 + r;
+        const int ntok = min(NTOK, a.M - m0);
+        const float *__restrict__ res =
+            splits == 1 && a.residual && mi == 0 ? a.residual + (size_t)m0 * ncols + feat : nullptr;
         griddep_wait();   // outputs / residual may belong to the previous kernel
-        bias = feat < ncols && a.bias[mi] ? a.bias[mi][feat] : 0.f;
-        ok = __all_sync(0xffffffffu, mbar_wait(done, 0, a.err, kErrMmaTimeout));  // tcgen05.ld is warp-wide
+        const float bias = splits == 1 && feat < ncols && a.bias[mi] ? a.bias[mi][feat] : 0.f;
+        mbar_wait(done, 0, a.err, kErrMmaTimeout);
         tc_fence_after();
-    }
-
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    if (splits == 1) {
-        if (epi && ok) {
+        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
 #pragma unroll 1
-            for (int c = 0; c < NTOK / 32 && c * 32 < ntok; ++c) {
-                uint32_t v[32];
-                tc_ld32_nowait(tmem + lane_base + c * 32, v);
-                float x[32];
+        // Every warp runs every chunk (the named barriers count all four); after a timeout the
+        // error word is set and the values are meaningless.
+        for (int c = 0; c < NTOK / 32 && c * 32 < ntok; ++c) {
+            float *stage = reinterpret_cast<float *>(smem + (c & 1) * L::kOutTile);
+            if (c >= 2 && threadIdx.x == 0) bulk_wait_read_1();  // the TMA has read this buffer
+            named_barrier_sync(2, 128);
+            uint32_t v[32];
+            tc_ld32_nowait(tmem + lane_base + c * 32, v);
+            float x[32];
 #pragma unroll
-                for (int e = 0; e < 32; ++e)
-                    x[e] = res && feat < ncols && c * 32 + e < ntok ? res[(size_t)(c * 32 + e) * ncols] : 0.f;
-                tc_wait_ld();
-                if (feat < ncols) {
+            for (int e = 0; e < 32; ++e)
+                x[e] = res && feat < ncols && c * 32 + e < ntok ? res[(size_t)(c * 32 + e) * ncols] : 0.f;
+            tc_wait_ld();
 #pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        if (c * 32 + e < ntok) out[(size_t)(c * 32 + e) * ncols] = __uint_as_float(v[e]) + bias + x[e];
-                }
+            for (int e = 0; e < 32; ++e) stage[e * kFM + r] = __uint_as_float(v[e]) + bias + x[e];
+            fence_proxy_async_smem();  // generic writes -> visible to the TMA engine
+            named_barrier_sync(2, 128);
+            if (threadIdx.x == 0) {
+                if (splits == 1)
+                    tma_store_2d(to, stage, f0, m0 + c * 32);
+                else
+                    tma_reduce_add_2d(to, stage, f0, m0 + c * 32);
+                bulk_commit();
             }
         }
-    } else {
-        // Park the partial [token][feature] in this CTA's shared memory (the ring is idle now).
-        float *part = reinterpret_cast<float *>(smem);
-        if (epi) {
-#pragma unroll 1
-            for (int c = 0; c < NTOK / 32 && c * 32 < ntok; ++c) {
-                uint32_t v[32];
-                tc_ld32_nowait(tmem + lane_base + c * 32, v);
-                tc_wait_ld();
-#pragma unroll
-                for (int e = 0; e < 32; ++e) part[(c * 32 + e) * kFM + r] = ok ? __uint_as_float(v[e]) : 0.f;
-            }
-        }
-        cluster_sync_all();
-        // This CTA sums tokens [t0, t1) over every split, in split order, four tokens per step.
-        // The loop body stays small: each CTA runs it once, from a cold instruction cache.
-        if (epi && feat < ncols) {
-            const float *src[8];
-#pragma unroll
-            for (int q = 0; q < 8; ++q) src[q] = map_cluster_ptr(part + r, (uint32_t)min(q, splits - 1));
-#pragma unroll 1
-            for (int t = t0; t < t1; t += 4) {
-                float pv[8][4], x[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) x[u] = res && t + u < t1 ? res[(size_t)(t + u) * ncols] : 0.f;
-#pragma unroll
-                for (int q = 0; q < 8; ++q)
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) pv[q][u] = q < splits && t + u < t1 ? src[q][(t + u) * kFM] : 0.f;
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    float acc = 0.f;
-#pragma unroll
-                    for (int q = 0; q < 8; ++q)
-                        if (q < splits) acc += pv[q][u];
-                    if (t + u < t1) out[(size_t)(t + u) * ncols] = acc + bias + x[u];
-                }
-            }
-        }
-        // No CTA leaves while another still reads its shared memory.  Those reads have returned
-        // their values by now, so a relaxed arrive suffices (and the output stores need not drain).
-        cluster_sync_relaxed();
+        if (threadIdx.x == 0) bulk_wait_all();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     if (warp == kPMma)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)NTOK) : "memory");
-}
-
-template <int NTOK>
-const void *proj_fn() {
-    return reinterpret_cast<const void *>(proj_kernel<NTOK>);
 }
 
 template <int NTOK>
@@ -354,90 +330,55 @@ cudaError_t configure() {
     if (dev < 64 && (configured & (1ull << dev))) return cudaSuccess;
     cudaError_t e = cudaFuncSetAttribute(proj_kernel<NTOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          ProjLayout<NTOK>::kSmemBytes);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(proj_kernel<NTOK>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
     if (e == cudaSuccess && dev < 64) configured |= 1ull << dev;
     return e;
 }
 
-// Clusters of `splits` CTAs that can be resident at once (0 when the query fails).
 template <int NTOK>
-int max_clusters(int splits, int tiles) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(tiles, 1, splits);
-    cfg.blockDim = dim3(kPThreads);
-    cfg.dynamicSmemBytes = ProjLayout<NTOK>::kSmemBytes;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = splits;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, proj_kernel<NTOK>, &cfg) != cudaSuccess) {
-        cudaGetLastError();
-        return 0;
-    }
-    return n;
-}
-
-// Split count: the largest cluster size (<= 8, <= the k steps) whose clusters for all output tiles
-// are resident in one wave, when one CTA per tile would leave most CTA slots idle.
-template <int NTOK>
-int choose_splits(int tiles, int nk, int slots) {
-    static int cache[64][9];  // [device][splits] -> resident clusters (+1; 0 = unknown)
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (tiles * 2 > slots || nk < 4) return 1;
-    int best = 1;
-    for (int s = 2; s <= 8 && s * 2 <= nk; ++s) {
-        if (tiles * s > slots) break;
-        int n;
-        if (dev < 64 && cache[dev][s]) {
-            n = cache[dev][s] - 1;
-        } else {
-            n = max_clusters<NTOK>(s, tiles);
-            if (dev < 64) cache[dev][s] = n + 1;
-        }
-        if (n >= tiles) best = s;
-    }
-    return best;
-}
-
-template <int NTOK>
-cudaError_t launch_t(const CUtensorMap &tx, const CUtensorMap *tw, ProjArgs a, int sms, cudaStream_t s) {
+cudaError_t launch_t(const CUtensorMap &tx, const CUtensorMap *tw, const CUtensorMap *to, const ProjArgs &a,
+                     cudaStream_t s) {
     cudaError_t e = configure<NTOK>();
     if (e != cudaSuccess) return e;
-    const int tiles = a.tile_end[a.nmat - 1];
-    const int nk = (a.K + ProjLayout<NTOK>::kStepK - 1) / ProjLayout<NTOK>::kStepK;
-    int splits = choose_splits<NTOK>(tiles * ((a.M + NTOK - 1) / NTOK), nk, sms * ProjLayout<NTOK>::kCtasPerSm);
-    a.kps = (nk + splits - 1) / splits;
-    splits = (nk + a.kps - 1) / a.kps;  // no empty split
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(tiles, (a.M + NTOK - 1) / NTOK, splits);
+    cfg.gridDim = dim3(a.tile_end[a.nmat - 1], (a.M + NTOK - 1) / NTOK, a.splits);
     cfg.blockDim = dim3(kPThreads);
     cfg.dynamicSmemBytes = ProjLayout<NTOK>::kSmemBytes;
     cfg.stream = s;
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
-    attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = 1;
-    attr[1].val.clusterDim.y = 1;
-    attr[1].val.clusterDim.z = splits;
     cfg.attrs = attr;
-    cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, proj_kernel<NTOK>, tx, tw[0], tw[1], tw[2], a);
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, proj_kernel<NTOK>, tx, tw[0], tw[1], tw[2], to[0], to[1], to[2], a);
+}
+
+template <int NTOK>
+constexpr int ctas_per_sm() {
+    return ProjLayout<NTOK>::kCtasPerSm;
 }
 
 }  // namespace
 
 int proj_token_tile(int rows) { return rows <= 32 ? 32 : rows <= 64 ? 64 : rows <= 128 ? 128 : 256; }
 
+// Split-K plan: when the output tiles leave most CTA slots idle, split the k steps (>= 2 per split)
+// over up to 8 CTAs so that about one wave of slots is busy.
+void proj_plan(ProjArgs &a, int ntok, int sms) {
+    const int step = ProjLayout<32>::kStepK;
+    const int nk = (a.K + step - 1) / step;
+    const int tiles = a.tile_end[a.nmat - 1] * ((a.M + ntok - 1) / ntok);
+    const int slots = sms * (ntok == 32 ? ctas_per_sm<32>() : ntok == 64 ? ctas_per_sm<64>()
+                             : ntok == 128 ? ctas_per_sm<128>() : ctas_per_sm<256>());
+    int splits = 1;
+    if (tiles * 2 <= slots) splits = std::min(std::min(8, slots / tiles), std::max(1, nk / 2));
+    a.kps = (nk + splits - 1) / splits;
+    a.splits = (nk + a.kps - 1) / a.kps;  // no empty split
+}
+
 cudaError_t launch_norm_cast(const float *x, const float *gain, float eps, int one_plus, __half *out, int rows, int K,
-                             cudaStream_t s) {
+                             const ProjArgs &a, cudaStream_t s) {
     if (rows == 0) return cudaSuccess;
-    norm_cast_kernel<<<rows, kRowThreads, 0, s>>>(x, gain, eps, one_plus, out, K);
+    norm_cast_kernel<<<rows, kRowThreads, 0, s>>>(x, gain, eps, one_plus, out, K, a, a.splits > 1);
     return cudaGetLastError();
 }
 
@@ -448,13 +389,13 @@ cudaError_t launch_post_norm_residual(float *h, const float *x, const float *gai
     return cudaGetLastError();
 }
 
-cudaError_t launch_proj(int ntok, const CUtensorMap &tx, const CUtensorMap *tw, const ProjArgs &a, int sms,
-                        cudaStream_t s) {
+cudaError_t launch_proj(int ntok, const CUtensorMap &tx, const CUtensorMap *tw, const CUtensorMap *to,
+                        const ProjArgs &a, cudaStream_t s) {
     switch (ntok) {
-        case 32: return launch_t<32>(tx, tw, a, sms, s);
-        case 64: return launch_t<64>(tx, tw, a, sms, s);
-        case 128: return launch_t<128>(tx, tw, a, sms, s);
-        case 256: return launch_t<256>(tx, tw, a, sms, s);
+        case 32: return launch_t<32>(tx, tw, to, a, s);
+        case 64: return launch_t<64>(tx, tw, to, a, s);
+        case 128: return launch_t<128>(tx, tw, to, a, s);
+        case 256: return launch_t<256>(tx, tw, to, a, s);
         default: return cudaErrorInvalidValue;
     }
 }
