@@ -239,7 +239,10 @@ int brk_attn_combine(brk_ctx *ctx, int n_parts, int rows, int head_dim, const fl
  * GEMMs.  Weights are the engine's fp16 matrices [n][k] (matmul_t_f16w: C = A W^T), passed as
  * raw fp16 bits; activations are f32 [rows][width] (rows = batch * n_tokens) and are cast to
  * fp16 for the tensor cores.  Widths: d_model / q_dim multiples of 8 as inputs, projection
- * outputs multiples of 32.
+ * outputs multiples of 4; all pointers 16-byte aligned.  Small row counts (decode) split K over
+ * several CTAs whose f32 partials are added in L2 in no fixed order, so those outputs may differ
+ * in the last bit from run to run.  One context runs one projection at a time (its activation
+ * staging buffer is shared).
  *   brk_proj_qkv: n1 = rmsnorm(x, attn_norm) (attn_norm NULL: no norm), q = n1 wq^T (+ bq), k, v
  *   likewise (biases may be NULL).
  *   brk_proj_out: h = x + o where o = attn wo^T, or rmsnorm(o, post_norm) when post_norm is given
