@@ -471,10 +471,16 @@ int brk_rope_create(brk_ctx *ctx, int head_dim, double base, const float *ff_hos
     r->ctx = ctx;
     r->head_dim = head_dim;
     r->max_pos = max_positions;
+    std::vector<float2> table32(table.size());
+    for (size_t i = 0; i < table.size(); ++i) table32[i] = make_float2((float)table[i].x, (float)table[i].y);
     cudaError_t e = cudaMalloc(&r->table, table.size() * sizeof(double2));
     if (e == cudaSuccess) e = cudaMemcpy(r->table, table.data(), table.size() * sizeof(double2), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMalloc(&r->table32, table32.size() * sizeof(float2));
+    if (e == cudaSuccess)
+        e = cudaMemcpy(r->table32, table32.data(), table32.size() * sizeof(float2), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         cudaFree(r->table);
+        cudaFree(r->table32);
         delete r;
         return cuda_fail(e, "rope table");
     }
@@ -486,6 +492,7 @@ int brk_rope_destroy(brk_rope *rope) {
     if (!rope) return BRK_OK;
     DeviceGuard g(rope->ctx->device);
     cudaFree(rope->table);
+    cudaFree(rope->table32);
     delete rope;
     return BRK_OK;
 }
@@ -841,8 +848,8 @@ int prefill_impl(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_param
     a.q = q_raw ? nullptr : q;
     a.q_raw = q_raw;
     a.q_norm = q_raw ? p->q_norm : nullptr;
-    a.rope = q_raw && p->rope ? p->rope->table : nullptr;
-    a.eps = p->eps;
+    a.rope = q_raw && p->rope ? p->rope->table32 : nullptr;
+    a.eps = (float)p->eps;
     a.one_plus = p->norm_one_plus ? 1 : 0;
     a.out = out;
     a.err = ctx->d_err;

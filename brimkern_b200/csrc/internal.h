@@ -43,7 +43,8 @@ struct brk_rope {
     brk_ctx *ctx = nullptr;
     int head_dim = 0;
     int max_pos = 0;
-    double2 *table = nullptr;  // [max_pos][head_dim/2] (cos, sin)
+    double2 *table = nullptr;  // [max_pos][head_dim/2] (cos, sin), the K / q rotation of the append
+    float2 *table32 = nullptr; // the same rounded to f32: the prefill kernel's q prologue
 };
 
 struct brk_kv {
@@ -115,11 +116,11 @@ struct DecodeArgs {
 struct PrefillArgs {
     const float *q;  // [B][T][Hq][D] f32 (rotated), or nullptr when q_raw is given
     float *out;      // [B][T][Hq][D] f32
-    // Fused q prologue (brk_attn_prefill_step): raw projection q, gain, rope table.
+    // Fused q prologue (brk_attn_prefill_step): raw projection q, gain, f32 rope table.
     const float *q_raw;
     const float *q_norm;
-    const double2 *rope;
-    double eps;
+    const float2 *rope;
+    float eps;
     int one_plus;
     int *err;
     int B, T, Hq, Hkv, layer, cap, kv_offset, window;

@@ -231,62 +231,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int t = q0 + r;
         // Stage q row r as fp16 in the 128-byte swizzled K-major layout of the MMA's A operand.
         if (a.q_raw) {
-            // Fused q prologue: the append kernel's per-head RMSNorm and NeoX rotation of this
-            // query row, same fp64 arithmetic in the same order (rmsnormCpu kernels.ts:3395,
-            // ropeCpu :3445), so the staged fp16 q equals the one an append would produce.
+            // Fused q prologue: the per-head RMSNorm and NeoX rotation of this query row
+            // (rmsnormCpu kernels.ts:3395, ropeCpu :3445) in f32 with the f32 copy of the table.
+            // q only feeds the fp16 tensor-core operand, so the append's fp64 path (which the
+            // cache rows need bit for bit) is not required here; all loads of a pass are issued
+            // before their arithmetic.
             const float *src = a.q_raw + (((size_t)b * T + (row_ok ? t : 0)) * a.Hq + h) * D;
             constexpr int H2 = D / 2;
-            double inv = 0.0;
-            if (a.q_norm && row_ok) {
-                // Ordered sum of squares; 16-byte loads keep several in flight ahead of the chain.
-                double ss = 0.0;
-#pragma unroll 8
+            float inv = 1.f;
+            if (a.q_norm) {
+                float ss[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
                 for (int c = 0; c < D / 4; ++c) {
-                    const float4 x = *reinterpret_cast<const float4 *>(src + 4 * c);
-                    ss = __dadd_rn(ss, __dmul_rn((double)x.x, (double)x.x));
-                    ss = __dadd_rn(ss, __dmul_rn((double)x.y, (double)x.y));
-                    ss = __dadd_rn(ss, __dmul_rn((double)x.z, (double)x.z));
-                    ss = __dadd_rn(ss, __dmul_rn((double)x.w, (double)x.w));
+                    const float4 x = row_ok ? *reinterpret_cast<const float4 *>(src + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    ss[c & 3] = fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, fmaf(x.w, x.w, ss[c & 3]))));
                 }
-                inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)D), a.eps)));
+                inv = 1.f / sqrtf(((ss[0] + ss[1]) + (ss[2] + ss[3])) / (float)D + a.eps);
             }
-            const double2 *cs = a.rope ? a.rope + (size_t)(row_ok ? past + t : 0) * H2 : nullptr;
-#pragma unroll 2
+            const float2 *cs = a.rope ? a.rope + (size_t)(row_ok ? past + t : 0) * H2 : nullptr;
+#pragma unroll 4
             for (int i = 0; i < H2; i += 4) {
-                float x0[4] = {0.f, 0.f, 0.f, 0.f}, x1[4] = {0.f, 0.f, 0.f, 0.f};
+                float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
                 if (row_ok) {
-                    const float4 lo = *reinterpret_cast<const float4 *>(src + i);
-                    const float4 hi = *reinterpret_cast<const float4 *>(src + i + H2);
-                    x0[0] = lo.x, x0[1] = lo.y, x0[2] = lo.z, x0[3] = lo.w;
-                    x1[0] = hi.x, x1[1] = hi.y, x1[2] = hi.z, x1[3] = hi.w;
+                    lo = *reinterpret_cast<const float4 *>(src + i);
+                    hi = *reinterpret_cast<const float4 *>(src + i + H2);
                 }
-                double y0[4], y1[4];
+                float y0[4] = {lo.x, lo.y, lo.z, lo.w}, y1[4] = {hi.x, hi.y, hi.z, hi.w};
                 if (a.q_norm) {
                     const float4 glo = *reinterpret_cast<const float4 *>(a.q_norm + i);
                     const float4 ghi = *reinterpret_cast<const float4 *>(a.q_norm + i + H2);
                     const float gl[4] = {glo.x, glo.y, glo.z, glo.w}, gh[4] = {ghi.x, ghi.y, ghi.z, ghi.w};
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const double g0 = a.one_plus ? __dadd_rn(1.0, (double)gl[u]) : (double)gl[u];
-                        const double g1 = a.one_plus ? __dadd_rn(1.0, (double)gh[u]) : (double)gh[u];
-                        y0[u] = (double)(float)__dmul_rn(__dmul_rn((double)x0[u], inv), g0);
-                        y1[u] = (double)(float)__dmul_rn(__dmul_rn((double)x1[u], inv), g1);
+                        y0[u] *= inv * (a.one_plus ? 1.f + gl[u] : gl[u]);
+                        y1[u] *= inv * (a.one_plus ? 1.f + gh[u] : gh[u]);
                     }
-                } else {
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) y0[u] = x0[u], y1[u] = x1[u];
                 }
                 float o0[4], o1[4];
                 if (cs) {
+                    const float4 c01 = *reinterpret_cast<const float4 *>(cs + i);
+                    const float4 c23 = *reinterpret_cast<const float4 *>(cs + i + 2);
+                    const float cc[4] = {c01.x, c01.z, c23.x, c23.z}, sn[4] = {c01.y, c01.w, c23.y, c23.w};
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const double2 e = cs[i + u];
-                        o0[u] = (float)__dsub_rn(__dmul_rn(y0[u], e.x), __dmul_rn(y1[u], e.y));
-                        o1[u] = (float)__dadd_rn(__dmul_rn(y1[u], e.x), __dmul_rn(y0[u], e.y));
+                        o0[u] = fmaf(y0[u], cc[u], -y1[u] * sn[u]);
+                        o1[u] = fmaf(y1[u], cc[u], y0[u] * sn[u]);
                     }
                 } else {
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) o0[u] = (float)y0[u], o1[u] = (float)y1[u];
+                    for (int u = 0; u < 4; ++u) o0[u] = y0[u], o1[u] = y1[u];
                 }
                 // Elements i..i+3 and i+D/2..i+D/2+3: 8-byte pieces of 16-byte swizzled chunks.
                 *reinterpret_cast<uint2 *>(sq + (i >> 6) * L::kQBlock + sw128(r, (i & 63) >> 3) + (i & 7) * 2) =

@@ -200,8 +200,9 @@ int brk_attn_prefill(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_p
 
 /* One prefill chunk of a layer's attention slice (recordLayerKV, kernels.ts:1707-1731, as the
  * chunked prefill of lfm2Model.ts:320-333): K/V appended as by brk_attn_append, then the
- * tensor-core kernel with the q prologue (QK-norm + RoPE, same arithmetic) fused into its q
- * staging, so the rotated q never round-trips through HBM.  head_dim 64 or 128.
+ * tensor-core kernel with the q prologue (QK-norm + RoPE in f32; q only feeds the fp16
+ * tensor-core operand) fused into its q staging, so the rotated q never round-trips through HBM.
+ * The cache rows equal brk_attn_append's bit for bit.  head_dim 64 or 128.
  * q_in [B][T][Hq][D], k_in / v_in [B][T][Hkv][D] f32 projections; out [B][T][Hq][D] f32. */
 int brk_attn_prefill_step(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p,
                           int batch, int n_tokens, const int32_t *past_len, const float *q_in,

@@ -94,9 +94,10 @@ def test_chunked_prefill_end_to_end(eng):
 
 
 @pytest.mark.parametrize("D,norm,one_plus", [(128, True, False), (64, False, False), (128, True, True)])
-def test_prefill_step_fused_prologue_is_identical(eng, D, norm, one_plus):
-    """brk_attn_prefill_step (q prologue fused into the prefill kernel) produces bit-for-bit the
-    output of append + prefill on the rotated q, and the same cache rows."""
+def test_prefill_step_fused_prologue_matches(eng, D, norm, one_plus):
+    """brk_attn_prefill_step (q prologue fused into the prefill kernel, in f32) matches append +
+    prefill on the append's fp64-rotated q within the north-star tolerance, and writes the same
+    cache rows bit for bit."""
     import torch
     from brimkern_b200.engine import AttnConfig, KvCache, RopeTable
     rng = np.random.default_rng(D + 7 * norm + 13 * one_plus)
@@ -120,7 +121,7 @@ def test_prefill_step_fused_prologue_is_identical(eng, D, norm, one_plus):
     eng.recAttention(kv_a, 0, cfg, q_rot, out_a, pasts, kernel="prefill")
     eng.prefillStep(kv_b, 0, cfg, q, k, v, out_b, pasts)
     eng.ctx.check()
-    assert torch.equal(out_a, out_b)
+    assert_close(out_b.cpu().numpy(), out_a.cpu().numpy(), what="fused prologue")
     for b, p in enumerate(pasts):
         ka, va = kv_a.read_rows(0, b, p, T)
         kb, vb = kv_b.read_rows(0, b, p, T)
