@@ -143,6 +143,27 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32) append_kernel(const __grid
 // rotation element by element (coalesced gains, table and stores), and an int8 cache quantises
 // each K / V row from its final f32 values.  Same operations in the same order as append_kernel,
 // so the outputs are the same bits.
+// The double equal to a normal f32 x, assembled from its bits (sign, exponent rebiased by
+// 1023 - 127, mantissa shifted up 29); zero, subnormal, inf and NaN take the conversion.
+__device__ __forceinline__ double f32_to_f64_exact(float x) {
+    const uint32_t b = __float_as_uint(x);
+    const uint32_t e = (b >> 23) & 0xFFu;
+    if (e == 0u || e == 0xFFu) return (double)x;
+    const uint32_t hi = (b & 0x80000000u) | ((e + 896u) << 20) | ((b & 0x7FFFFFu) >> 3);
+    return __hiloint2double((int)hi, (int)(b << 29));
+}
+
+// True when every value within E of v rounds to the same fp16 as v (round to nearest even): v is
+// a normal fp16-range value farther than E from the midpoints between consecutive fp16 values.
+// The midpoints sit where the 13 f32 mantissa bits below fp16 precision equal 0x1000.
+__device__ __forceinline__ bool fp16_rounding_stable(float v, float E) {
+    const uint32_t bits = __float_as_uint(v) & 0x7fffffffu;
+    if (bits < 0x38800000u || bits >= 0x477FE000u) return false;  // below 2^-14 or at the fp16 top
+    const int d = abs((int)(bits & 0x1FFFu) - 0x1000);            // f32 ulps to the nearest midpoint
+    const float ulp = __uint_as_float((bits & 0x7F800000u) - (23u << 23));
+    return (float)d * ulp > E;
+}
+
 template <int D, int ROWS>
 __global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant__ AppendArgs a) {
     griddep_launch_dependents();
@@ -153,27 +174,21 @@ __global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant
     double *inv_s = reinterpret_cast<double *>(smem_raw);                 // [ROWS]
     int4 *meta = reinterpret_cast<int4 *>(smem_raw + ROWS * sizeof(double));  // [ROWS] kind, bt, head, pos
     float *xs = reinterpret_cast<float *>(smem_raw + ROWS * (sizeof(double) + sizeof(int4)));  // [ROWS][D+1]
-    const int per_tok = a.Hq + 2 * a.Hkv;
+    // Only the rows asked for (q with q_out, k with k_in, v with v_in) are enumerated, per token
+    // in that order, so that a K / V-only append (prefill chunks) spends no blocks on q rows.
+    const int nq = a.q_out ? a.Hq : 0, nkh = a.k_in ? a.Hkv : 0, nvh = a.v_in ? a.Hkv : 0;
+    const int per_tok = nq + nkh + nvh;
     const long long total = (long long)a.B * a.T * per_tok;
     const long long row0 = (long long)blockIdx.x * ROWS;
     const int nrow = (int)min((long long)ROWS, total - row0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    // Row descriptors: kind 0 = q, 1 = k, 2 = v, -1 = nothing to do (no q_out / no k, v inputs).
+    // Row descriptors: kind 0 = q, 1 = k, 2 = v.
     if (threadIdx.x < nrow) {
         const long long row = row0 + threadIdx.x;
         const int bt = (int)(row / per_tok), kind_h = (int)(row % per_tok);
-        int kind, h;
-        if (kind_h < a.Hq) {
-            kind = a.q_out ? 0 : -1;
-            h = kind_h;
-        } else if (kind_h < a.Hq + a.Hkv) {
-            kind = a.k_in ? 1 : -1;
-            h = kind_h - a.Hq;
-        } else {
-            kind = a.v_in ? 2 : -1;
-            h = kind_h - a.Hq - a.Hkv;
-        }
+        const int kind = kind_h < nq ? 0 : kind_h < nq + nkh ? 1 : 2;
+        const int h = kind == 0 ? kind_h : kind == 1 ? kind_h - nq : kind_h - nq - nkh;
         meta[threadIdx.x] = make_int4(kind, bt, h, a.past_len[bt / a.T] + bt % a.T);
     }
     __syncthreads();
@@ -200,9 +215,14 @@ __global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant
         double inv = 0.0;
         if (m.x >= 0 && gain) {
             const float *x = xs + threadIdx.x * kStride;
+            // x^2 is exact in double, so one rounding of x^2 + ss (fma) is the oracle's
+            // ss + x*x; the doubles are built from the f32 bits without a conversion unit op.
             double ss = 0.0;
 #pragma unroll 16
-            for (int d = 0; d < D; ++d) ss = __dadd_rn(ss, __dmul_rn((double)x[d], (double)x[d]));
+            for (int d = 0; d < D; ++d) {
+                const double xd = f32_to_f64_exact(x[d]);
+                ss = __fma_rn(xd, xd, ss);
+            }
             inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)D), a.eps)));
         }
         inv_s[threadIdx.x] = inv;
@@ -214,6 +234,7 @@ __global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant
     constexpr int NP = H2 / 32;  // pairs per lane
     const bool q8 = a.kc == nullptr && a.kc8 != nullptr;
     double gq[NP][2], gk[NP][2];
+    float gkf[NP][2];
 #pragma unroll
     for (int u = 0; u < NP; ++u) {
         const int i = lane + 32 * u;
@@ -223,6 +244,7 @@ __global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant
             const double wk = a.k_norm ? (double)a.k_norm[i + e * H2] : 0.0;
             gq[u][e] = a.one_plus ? __dadd_rn(1.0, wq) : wq;
             gk[u][e] = a.one_plus ? __dadd_rn(1.0, wk) : wk;
+            gkf[u][e] = (float)gk[u][e];
         }
     }
     for (int lr = warp; lr < nrow; lr += 8) {
@@ -242,9 +264,48 @@ __global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant
                 ((size_t)(a.layer * a.B + m.y / a.T) * a.Hkv + m.z) * a.cap + (size_t)(m.w - a.kv_offset);
             cdst = (m.x == 1 ? a.kc : a.vc) + crow * D;
         }
+        if (m.x == 2 && cdst) {
+            // V into an fp16 cache: a plain round to nearest.
+#pragma unroll
+            for (int u = 0; u < NP; ++u) {
+                const int i = lane + 32 * u;
+                cdst[i] = __float2half_rn(xr[i]);
+                cdst[i + H2] = __float2half_rn(xr[i + H2]);
+            }
+            continue;
+        }
+        // K into an fp16 cache: f32 arithmetic, kept only when its fp16 rounding provably equals
+        // that of the exact value.  f32 path vs the fp64 chain below, per output element:
+        //   y = (x * f32(inv)) * g: three roundings vs one -> |dy| <= 4u|y|  (u = 2^-24);
+        //   rotation with the f32 table and one fma: <= (4u + u + u)(|y0| + |y1|) + u|o| + u|o|
+        //   (the exact chain rounds its double result to f32 once);
+        // so |o_f32 - o_exact| <= 8u (|y0| + |y1|).  E doubles that; a pair within E of an fp16
+        // midpoint takes the fp64 chain.
+        const bool fast = m.x == 1 && cdst;
+        const float invf = (float)inv;
+        const float2 *cs32 = rotate && fast ? a.rope32 + (size_t)m.w * H2 : nullptr;
 #pragma unroll
         for (int u = 0; u < NP; ++u) {
             const int i = lane + 32 * u;
+            if (fast) {
+                float f0 = xr[i], f1 = xr[i + H2];
+                if (norm) {
+                    f0 = (f0 * invf) * gkf[u][0];
+                    f1 = (f1 * invf) * gkf[u][1];
+                }
+                float r0 = f0, r1 = f1;
+                if (rotate) {
+                    const float2 e = cs32[i];
+                    r0 = fmaf(f0, e.x, -(f1 * e.y));
+                    r1 = fmaf(f1, e.x, f0 * e.y);
+                }
+                const float E = 0x1p-20f * (fabsf(f0) + fabsf(f1));
+                if (fp16_rounding_stable(r0, E) && fp16_rounding_stable(r1, E)) {
+                    cdst[i] = __float2half_rn(r0);
+                    cdst[i + H2] = __float2half_rn(r1);
+                    continue;
+                }
+            }
             double y0 = xr[i], y1 = xr[i + H2];
             if (norm) {
                 const double g0 = m.x == 0 ? gq[u][0] : gk[u][0], g1 = m.x == 0 ? gq[u][1] : gk[u][1];
@@ -326,8 +387,11 @@ cudaError_t launch_block(cudaLaunchConfig_t cfg, const AppendArgs &a, long long 
 }
 
 cudaError_t launch_append(const AppendArgs &a, cudaStream_t s, bool pdl) {
-    const long long rows = (long long)a.B * a.T * (a.Hq + 2 * a.Hkv);
+    long long rows = (long long)a.B * a.T * (a.Hq + 2 * a.Hkv);
     if (rows == 0) return cudaSuccess;
+    // The row-block kernels enumerate only the rows asked for.
+    const long long block_rows =
+        (long long)a.B * a.T * ((a.q_out ? a.Hq : 0) + (a.k_in ? a.Hkv : 0) + (a.v_in ? a.Hkv : 0));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)((rows + kRowsPerBlock - 1) / kRowsPerBlock));
     cfg.blockDim = dim3(kRowsPerBlock * 32);
@@ -340,6 +404,10 @@ cudaError_t launch_append(const AppendArgs &a, cudaStream_t s, bool pdl) {
     cfg.numAttrs = pdl ? 1 : 0;
     // Head dims 64 / 128 / 256: row blocks (large appends: 8 KB of rows per block; decode-sized
     // ones: 16 rows per block, so that the rows spread over the SMs).
+    if (a.D == 64 || a.D == 128 || a.D == 256) {
+        if (block_rows == 0) return cudaSuccess;
+        rows = block_rows;
+    }
     const bool big = rows >= 148LL * 2 * (8192 / (a.D > 0 ? a.D : 1));
     cfg.blockDim = dim3(256);
     switch (a.D) {

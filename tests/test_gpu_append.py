@@ -31,6 +31,10 @@ CASES = {
     "rows32_qwen3_d128": (32, 8, 128, 1e6, None, True, False, [0, 1000], 300, 1300),
     "rows32_llama_d64": (32, 8, 64, 5e5, "llama3", False, False, [100, 131000], 200, 131200),
     "rows32_oneplus_d256": (8, 4, 256, 1e4, None, True, True, [0, 50], 600, 700),
+    # K rows spread over 10 decades (fp16 subnormals to overflow): the K store's f32 fast path and
+    # its fallback to the fp64 chain near fp16 rounding midpoints.
+    "rows32_wide_range_d128": (32, 8, 128, 1e6, None, False, False, [0, 700], 512, 1300, "wide"),
+    "rows32_wide_range_norm_d64": (16, 4, 64, 1e4, None, True, True, [3, 0], 700, 710, "wide"),
 }
 
 
@@ -39,7 +43,8 @@ def test_append_bit_exact(eng, name):
     import torch
     from brimkern_b200.engine import AttnConfig, KvCache, RopeTable, llama3_rope_factors
 
-    Hq, Hkv, D, base, ffkind, norm, one_plus, pasts, T, cap = CASES[name]
+    Hq, Hkv, D, base, ffkind, norm, one_plus, pasts, T, cap = CASES[name][:10]
+    spread = CASES[name][10] if len(CASES[name]) > 10 else None
     B = len(pasts)
     rng = np.random.default_rng(zlib.crc32(name.encode()))
     ff = None
@@ -55,6 +60,9 @@ def test_append_bit_exact(eng, name):
     q_in = normal(rng, B, T, Hq, D)
     k_in = normal(rng, B, T, Hkv, D)
     v_in = normal(rng, B, T, Hkv, D)
+    if spread == "wide":
+        k_in *= (10.0 ** rng.uniform(-6.0, 4.2, size=(B, T, Hkv, 1))).astype(np.float32)
+        v_in *= (10.0 ** rng.uniform(-6.0, 4.2, size=(B, T, Hkv, 1))).astype(np.float32)
 
     dev = eng.device
     rope = RopeTable(eng.ctx, D, base, ff, max(pasts) + T)
