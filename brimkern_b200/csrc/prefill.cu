@@ -231,62 +231,88 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int t = q0 + r;
         // Stage q row r as fp16 in the 128-byte swizzled K-major layout of the MMA's A operand.
         if (a.q_raw) {
-            // Fused q prologue: the per-head RMSNorm and NeoX rotation of this query row
+            // Fused q prologue: the per-head RMSNorm and NeoX rotation of the stream's query rows
             // (rmsnormCpu kernels.ts:3395, ropeCpu :3445) in f32 with the f32 copy of the table.
             // q only feeds the fp16 tensor-core operand, so the append's fp64 path (which the
-            // cache rows need bit for bit) is not required here; all loads of a pass are issued
-            // before their arithmetic.
-            const float *src = a.q_raw + (((size_t)b * T + (row_ok ? t : 0)) * a.Hq + h) * D;
-            constexpr int H2 = D / 2;
-            float inv = 1.f;
-            if (a.q_norm) {
-                float ss[4] = {0.f, 0.f, 0.f, 0.f};
+            // cache rows need bit for bit) is not required here.  One warp per row: lane l holds
+            // rotation pairs (i, i + D/2) for i in [l*P, l*P + P), so every load is coalesced and
+            // the sum of squares is a warp reduction.
+            constexpr int H2 = D / 2, P = H2 / 32;
+            const int wl = warp & 3, i0 = lane * P;
+            float g0[P], g1[P];
 #pragma unroll
-                for (int c = 0; c < D / 4; ++c) {
-                    const float4 x = row_ok ? *reinterpret_cast<const float4 *>(src + 4 * c) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    ss[c & 3] = fmaf(x.x, x.x, fmaf(x.y, x.y, fmaf(x.z, x.z, fmaf(x.w, x.w, ss[c & 3]))));
-                }
-                inv = 1.f / sqrtf(((ss[0] + ss[1]) + (ss[2] + ss[3])) / (float)D + a.eps);
+            for (int p = 0; p < P; ++p) {
+                const float w0 = a.q_norm ? a.q_norm[i0 + p] : 1.f, w1 = a.q_norm ? a.q_norm[i0 + p + H2] : 1.f;
+                g0[p] = a.q_norm && a.one_plus ? 1.f + w0 : w0;
+                g1[p] = a.q_norm && a.one_plus ? 1.f + w1 : w1;
             }
-            const float2 *cs = a.rope ? a.rope + (size_t)(row_ok ? past + t : 0) * H2 : nullptr;
-#pragma unroll 4
-            for (int i = 0; i < H2; i += 4) {
-                float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
-                if (row_ok) {
-                    lo = *reinterpret_cast<const float4 *>(src + i);
-                    hi = *reinterpret_cast<const float4 *>(src + i + H2);
-                }
-                float y0[4] = {lo.x, lo.y, lo.z, lo.w}, y1[4] = {hi.x, hi.y, hi.z, hi.w};
-                if (a.q_norm) {
-                    const float4 glo = *reinterpret_cast<const float4 *>(a.q_norm + i);
-                    const float4 ghi = *reinterpret_cast<const float4 *>(a.q_norm + i + H2);
-                    const float gl[4] = {glo.x, glo.y, glo.z, glo.w}, gh[4] = {ghi.x, ghi.y, ghi.z, ghi.w};
+            // Rows wl, wl + 4, ... in batches of kB: all loads of a batch are issued before its
+            // first shared-memory store (stores through the generic pointer would otherwise keep
+            // later loads behind them).
+            constexpr int kB = 8;
+#pragma unroll 1
+            for (int rb = 0; rb < kTQ / 4; rb += kB) {
+                float x0[kB][P], x1[kB][P], c[kB][P], sn[kB][P];
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        y0[u] *= inv * (a.one_plus ? 1.f + gl[u] : gl[u]);
-                        y1[u] *= inv * (a.one_plus ? 1.f + gh[u] : gh[u]);
+                for (int u = 0; u < kB; ++u) {
+                    const int rr = wl + 4 * (rb + u);
+                    const bool ok_r = rr < nqs;
+                    const int tr = q0 + rr;
+                    const float *src = a.q_raw + (((size_t)b * T + (ok_r ? tr : 0)) * a.Hq + h) * D;
+#pragma unroll
+                    for (int p = 0; p < P; ++p) x0[u][p] = x1[u][p] = 0.f, c[u][p] = 1.f, sn[u][p] = 0.f;
+                    if (ok_r) {
+                        if constexpr (P == 2) {
+                            const float2 lo = *reinterpret_cast<const float2 *>(src + i0);
+                            const float2 hi = *reinterpret_cast<const float2 *>(src + i0 + H2);
+                            x0[u][0] = lo.x, x0[u][1] = lo.y, x1[u][0] = hi.x, x1[u][1] = hi.y;
+                            if (a.rope) {
+                                const float4 e = *reinterpret_cast<const float4 *>(a.rope + (size_t)(past + tr) * H2 + i0);
+                                c[u][0] = e.x, sn[u][0] = e.y, c[u][1] = e.z, sn[u][1] = e.w;
+                            }
+                        } else {
+#pragma unroll
+                            for (int p = 0; p < P; ++p) {
+                                x0[u][p] = src[i0 + p], x1[u][p] = src[i0 + p + H2];
+                                if (a.rope) {
+                                    const float2 e = a.rope[(size_t)(past + tr) * H2 + i0 + p];
+                                    c[u][p] = e.x, sn[u][p] = e.y;
+                                }
+                            }
+                        }
                     }
                 }
-                float o0[4], o1[4];
-                if (cs) {
-                    const float4 c01 = *reinterpret_cast<const float4 *>(cs + i);
-                    const float4 c23 = *reinterpret_cast<const float4 *>(cs + i + 2);
-                    const float cc[4] = {c01.x, c01.z, c23.x, c23.z}, sn[4] = {c01.y, c01.w, c23.y, c23.w};
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        o0[u] = fmaf(y0[u], cc[u], -y1[u] * sn[u]);
-                        o1[u] = fmaf(y1[u], cc[u], y0[u] * sn[u]);
+                for (int u = 0; u < kB; ++u) {
+                    const int rr = wl + 4 * (rb + u);
+                    float inv = 1.f;
+                    if (a.q_norm) {
+                        float ss = 0.f;
+#pragma unroll
+                        for (int p = 0; p < P; ++p) ss = fmaf(x0[u][p], x0[u][p], fmaf(x1[u][p], x1[u][p], ss));
+#pragma unroll
+                        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+                        inv = 1.f / sqrtf(ss / (float)D + a.eps);
                     }
-                } else {
+                    float o0[P], o1[P];
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) o0[u] = y0[u], o1[u] = y1[u];
+                    for (int p = 0; p < P; ++p) {
+                        const float y0 = x0[u][p] * inv * g0[p], y1 = x1[u][p] * inv * g1[p];
+                        o0[p] = fmaf(y0, c[u][p], -(y1 * sn[u][p]));
+                        o1[p] = fmaf(y1, c[u][p], y0 * sn[u][p]);
+                    }
+                    // Elements i0.. and i0 + D/2..: pieces of the row's swizzled 16-byte chunks.
+                    const int j0 = i0 + H2;
+                    uint8_t *d0 = sq + (i0 >> 6) * L::kQBlock + sw128(rr, (i0 & 63) >> 3) + (i0 & 7) * 2;
+                    uint8_t *d1 = sq + (j0 >> 6) * L::kQBlock + sw128(rr, (j0 & 63) >> 3) + (j0 & 7) * 2;
+                    if constexpr (P == 2) {
+                        *reinterpret_cast<uint32_t *>(d0) = pack_half2(o0[0], o0[1]);
+                        *reinterpret_cast<uint32_t *>(d1) = pack_half2(o1[0], o1[1]);
+                    } else {
+                        *reinterpret_cast<__half *>(d0) = __float2half_rn(o0[0]);
+                        *reinterpret_cast<__half *>(d1) = __float2half_rn(o1[0]);
+                    }
                 }
-                // Elements i..i+3 and i+D/2..i+D/2+3: 8-byte pieces of 16-byte swizzled chunks.
-                *reinterpret_cast<uint2 *>(sq + (i >> 6) * L::kQBlock + sw128(r, (i & 63) >> 3) + (i & 7) * 2) =
-                    make_uint2(pack_half2(o0[0], o0[1]), pack_half2(o0[2], o0[3]));
-                const int j = i + H2;
-                *reinterpret_cast<uint2 *>(sq + (j >> 6) * L::kQBlock + sw128(r, (j & 63) >> 3) + (j & 7) * 2) =
-                    make_uint2(pack_half2(o1[0], o1[1]), pack_half2(o1[2], o1[3]));
             }
             fence_proxy_async_smem();
             mbar_arrive(&bars[kBarQFull]);
