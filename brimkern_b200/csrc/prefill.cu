@@ -317,20 +317,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             fence_proxy_async_smem();
             mbar_arrive(&bars[kBarQFull]);
         } else {
-            const float *src = a.q + (((size_t)b * T + (row_ok ? t : 0)) * a.Hq + h) * D;
+            // Pre-rotated f32 q: one warp per row (lane l: elements 4l.. of each 128-wide half),
+            // batches of 8 rows loaded before their shared-memory stores.
+            constexpr int kB = 8, PE = D / 32;  // elements per lane
+            const int wl = warp & 3;
+#pragma unroll 1
+            for (int rb = 0; rb < kTQ / 4; rb += kB) {
+                float x[kB][PE];
 #pragma unroll
-            for (int c = 0; c < D / 8; ++c) {
-                float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
-                if (row_ok) {
-                    x0 = *reinterpret_cast<const float4 *>(src + c * 8);
-                    x1 = *reinterpret_cast<const float4 *>(src + c * 8 + 4);
+                for (int u = 0; u < kB; ++u) {
+                    const int rr = wl + 4 * (rb + u);
+                    const bool ok_r = rr < nqs;
+                    const float *src = a.q + (((size_t)b * T + (ok_r ? q0 + rr : 0)) * a.Hq + h) * D;
+                    if constexpr (PE == 4) {
+                        const float4 v4 = ok_r ? *reinterpret_cast<const float4 *>(src + 4 * lane)
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                        x[u][0] = v4.x, x[u][1] = v4.y, x[u][2] = v4.z, x[u][3] = v4.w;
+                    } else {
+                        const float2 v2 = ok_r ? *reinterpret_cast<const float2 *>(src + 2 * lane) : make_float2(0.f, 0.f);
+                        x[u][0] = v2.x, x[u][1] = v2.y;
+                    }
                 }
-                uint4 pk;
-                pk.x = pack_half2(x0.x, x0.y);
-                pk.y = pack_half2(x0.z, x0.w);
-                pk.z = pack_half2(x1.x, x1.y);
-                pk.w = pack_half2(x1.z, x1.w);
-                *reinterpret_cast<uint4 *>(sq + (c >> 3) * L::kQBlock + sw128(r, c & 7)) = pk;
+#pragma unroll
+                for (int u = 0; u < kB; ++u) {
+                    const int rr = wl + 4 * (rb + u);
+                    const int i = PE * lane;  // first element of this lane
+                    uint8_t *d = sq + (i >> 6) * L::kQBlock + sw128(rr, (i & 63) >> 3) + (i & 7) * 2;
+                    if constexpr (PE == 4)
+                        *reinterpret_cast<uint2 *>(d) = make_uint2(pack_half2(x[u][0], x[u][1]), pack_half2(x[u][2], x[u][3]));
+                    else
+                        *reinterpret_cast<uint32_t *>(d) = pack_half2(x[u][0], x[u][1]);
+                }
             }
             fence_proxy_async_smem();
             mbar_arrive(&bars[kBarQFull]);
