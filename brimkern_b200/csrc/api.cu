@@ -822,7 +822,7 @@ int ensure_stage(brk_ctx *ctx, size_t bytes) {
 // the non-causal path whose rows all sit at the last key.
 int prefill_impl(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
                  const int32_t *past_len, const float *q, const float *q_raw, float *out, void *stream,
-                 bool clamp_rows = false) {
+                 bool clamp_rows = false, bool pdl = false) {
     int rc = check_call(ctx, kv, layer, p, batch, n_tokens, past_len);
     if (rc) return rc;
     if ((!q && !q_raw) || !out) return fail(BRK_ERR_INVALID, "null q or out");
@@ -895,7 +895,7 @@ int prefill_impl(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_param
         ++ctx->launches;
         return BRK_OK;
     }
-    cudaError_t e = brk::launch_prefill(p->head_dim, kv->tm_pre_k, kv->tm_pre_v, a, st);
+    cudaError_t e = brk::launch_prefill(p->head_dim, kv->tm_pre_k, kv->tm_pre_v, a, st, pdl);
     if (e != cudaSuccess) return cuda_fail(e, "prefill kernel launch");
     ++ctx->launches;
     return BRK_OK;
@@ -911,10 +911,11 @@ int brk_attn_prefill_step(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_pa
                           const int32_t *past_len, const float *q_in, const float *k_in, const float *v_in, float *out,
                           void *stream) {
     if (!q_in || !k_in || !v_in || !out) return fail(BRK_ERR_INVALID, "null tensor argument");
-    // K/V rows only: the q prologue runs inside the prefill kernel.
+    // K/V rows only: the q prologue runs inside the prefill kernel, launched programmatically
+    // dependent on the append so that the prologue overlaps it.
     int rc = append_impl(ctx, kv, layer, p, batch, n_tokens, past_len, nullptr, k_in, v_in, nullptr, stream, false);
     if (rc) return rc;
-    return prefill_impl(ctx, kv, layer, p, batch, n_tokens, past_len, nullptr, q_in, out, stream);
+    return prefill_impl(ctx, kv, layer, p, batch, n_tokens, past_len, nullptr, q_in, out, stream, false, true);
 }
 
 int brk_attn_forward(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,

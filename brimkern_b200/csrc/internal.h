@@ -171,7 +171,7 @@ cudaError_t launch_combine_peers(const CombineArgs &a, const unsigned *flags, in
                                  unsigned long long wait_ns, int *err, cudaStream_t s);
 // Tensor-core prefill (head_dim 64 or 128); maps with prefill_tile_keys()-row boxes.
 cudaError_t launch_prefill(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const PrefillArgs &a,
-                           cudaStream_t s);
+                           cudaStream_t s, bool pdl = false);
 // Concurrent CTAs per SM of the decode kernel for a head dim and cache type (occupancy query).
 int decode_ctas_per_sm(int head_dim, bool q8);
 

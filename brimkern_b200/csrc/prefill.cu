@@ -147,6 +147,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0 && nk > 0) {
             tma_prefetch_desc(&tmk);
             tma_prefetch_desc(&tmv);
+            // Launched right behind the append of this chunk's K/V (programmatic dependent launch):
+            // only these cache reads depend on it; the q prologue already overlaps the append.
+            griddep_wait();
             int issued = 0;
             for (int j = 0; j < nk; ++j) {
                 const int st = j % kStages;
@@ -496,7 +499,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int D, bool CAP>
-cudaError_t launch_prefill_t(const CUtensorMap &tmk, const CUtensorMap &tmv, const PrefillArgs &a, cudaStream_t s) {
+cudaError_t launch_prefill_t(const CUtensorMap &tmk, const CUtensorMap &tmv, const PrefillArgs &a, cudaStream_t s,
+                             bool pdl) {
     static unsigned long long configured = 0;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -509,8 +513,17 @@ cudaError_t launch_prefill_t(const CUtensorMap &tmk, const CUtensorMap &tmv, con
     const int G = a.Hq / a.Hkv;
     const int ntq = (a.T + kTQ - 1) / kTQ;
     const dim3 grid(G % 2 == 0 ? a.Hq / 2 : a.Hq, G % 2 == 0 ? ntq : (ntq + 1) / 2, a.B);
-    prefill_attn_kernel<D, CAP><<<grid, kThreads, PrefillLayout<D>::kSmemBytes, s>>>(tmk, tmv, a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = PrefillLayout<D>::kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, prefill_attn_kernel<D, CAP>, tmk, tmv, a);
 }
 
 }  // namespace
@@ -518,12 +531,14 @@ cudaError_t launch_prefill_t(const CUtensorMap &tmk, const CUtensorMap &tmv, con
 int prefill_tile_keys() { return kTK; }
 
 cudaError_t launch_prefill(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const PrefillArgs &a,
-                           cudaStream_t s) {
+                           cudaStream_t s, bool pdl) {
     const bool cap = a.softcap > 0.f;
     switch (head_dim) {
-        case 64: return cap ? launch_prefill_t<64, true>(tmk, tmv, a, s) : launch_prefill_t<64, false>(tmk, tmv, a, s);
+        case 64:
+            return cap ? launch_prefill_t<64, true>(tmk, tmv, a, s, pdl) : launch_prefill_t<64, false>(tmk, tmv, a, s, pdl);
         case 128:
-            return cap ? launch_prefill_t<128, true>(tmk, tmv, a, s) : launch_prefill_t<128, false>(tmk, tmv, a, s);
+            return cap ? launch_prefill_t<128, true>(tmk, tmv, a, s, pdl)
+                       : launch_prefill_t<128, false>(tmk, tmv, a, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
