@@ -734,7 +734,6 @@ int append_impl(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, i
     a.scales = kv ? kv->scales : nullptr;
     a.scale_pitch = kv ? kv->scale_pitch : 0;
     a.rope = p->rope ? p->rope->table : nullptr;
-    a.rope32 = p->rope ? p->rope->table32 : nullptr;
     a.rope_max = p->rope ? p->rope->max_pos : 0;
     a.q_norm = p->q_norm;
     a.k_norm = p->k_norm;

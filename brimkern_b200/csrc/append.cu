@@ -143,27 +143,6 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32) append_kernel(const __grid
 // rotation element by element (coalesced gains, table and stores), and an int8 cache quantises
 // each K / V row from its final f32 values.  Same operations in the same order as append_kernel,
 // so the outputs are the same bits.
-// The double equal to a normal f32 x, assembled from its bits (sign, exponent rebiased by
-// 1023 - 127, mantissa shifted up 29); zero, subnormal, inf and NaN take the conversion.
-__device__ __forceinline__ double f32_to_f64_exact(float x) {
-    const uint32_t b = __float_as_uint(x);
-    const uint32_t e = (b >> 23) & 0xFFu;
-    if (e == 0u || e == 0xFFu) return (double)x;
-    const uint32_t hi = (b & 0x80000000u) | ((e + 896u) << 20) | ((b & 0x7FFFFFu) >> 3);
-    return __hiloint2double((int)hi, (int)(b << 29));
-}
-
-// True when every value within E of v rounds to the same fp16 as v (round to nearest even): v is
-// a normal fp16-range value farther than E from the midpoints between consecutive fp16 values.
-// The midpoints sit where the 13 f32 mantissa bits below fp16 precision equal 0x1000.
-__device__ __forceinline__ bool fp16_rounding_stable(float v, float E) {
-    const uint32_t bits = __float_as_uint(v) & 0x7fffffffu;
-    if (bits < 0x38800000u || bits >= 0x477FE000u) return false;  // below 2^-14 or at the fp16 top
-    const int d = abs((int)(bits & 0x1FFFu) - 0x1000);            // f32 ulps to the nearest midpoint
-    const float ulp = __uint_as_float((bits & 0x7F800000u) - (23u << 23));
-    return (float)d * ulp > E;
-}
-
 template <int D, int ROWS>
 __global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant__ AppendArgs a) {
     griddep_launch_dependents();
@@ -215,12 +194,11 @@ __global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant
         double inv = 0.0;
         if (m.x >= 0 && gain) {
             const float *x = xs + threadIdx.x * kStride;
-            // x^2 is exact in double, so one rounding of x^2 + ss (fma) is the oracle's
-            // ss + x*x; the doubles are built from the f32 bits without a conversion unit op.
+            // x^2 is exact in double, so one rounding of x^2 + ss (fma) is the oracle's ss + x*x.
             double ss = 0.0;
 #pragma unroll 16
             for (int d = 0; d < D; ++d) {
-                const double xd = f32_to_f64_exact(x[d]);
+                const double xd = (double)x[d];
                 ss = __fma_rn(xd, xd, ss);
             }
             inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)D), a.eps)));
@@ -234,7 +212,6 @@ __global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant
     constexpr int NP = H2 / 32;  // pairs per lane
     const bool q8 = a.kc == nullptr && a.kc8 != nullptr;
     double gq[NP][2], gk[NP][2];
-    float gkf[NP][2];
 #pragma unroll
     for (int u = 0; u < NP; ++u) {
         const int i = lane + 32 * u;
@@ -244,7 +221,6 @@ __global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant
             const double wk = a.k_norm ? (double)a.k_norm[i + e * H2] : 0.0;
             gq[u][e] = a.one_plus ? __dadd_rn(1.0, wq) : wq;
             gk[u][e] = a.one_plus ? __dadd_rn(1.0, wk) : wk;
-            gkf[u][e] = (float)gk[u][e];
         }
     }
     for (int lr = warp; lr < nrow; lr += 8) {
@@ -274,38 +250,9 @@ __global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant
             }
             continue;
         }
-        // K into an fp16 cache: f32 arithmetic, kept only when its fp16 rounding provably equals
-        // that of the exact value.  f32 path vs the fp64 chain below, per output element:
-        //   y = (x * f32(inv)) * g: three roundings vs one -> |dy| <= 4u|y|  (u = 2^-24);
-        //   rotation with the f32 table and one fma: <= (4u + u + u)(|y0| + |y1|) + u|o| + u|o|
-        //   (the exact chain rounds its double result to f32 once);
-        // so |o_f32 - o_exact| <= 8u (|y0| + |y1|).  E doubles that; a pair within E of an fp16
-        // midpoint takes the fp64 chain.
-        const bool fast = m.x == 1 && cdst;
-        const float invf = (float)inv;
-        const float2 *cs32 = rotate && fast ? a.rope32 + (size_t)m.w * H2 : nullptr;
 #pragma unroll
         for (int u = 0; u < NP; ++u) {
             const int i = lane + 32 * u;
-            if (fast) {
-                float f0 = xr[i], f1 = xr[i + H2];
-                if (norm) {
-                    f0 = (f0 * invf) * gkf[u][0];
-                    f1 = (f1 * invf) * gkf[u][1];
-                }
-                float r0 = f0, r1 = f1;
-                if (rotate) {
-                    const float2 e = cs32[i];
-                    r0 = fmaf(f0, e.x, -(f1 * e.y));
-                    r1 = fmaf(f1, e.x, f0 * e.y);
-                }
-                const float E = 0x1p-20f * (fabsf(f0) + fabsf(f1));
-                if (fp16_rounding_stable(r0, E) && fp16_rounding_stable(r1, E)) {
-                    cdst[i] = __float2half_rn(r0);
-                    cdst[i + H2] = __float2half_rn(r1);
-                    continue;
-                }
-            }
             double y0 = xr[i], y1 = xr[i + H2];
             if (norm) {
                 const double g0 = m.x == 0 ? gq[u][0] : gk[u][0], g1 = m.x == 0 ? gq[u][1] : gk[u][1];
@@ -340,6 +287,117 @@ __global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant
             const size_t r = (size_t)(m.w - a.kv_offset);
             quantize_row_warp(xs + lr * kStride, D, (m.x == 1 ? a.kc8 : a.vc8) + (seg * a.cap + r) * D,
                               a.scales + (seg * 2 + (m.x == 1 ? 0 : 1)) * a.scale_pitch + r, lane);
+        }
+    }
+}
+
+// K / V rows of a multi-token append (prefill chunks) into an fp16 cache, no q: one block per
+// (32 tokens, kv head, sequence), so the block's cache rows are contiguous.  Warps load their
+// rows (all loads of a warp issued before its first store), V rows go straight to the cache
+// (round to nearest), K rows are staged in shared memory; one thread per K row runs the ordered
+// double sum of squares; then a warp per K row applies the norm and the rotation with exactly
+// append_block_kernel's double operations (same bits; it only spends far fewer instructions on
+// row bookkeeping).
+template <int D>
+__global__ void __launch_bounds__(256) kv_append_kernel(const __grid_constant__ AppendArgs a) {
+    griddep_launch_dependents();
+    griddep_wait();
+    constexpr int TT = 32, RPW = TT / 8;         // tokens per block, rows per warp
+    constexpr int H2 = D / 2, NP = H2 / 32;      // rotation pairs per lane
+    constexpr int C4 = D / 4 >= 32 ? D / 128 : 1;  // float4 per lane per row
+    constexpr int kStride = D + 1;
+    __shared__ float xs[TT * kStride];
+    __shared__ double inv_s[TT];
+    const int t0 = blockIdx.x * TT, h = blockIdx.y, b = blockIdx.z;
+    const int nt = min(TT, a.T - t0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pos0 = a.past_len[b] + t0;
+    const size_t crow0 = ((size_t)(a.layer * a.B + b) * a.Hkv + h) * a.cap + (size_t)(pos0 - a.kv_offset);
+    __half *kc = a.kc + crow0 * D, *vc = a.vc + crow0 * D;
+
+    // 1. Loads: K -> shared memory, V -> cache.
+    {
+        float4 kx[RPW][C4], vx[RPW][C4];
+#pragma unroll
+        for (int u = 0; u < RPW; ++u) {
+            const int tl = warp + 8 * u;
+            const size_t in_row = ((size_t)(b * a.T + t0 + (tl < nt ? tl : 0)) * a.Hkv + h) * D;
+#pragma unroll
+            for (int c = 0; c < C4; ++c) {
+                const int col = lane + 32 * c;
+                const bool ok = tl < nt && col < D / 4;
+                kx[u][c] = ok ? reinterpret_cast<const float4 *>(a.k_in + in_row)[col] : make_float4(0.f, 0.f, 0.f, 0.f);
+                vx[u][c] = ok ? reinterpret_cast<const float4 *>(a.v_in + in_row)[col] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < RPW; ++u) {
+            const int tl = warp + 8 * u;
+#pragma unroll
+            for (int c = 0; c < C4; ++c) {
+                const int col = lane + 32 * c;
+                if (tl < nt && col < D / 4) {
+                    float *dst = xs + tl * kStride + 4 * col;
+                    dst[0] = kx[u][c].x, dst[1] = kx[u][c].y, dst[2] = kx[u][c].z, dst[3] = kx[u][c].w;
+                    *reinterpret_cast<uint2 *>(vc + (size_t)tl * D + 4 * col) =
+                        make_uint2(pack_half2(vx[u][c].x, vx[u][c].y), pack_half2(vx[u][c].z, vx[u][c].w));
+                }
+            }
+        }
+    }
+    __syncthreads();
+    // 2. rmsnormCpu's ordered sum (kernels.ts:3395), one thread per K row.
+    if (a.k_norm && threadIdx.x < nt) {
+        const float *x = xs + threadIdx.x * kStride;
+        double ss = 0.0;
+#pragma unroll 16
+        for (int d = 0; d < D; ++d) {
+            const double xd = (double)x[d];
+            ss = __fma_rn(xd, xd, ss);  // x^2 is exact in double: one rounding, as ss + x*x
+        }
+        inv_s[threadIdx.x] = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)D), a.eps)));
+    }
+    __syncthreads();
+    // 3. Norm and rotation (ropeCpu kernels.ts:3445), a warp per K row, lane l owning the pairs
+    //    (i, i + D/2) for i = l + 32u; the table entries of the warp's rows are loaded first.
+    double g0[NP], g1[NP];
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+        const int i = lane + 32 * u;
+        const double w0 = a.k_norm ? (double)a.k_norm[i] : 1.0, w1 = a.k_norm ? (double)a.k_norm[i + H2] : 1.0;
+        g0[u] = a.k_norm && a.one_plus ? __dadd_rn(1.0, w0) : w0;
+        g1[u] = a.k_norm && a.one_plus ? __dadd_rn(1.0, w1) : w1;
+    }
+    double2 cs[RPW][NP];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+        const int tl = warp + 8 * r;
+#pragma unroll
+        for (int u = 0; u < NP; ++u)
+            cs[r][u] = a.rope && tl < nt ? a.rope[(size_t)(pos0 + tl) * H2 + lane + 32 * u] : make_double2(1.0, 0.0);
+    }
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+        const int tl = warp + 8 * r;
+        if (tl >= nt) break;
+        const float *xr = xs + tl * kStride;
+        const double inv = a.k_norm ? inv_s[tl] : 0.0;
+        __half *dst = kc + (size_t)tl * D;
+#pragma unroll
+        for (int u = 0; u < NP; ++u) {
+            const int i = lane + 32 * u;
+            double y0 = xr[i], y1 = xr[i + H2];
+            if (a.k_norm) {
+                y0 = (double)(float)__dmul_rn(__dmul_rn(y0, inv), g0[u]);
+                y1 = (double)(float)__dmul_rn(__dmul_rn(y1, inv), g1[u]);
+            }
+            float o0 = (float)y0, o1 = (float)y1;
+            if (a.rope) {
+                o0 = (float)__dsub_rn(__dmul_rn(y0, cs[r][u].x), __dmul_rn(y1, cs[r][u].y));
+                o1 = (float)__dadd_rn(__dmul_rn(y1, cs[r][u].x), __dmul_rn(y0, cs[r][u].y));
+            }
+            dst[i] = __float2half_rn(o0);
+            dst[i + H2] = __float2half_rn(o1);
         }
     }
 }
@@ -407,6 +465,17 @@ cudaError_t launch_append(const AppendArgs &a, cudaStream_t s, bool pdl) {
     if (a.D == 64 || a.D == 128 || a.D == 256) {
         if (block_rows == 0) return cudaSuccess;
         rows = block_rows;
+        // K / V only into an fp16 cache (prefill chunks): the dedicated kernel.
+        if (!a.q_out && a.k_in && a.v_in && a.kc && a.T >= 8) {
+            cfg.gridDim = dim3((unsigned)((a.T + 31) / 32), (unsigned)a.Hkv, (unsigned)a.B);
+            cfg.blockDim = dim3(256);
+            cfg.dynamicSmemBytes = 0;
+            switch (a.D) {
+                case 64: return cudaLaunchKernelEx(&cfg, kv_append_kernel<64>, a);
+                case 128: return cudaLaunchKernelEx(&cfg, kv_append_kernel<128>, a);
+                default: return cudaLaunchKernelEx(&cfg, kv_append_kernel<256>, a);
+            }
+        }
     }
     const bool big = rows >= 148LL * 2 * (8192 / (a.D > 0 ? a.D : 1));
     cfg.blockDim = dim3(256);

@@ -77,7 +77,6 @@ struct AppendArgs {
     float *scales;            //   [seg][2][scale_pitch] scales
     int scale_pitch;
     const double2 *rope;
-    const float2 *rope32;     // the same table rounded to f32 (the K fast path of append_block_kernel)
     int rope_max;
     const float *q_norm, *k_norm;
     double eps;

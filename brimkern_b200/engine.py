@@ -520,7 +520,8 @@ class AttentionEngine:
         """QK-norm + RoPE of q and the new k, fp16 store of k and v at row pastLen
         (kernels.ts:1707-1730)."""
         B = kv.batch
-        T = q_in.numel() // (B * cfg.n_heads * cfg.head_dim)
+        T = (q_in.numel() // (B * cfg.n_heads * cfg.head_dim) if q_in is not None
+             else k_in.numel() // (B * cfg.n_kv_heads * cfg.head_dim))
         p = cfg.params()
         pos = _positions(past_len, B)
         check(L.lib().brk_attn_append(self.ctx.handle, kv.handle, layer, ctypes.byref(p), B, T, pos, _ptr(q_in),
