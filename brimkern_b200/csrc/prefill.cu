@@ -8,7 +8,7 @@
 // (320 threads):
 //   warps 0-3 / 4-7  softmax warpgroup of stream 0 / 1: thread r owns query row r (TMEM lane r);
 //   warp 8           TMA producer: 64-key K and V tiles (128-byte swizzled [keys][64] boxes,
-//                    CTA-local loads) into a 3-stage ring;
+//                    CTA-local loads) into a 4-stage (D 64: 6-stage) ring;
 //   warp 9           TMEM allocator and MMA issuer (one elected lane).
 // Per 64-key tile j and stream s: S_s = Q_s K_j^T (tcgen05.mma, M 128, N 64, fp16 -> fp32 in
 // TMEM); the stream's warpgroup reads S_s once, masks (causal offset pastLen, window) only on
@@ -29,7 +29,6 @@ namespace {
 
 constexpr int kTQ = 128;       // queries per stream (the MMA's M)
 constexpr int kTK = 64;        // keys per tile (N of QK^T, K of PV)
-constexpr int kStages = 3;     // K/V ring depth
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kThreads = 10 * 32;
@@ -38,6 +37,9 @@ constexpr float kRescaleLog2 = 8.f;  // raise the running max only when a tile e
 
 template <int D>
 struct PrefillLayout {
+    // K/V ring depth: TMA latency under a full chip (~2.7k cycles) exceeds one 64-key tile
+    // period, so the ring keeps more tiles in flight (D 128: all the shared memory left).
+    static constexpr int kStages = D == 64 ? 6 : 4;
     static constexpr int kBlocks = D / 64;
     static constexpr uint32_t kQBlock = kTQ * 128;             // [128 rows][64] fp16
     static constexpr uint32_t kKVBlock = kTK * 128;            // [64 keys][64] fp16
@@ -46,23 +48,25 @@ struct PrefillLayout {
     static constexpr uint32_t kPBytes = kTQ * 128;             // [128 rows][64 keys] fp16
     static constexpr uint32_t kOffQ = 0;                       // 2 streams
     static constexpr uint32_t kOffKV = 2 * kQBytes;            // kStages x (K, V)
+    static_assert(kStages <= 6, "barrier slots");
     static constexpr uint32_t kOffP = kOffKV + kStages * 2 * kTileBytes;  // 2 streams
     static constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;
     static constexpr uint32_t kNumBars = 24;
     static constexpr uint32_t kSmemBytes = 1024 + kOffBar + kNumBars * 8 + 16;
+    static_assert(kSmemBytes <= 232448, "more than 227 KB of shared memory per CTA");
     static constexpr uint32_t kColS = 0, kColO = 2 * kTK;     // TMEM columns: S_s at s*64, O_s at 128 + s*D
 };
 
 // Barrier slots.
 enum : int {
-    kBarKvFull = 0,   // [3] TMA -> MMA
-    kBarKvEmpty = 3,  // [3] MMA commit -> producer
-    kBarSFull = 6,    // [2] MMA commit (S_s ready) -> softmax s
-    kBarSFree = 8,    // [2] softmax s (S_s read) -> MMA
-    kBarPFull = 10,   // [2] softmax s (P_s written, O_s rescaled) -> MMA
-    kBarODone = 12,   // [2] MMA commit (PV_s done: P_s free, O_s stable) -> softmax s
-    kBarQFull = 14,   // both warpgroups staged q -> MMA
-    kBarMmaDone = 15, // everything issued has completed -> teardown
+    kBarKvFull = 0,   // [kStages] TMA -> MMA
+    kBarKvEmpty = 6,  // [kStages] MMA commit -> producer
+    kBarSFull = 12,   // [2] MMA commit (S_s ready) -> softmax s
+    kBarSFree = 14,   // [2] softmax s (S_s read) -> MMA
+    kBarPFull = 16,   // [2] softmax s (P_s written, O_s rescaled) -> MMA
+    kBarODone = 18,   // [2] MMA commit (PV_s done: P_s free, O_s stable) -> softmax s
+    kBarQFull = 20,   // both warpgroups staged q -> MMA
+    kBarMmaDone = 21, // everything issued has completed -> teardown
 };
 
 // Score in log2 units from a raw q.k dot product (monotonic, so maxima commute with it).
@@ -113,7 +117,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int seg_row = ((a.layer * a.B + b) * a.Hkv + kvh) * a.cap;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kStages; ++i) {
+        for (int i = 0; i < L::kStages; ++i) {
             mbar_init(&bars[kBarKvFull + i], 1);
             mbar_init(&bars[kBarKvEmpty + i], 1);
         }
@@ -152,9 +156,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             griddep_wait();
             int issued = 0;
             for (int j = 0; j < nk; ++j) {
-                const int st = j % kStages;
-                if (j >= kStages &&
-                    !mbar_wait(&bars[kBarKvEmpty + st], ((j / kStages) - 1) & 1, a.err, kErrSlotTimeout))
+                const int st = j % L::kStages;
+                if (j >= L::kStages &&
+                    !mbar_wait(&bars[kBarKvEmpty + st], ((j / L::kStages) - 1) & 1, a.err, kErrSlotTimeout))
                     break;
                 const int y = seg_row + klo + j * kTK;
                 mbar_arrive_expect_tx(&bars[kBarKvFull + st], 2 * L::kTileBytes);
@@ -165,8 +169,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 issued = j + 1;
             }
-            for (int j = issued > kStages ? issued - kStages : 0; j < issued; ++j)
-                mbar_wait(&bars[kBarKvFull + j % kStages], (j / kStages) & 1, a.err, kErrTmaTimeout);
+            for (int j = issued > L::kStages ? issued - L::kStages : 0; j < issued; ++j)
+                mbar_wait(&bars[kBarKvFull + j % L::kStages], (j / L::kStages) & 1, a.err, kErrTmaTimeout);
         }
         __syncwarp();
     } else if (warp == kMmaWarp) {
@@ -176,8 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int ns = active1 ? 2 : 1;
             bool ok = mbar_wait(&bars[kBarQFull], 0, a.err, kErrMmaTimeout);
             auto issue_s = [&](int s, int j) -> bool {
-                const int st = j % kStages;
-                if (s == 0 && !mbar_wait(&bars[kBarKvFull + st], (j / kStages) & 1, a.err, kErrTmaTimeout))
+                const int st = j % L::kStages;
+                if (s == 0 && !mbar_wait(&bars[kBarKvFull + st], (j / L::kStages) & 1, a.err, kErrTmaTimeout))
                     return false;
                 if (j >= 1 && !mbar_wait(&bars[kBarSFree + s], (j - 1) & 1, a.err, kErrMmaTimeout)) return false;
                 tc_fence_after();
@@ -192,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 return true;
             };
             auto issue_pv = [&](int s, int j) -> bool {
-                const int st = j % kStages;
+                const int st = j % L::kStages;
                 if (!mbar_wait(&bars[kBarPFull + s], j & 1, a.err, kErrMmaTimeout)) return false;
                 tc_fence_after();
                 const uint32_t p_base = smem_addr(sP(s)), v_base = smem_addr(sV(st));
@@ -215,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (!issue_pv(0, j)) break;
                 if (ns == 2 && !issue_pv(1, j)) break;
-                tc_commit(&bars[kBarKvEmpty + j % kStages]);
+                tc_commit(&bars[kBarKvEmpty + j % L::kStages]);
             }
             // Every MMA this thread issued must finish before TMEM is released.
             tc_commit(&bars[kBarMmaDone]);
@@ -453,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // Keys past the range end: zero their V rows so that 0 * (stale data) stays 0
                 // (one warpgroup does it; PV of both streams waits for both P_s arrivals).
                 if (s == 0 && kbase + kTK > khi && r < kTK && kbase + r >= khi) {
-                    if (!mbar_wait(&bars[kBarKvFull + j % kStages], (j / kStages) & 1, a.err, kErrTmaTimeout)) {
+                    if (!mbar_wait(&bars[kBarKvFull + j % L::kStages], (j / L::kStages) & 1, a.err, kErrTmaTimeout)) {
                         ok = false;
                         break;
                     }
@@ -461,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int blk = 0; blk < L::kBlocks; ++blk)
 #pragma unroll
                         for (int c = 0; c < 8; ++c)
-                            *reinterpret_cast<uint4 *>(sV(j % kStages) + blk * L::kKVBlock + sw128(r, c)) =
+                            *reinterpret_cast<uint4 *>(sV(j % L::kStages) + blk * L::kKVBlock + sw128(r, c)) =
                                 make_uint4(0u, 0u, 0u, 0u);
                 }
                 fence_proxy_async_smem();
