@@ -37,6 +37,9 @@ namespace {
 
 constexpr int kRT = 8;  // query rows per CTA tile (the MMA N dimension)
 
+// Ring stages, CTAs per SM (launch bound), head-dim split and key groups per (cache type, D),
+// chosen by timing sweeps on B200: the int8 kernels run 4 CTAs per SM with shallower rings, the
+// extra consumer warps hiding the code conversion.
 template <bool Q8, int D>
 struct DecodeCfg;
 template <>
@@ -53,15 +56,15 @@ struct DecodeCfg<false, 256> {
 };
 template <>
 struct DecodeCfg<true, 64> {
-    static constexpr int kStages = 6, kMinBlocks = 3, kDSplit = 1, kKeyGroups = 4;
+    static constexpr int kStages = 4, kMinBlocks = 4, kDSplit = 1, kKeyGroups = 4;
 };
 template <>
 struct DecodeCfg<true, 128> {
-    static constexpr int kStages = 4, kMinBlocks = 3, kDSplit = 1, kKeyGroups = 4;
+    static constexpr int kStages = 3, kMinBlocks = 4, kDSplit = 1, kKeyGroups = 4;
 };
 template <>
 struct DecodeCfg<true, 256> {
-    static constexpr int kStages = 4, kMinBlocks = 3, kDSplit = 2, kKeyGroups = 2;
+    static constexpr int kStages = 2, kMinBlocks = 4, kDSplit = 2, kKeyGroups = 2;
 };
 
 template <bool Q8, int D>
