@@ -33,6 +33,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 CONFIGS = {
+    # the reference's CPU-runnable case (Qwen2.5-0.5B, one layer, one sequence).
+    "qwen2.5-0.5b": dict(layers=1, Hq=14, Hkv=2, D=64, L=1025, base=1e6, qk_norm=False, batch=1, scale=None,
+                         softcap=0.0, window_even=0, ff=None, d_model=896),
     # BASELINE config 2 at batch 64 (the north-star target shape).
     "qwen3-4b": dict(layers=36, Hq=32, Hkv=8, D=128, L=4096, base=1e6, qk_norm=True, batch=64, scale=None,
                      softcap=0.0, window_even=0, ff=None, d_model=2560),

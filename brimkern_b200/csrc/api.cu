@@ -294,7 +294,9 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
         a.part_o = part_o;
     } else {
         const size_t cbytes = counters_bytes(batch * p->n_kv_heads * a.mtiles);
-        const size_t need = cbytes + (size_t)nsplit * rows * (2 + D) * sizeof(float);
+        // (m, l) pairs, then the outputs from a 16-byte boundary (the merge reads them as float4).
+        const size_t ml_floats = ((size_t)nsplit * rows * 2 + 3) / 4 * 4;
+        const size_t need = cbytes + (ml_floats + (size_t)nsplit * rows * D) * sizeof(float);
         char *ws;
         if (fixed_ws) {
             if (need > fixed_bytes)
@@ -315,7 +317,7 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
         }
         a.counters = reinterpret_cast<int *>(ws);
         a.part_ml = reinterpret_cast<float *>(ws + cbytes);
-        a.part_o = a.part_ml + (size_t)nsplit * rows * 2;
+        a.part_o = a.part_ml + ml_floats;
         a.out = out;
         a.res_ml = part_ml;
         a.res_o = part_o;

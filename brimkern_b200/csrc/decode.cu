@@ -60,7 +60,7 @@ struct DecodeCfg<true, 64> {
 };
 template <>
 struct DecodeCfg<true, 128> {
-    static constexpr int kStages = 3, kMinBlocks = 4, kDSplit = 1, kKeyGroups = 4;
+    static constexpr int kStages = 2, kMinBlocks = 4, kDSplit = 1, kKeyGroups = 4;
 };
 template <>
 struct DecodeCfg<true, 256> {

@@ -133,38 +133,66 @@ __device__ __forceinline__ void decode_epilogue(const DecodeArgs &a, uint8_t *ri
     named_barrier_sync(1, NC * 32);
     if (!flag[0]) return;
     __threadfence();
-    for (int r = threadIdx.x; r < nvalid; r += NC * 32) {
+    // Row statistics: a warp per row, its lanes over the splits (one round of loads per row).
+    const int mw = threadIdx.x >> 5, ml = threadIdx.x & 31;
+    for (int r = mw; r < nvalid; r += NC) {
         const int rr = row0 + r;
         const size_t R = ((size_t)b * T + rr / G) * a.Hq + kvh * G + rr % G;
-        float M = -CUDART_INF_F;
-        for (int sp = 0; sp < a.nsplit; ++sp) M = fmaxf(M, __ldcg(&a.part_ml[((size_t)sp * rows_total + R) * 2]));
-        float Lsum = 0.f;
-        for (int sp = 0; sp < a.nsplit; ++sp) {
-            const float m = __ldcg(&a.part_ml[((size_t)sp * rows_total + R) * 2]);
-            const float w = m == -CUDART_INF_F ? 0.f : expf(m - M);
+        float mloc = -CUDART_INF_F;
+        for (int sp = ml; sp < a.nsplit; sp += 32)
+            mloc = fmaxf(mloc, __ldcg(&a.part_ml[((size_t)sp * rows_total + R) * 2]));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, off));
+        const float M = mloc;
+        float lloc = 0.f;
+        for (int sp = ml; sp < a.nsplit; sp += 32) {
+            const float2 ml2 = __ldcg(reinterpret_cast<const float2 *>(&a.part_ml[((size_t)sp * rows_total + R) * 2]));
+            const float w = ml2.x == -CUDART_INF_F ? 0.f : expf(ml2.x - M);
             wts[r * a.nsplit + sp] = w;
-            Lsum += w * __ldcg(&a.part_ml[((size_t)sp * rows_total + R) * 2 + 1]);
+            lloc += w * ml2.y;
         }
-        row_l[r] = Lsum;
-        row_m[r] = M;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) lloc += __shfl_xor_sync(0xffffffffu, lloc, off);
+        if (ml == 0) {
+            row_l[r] = lloc;
+            row_m[r] = M;
+        }
     }
     named_barrier_sync(1, NC * 32);
-    for (int idx = threadIdx.x; idx < nvalid * D; idx += NC * 32) {
-        const int r = idx / D, d = idx % D;
+    // Outputs: a thread per (row, 4 head-dim values); eight splits' loads in flight at a time.
+    for (int idx = threadIdx.x; idx < nvalid * (D / 4); idx += NC * 32) {
+        const int r = idx / (D / 4), d4 = idx % (D / 4);
         const int rr = row0 + r;
         const size_t R = ((size_t)b * T + rr / G) * a.Hq + kvh * G + rr % G;
-        float O = 0.f;
-        for (int sp = 0; sp < a.nsplit; ++sp)
-            O += wts[r * a.nsplit + sp] * __ldcg(&a.part_o[((size_t)sp * rows_total + R) * D + d]);
-        if (a.out) {
-            a.out[R * D + d] = O / row_l[r];
-        } else if (a.push_world) {
-            push_partial<D>(a, R, d, O, row_m[r], row_l[r]);
-        } else {
-            a.res_o[R * D + d] = O;
-            if (d == 0) {
-                a.res_ml[R * 2] = row_m[r];
-                a.res_ml[R * 2 + 1] = row_l[r];
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int sp0 = 0; sp0 < a.nsplit; sp0 += 8) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                v[u] = sp0 + u < a.nsplit
+                           ? __ldcg(reinterpret_cast<const float4 *>(&a.part_o[((size_t)(sp0 + u) * rows_total + R) * D]) + d4)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float w = sp0 + u < a.nsplit ? wts[r * a.nsplit + sp0 + u] : 0.f;
+                O.x = fmaf(w, v[u].x, O.x), O.y = fmaf(w, v[u].y, O.y), O.z = fmaf(w, v[u].z, O.z),
+                O.w = fmaf(w, v[u].w, O.w);
+            }
+        }
+        const float o4[4] = {O.x, O.y, O.z, O.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int d = 4 * d4 + e;
+            if (a.out) {
+                a.out[R * D + d] = o4[e] / row_l[r];
+            } else if (a.push_world) {
+                push_partial<D>(a, R, d, o4[e], row_m[r], row_l[r]);
+            } else {
+                a.res_o[R * D + d] = o4[e];
+                if (d == 0) {
+                    a.res_ml[R * 2] = row_m[r];
+                    a.res_ml[R * 2 + 1] = row_l[r];
+                }
             }
         }
     }
