@@ -749,6 +749,9 @@ def main():
     ap.add_argument("--slice", action="store_true",
                     help="decode workloads: the whole attention slice (RMSNorm + q/k/v projections, attention, "
                          "output projection + residual) on one GPU")
+    ap.add_argument("--eager", action="store_true",
+                    help="decode: launch every kernel from the host in the timed loop instead of replaying a CUDA "
+                         "graph of the step (host launch cost then dominates small batches)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
@@ -846,6 +849,25 @@ def main():
     eng.ctx.check()
     barrier()
     torch.cuda.synchronize()
+
+    def capture(fn):
+        """A CUDA graph of fn's launches (the same kernels and arguments), captured on a side
+        stream after the warm-up has sized every workspace."""
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            fn()
+        stream.wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        g.replay()
+        torch.cuda.synchronize()
+        eng.ctx.check()
+        return g
+
+    graph = None if args.eager else capture(step)
     vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
     phys = int(vis[local]) if len(vis) > local and vis[local].strip().isdigit() else local
     sampler = ClockSampler(phys)
@@ -855,24 +877,46 @@ def main():
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record(stream)
     for s in range(args.steps):
-        step()
+        if graph is None:
+            step()
+        else:
+            graph.replay()
     stop.record(stream)
     torch.cuda.synchronize()
-    launches = eng.ctx.launches - n0
+    # Kernels launched in the timed region (a replay launches the captured step's kernels).
+    launches = eng.ctx.launches - n0 if graph is None else (eng.ctx.launches - n0) + args.steps * 2 * layers
     clocks = sampler.stop()
     eng.ctx.check()
     barrier()
     ms_total = start.elapsed_time(stop)
-    # Roofline pass: the same steps with CUDA events bracketing every decode launch (launched
-    # on its own, without the append overlap, so the events time the decode kernel alone).
+    # Roofline pass: the decode kernel alone (no append overlap), every layer's launch back to
+    # back in a CUDA graph timed by CUDA events around the replays (so no host launch gap is
+    # counted); --eager brackets each host-launched decode kernel with events instead.
     rsteps = max(2, min(args.steps, 5))
-    layer_ev = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(layers)]
-                for _ in range(rsteps)]
-    for s in range(rsteps):
-        step(layer_ev[s])
-    torch.cuda.synchronize()
-    eng.ctx.check()
-    attn_ms = [layer_ev[s][l][0].elapsed_time(layer_ev[s][l][1]) for s in range(rsteps) for l in range(layers)]
+
+    def decode_only():
+        for layer in range(layers):
+            eng.recAttention(kv, layer, cfgs[layer], q_work[layer], out[layer], past)
+
+    if args.eager:
+        layer_ev = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+                     for _ in range(layers)] for _ in range(rsteps)]
+        for s in range(rsteps):
+            step(layer_ev[s])
+        torch.cuda.synchronize()
+        eng.ctx.check()
+        attn_ms = [layer_ev[s][l][0].elapsed_time(layer_ev[s][l][1]) for s in range(rsteps) for l in range(layers)]
+    else:
+        dgraph = capture(decode_only)
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record(stream)
+        for _ in range(rsteps):
+            dgraph.replay()
+        r1.record(stream)
+        torch.cuda.synchronize()
+        eng.ctx.check()
+        attn_ms = [r0.elapsed_time(r1) / (rsteps * layers)]
+        del dgraph
     if world > 1:
         t = torch.tensor([ms_total], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -891,7 +935,8 @@ def main():
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
                 "kernel": "decode_kernel<int8>" if q8 else "decode_kernel<fp16>",
-                "timing": f"CUDA events around each decode launch, {rsteps} steps",
+                "timing": (f"CUDA events around each host-launched decode kernel, {rsteps} steps" if args.eager else
+                           f"CUDA events around {rsteps} replays of a graph of the {layers} layers' decode launches"),
                 "bytes_per_launch": bytes_launch,
                 "avg_launch_ms": round(attn_avg_ms, 5), "frac_of_8TBs": round(achieved / 8000.0, 4)}
 
@@ -958,6 +1003,7 @@ def main():
                        "batch_per_gpu": B, "kv_len": Lkv,
                        "layers": layers, "heads": f"{Hq}q/{Hkv}kv", "head_dim": D,
                        "parallelism": f"batch-sharded x{world} (no communication)",
+                       "launch": "host launches" if args.eager else "CUDA-graph replay of the step",
                        "l2": f"no flush: each step streams {bytes_step / 1e9:.1f} GB of KV > 126 MB L2"},
             "tokens_per_s": round(tok_s, 1),
             "frac_of_measured_hbm": round(value / world / peak, 4),
