@@ -622,6 +622,32 @@ def run_slice(args, c, workload):
         step()
     eng.ctx.check()
     torch.cuda.synchronize()
+
+    def capture(fn):
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            fn()
+        stream.wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        g.replay()
+        torch.cuda.synchronize()
+        eng.ctx.check()
+        return g
+
+    def timed(g, reps):
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1) / reps
+
+    graph = None if args.eager else capture(step)
     sampler = ClockSampler(0)
     sampler.start()
     time.sleep(0.3)
@@ -629,22 +655,44 @@ def run_slice(args, c, workload):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        step()
+        if graph is None:
+            step()
+        else:
+            graph.replay()
     e1.record(stream)
     torch.cuda.synchronize()
-    launches = eng.ctx.launches - n0
+    # Per layer: cast + GEMM for q/k/v, append + decode, cast + GEMM for the output.
+    launches = eng.ctx.launches - n0 if graph is None else args.steps * 6 * layers
     clocks = sampler.stop()
     eng.ctx.check()
     ms_step = e0.elapsed_time(e1) / args.steps
     rsteps = max(2, min(args.steps, 5))
-    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(layers)] for _ in range(rsteps)]
-    for si in range(rsteps):
-        step(ev[si])
-    torch.cuda.synchronize()
-    eng.ctx.check()
-    n = rsteps * layers
-    proj_ms = sum(e[0].elapsed_time(e[1]) + e[3].elapsed_time(e[4]) for es in ev for e in es) / n
-    attn_ms = sum(e[2].elapsed_time(e[3]) for es in ev for e in es) / n
+    if args.eager:
+        ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(layers)]
+              for _ in range(rsteps)]
+        for si in range(rsteps):
+            step(ev[si])
+        torch.cuda.synchronize()
+        eng.ctx.check()
+        n = rsteps * layers
+        proj_ms = sum(e[0].elapsed_time(e[1]) + e[3].elapsed_time(e[4]) for es in ev for e in es) / n
+        attn_ms = sum(e[2].elapsed_time(e[3]) for es in ev for e in es) / n
+    else:
+        # The projections alone and the decode kernels alone, each as a graph of every layer's
+        # launches back to back (inputs from the warm-up steps).
+        def projections():
+            for layer in range(layers):
+                eng.projQkv(x[layer], wq[layer], wk[layer], wv[layer], q, k, v, attn_norm=g1[layer], eps=1e-6)
+                eng.projOut(att.view(B, qd), wo[layer], x[layer], h[layer])
+
+        def decodes():
+            for layer in range(layers):
+                eng.recAttention(kv, layer, cfgs[layer], q_work, att, past)
+
+        gp, gd = capture(projections), capture(decodes)
+        proj_ms = timed(gp, rsteps) / layers
+        attn_ms = timed(gd, rsteps) / layers
+        del gp, gd
     wbytes = weight_bytes_per_step(c)
     kbytes = kv_bytes_per_step(c, B)
     value = (wbytes + kbytes) / (ms_step * 1e-3) / 1e9
@@ -688,12 +736,14 @@ def run_slice(args, c, workload):
         "dtype": "f16 weights + f16 KV / f32 accumulate", "data": "synthetic (random-init weights)",
         "config": {"workload": workload + "-slice", "global_batch": B, "kv_len": Lkv, "layers": layers,
                    "d_model": d, "heads": f"{Hq}q/{Hkv}kv", "head_dim": D, "parallelism": "single GPU",
+                   "launch": "host launches" if args.eager else "CUDA-graph replay of the step",
                    "l2": f"no flush: each step streams {(wbytes + kbytes) / 1e9:.1f} GB > 126 MB L2"},
         "tokens_per_s": round(B / (ms_step * 1e-3), 1),
         "roofline": {"bound": "hbm", "achieved": round(proj_ach, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(proj_ach / peak, 4), "traffic": None, "peak_kind": peak_kind,
                      "kernel": "projections (norm_cast + proj_kernel, q/k/v and output)",
-                     "timing": f"CUDA events around projQkv and projOut, {rsteps} steps",
+                     "timing": (f"CUDA events around projQkv and projOut, {rsteps} steps" if args.eager else
+                                f"CUDA events around {rsteps} replays of a graph of every layer's projections"),
                      "bytes_per_layer": wl, "proj_ms_per_layer": round(proj_ms, 5),
                      "attention_ms_per_layer": round(attn_ms, 5), "attention_achieved_gbs": round(attn_ach, 1)},
         "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
