@@ -27,6 +27,8 @@ def _weights(rng, n, k):
     ("qwen05_bias", 10, 896, 896, 128, True, True, False),
     ("gemma_oneplus", 33, 2304, 2048, 1024, True, False, True),
     ("no_norm", 7, 1024, 512, 256, False, False, False),
+    # 48 feature tiles x 2 token tiles: one split, so the bias is added in the epilogue's TMA store.
+    ("one_split_bias", 300, 1024, 4096, 1024, True, True, False),
 ])
 def test_proj_qkv(eng, name, rows, d, qd, kvd, norm, bias, one_plus):
     import torch
@@ -53,6 +55,8 @@ def test_proj_qkv(eng, name, rows, d, qd, kvd, norm, bias, one_plus):
     ("qwen3_decode", 64, 4096, 2560, False),
     ("qwen3_prefill", 300, 4096, 2560, False),
     ("gemma_post_norm", 17, 2048, 2304, True),
+    # 32 feature tiles x 3 token tiles: one split, residual added in the epilogue's TMA store.
+    ("one_split_residual", 600, 1024, 4096, False),
 ])
 def test_proj_out(eng, name, rows, qd, d, post):
     import torch
