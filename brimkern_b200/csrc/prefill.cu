@@ -5,11 +5,11 @@
 //
 // One CTA runs two query streams that share every K/V tile: two q heads of the same kv head
 // (even group size) or two consecutive 128-query tiles of one head (odd group size).  Roles
-// (320 threads):
+// (352 threads):
 //   warps 0-3 / 4-7  softmax warpgroup of stream 0 / 1: thread r owns query row r (TMEM lane r);
 //   warp 8           TMA producer: 64-key K and V tiles (128-byte swizzled [keys][64] boxes,
 //                    CTA-local loads) into a 4-stage (D 64: 6-stage) ring;
-//   warp 9           TMEM allocator and MMA issuer (one elected lane).
+//   warp 9 / 10      MMA issuer of stream 0 / 1 (one lane each); warp 9 also allocates TMEM.
 // Per 64-key tile j and stream s: S_s = Q_s K_j^T (tcgen05.mma, M 128, N 64, fp16 -> fp32 in
 // TMEM); the stream's warpgroup reads S_s once, masks (causal offset pastLen, window) only on
 // boundary tiles, and writes P_s = exp2(s - m) as fp16 to shared memory; the MMA warp
@@ -30,8 +30,9 @@ namespace {
 constexpr int kTQ = 128;       // queries per stream (the MMA's M)
 constexpr int kTK = 64;        // keys per tile (N of QK^T, K of PV)
 constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kThreads = 10 * 32;
+constexpr int kMmaWarp = 9;   // stream 0's MMA issuer (and the TMEM allocator)
+constexpr int kMmaWarp1 = 10; // stream 1's MMA issuer
+constexpr int kThreads = 11 * 32;
 constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O0 | O1
 constexpr float kRescaleLog2 = 8.f;  // raise the running max only when a tile exceeds it by 2^8
 
@@ -66,7 +67,7 @@ enum : int {
     kBarPFull = 16,   // [2] softmax s (P_s written, O_s rescaled) -> MMA
     kBarODone = 18,   // [2] MMA commit (PV_s done: P_s free, O_s stable) -> softmax s
     kBarQFull = 20,   // both warpgroups staged q -> MMA
-    kBarMmaDone = 21, // everything issued has completed -> teardown
+    kBarMmaDone = 21, // [2] everything an issuer issued has completed -> teardown
 };
 
 // Score in log2 units from a raw q.k dot product (monotonic, so maxima commute with it).
@@ -119,7 +120,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < L::kStages; ++i) {
             mbar_init(&bars[kBarKvFull + i], 1);
-            mbar_init(&bars[kBarKvEmpty + i], 1);
+            mbar_init(&bars[kBarKvEmpty + i], active1 ? 2 : 1);  // one commit per MMA issuer
         }
         for (int s = 0; s < 2; ++s) {
             mbar_init(&bars[kBarSFull + s], 1);
@@ -129,6 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(&bars[kBarQFull], 256);
         mbar_init(&bars[kBarMmaDone], 1);
+        mbar_init(&bars[kBarMmaDone + 1], 1);
         fence_barrier_init();
     }
     if (warp == kMmaWarp) {
@@ -173,16 +175,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_wait(&bars[kBarKvFull + j % L::kStages], (j / L::kStages) & 1, a.err, kErrTmaTimeout);
         }
         __syncwarp();
-    } else if (warp == kMmaWarp) {
-        if (lane == 0 && nk > 0) {
+    } else if (warp == kMmaWarp || warp == kMmaWarp1) {
+        // One issuing thread per stream: each stream's S and PV MMAs go out as soon as that
+        // stream's softmax allows, independent of the other stream.
+        const int s = warp - kMmaWarp;
+        if (lane == 0 && nk > 0 && (s == 0 || active1)) {
             constexpr uint32_t idesc_qk = f16_idesc(kTQ, kTK, 0, 0);
             constexpr uint32_t idesc_pv = f16_idesc(kTQ, D, 0, 1);
-            const int ns = active1 ? 2 : 1;
+            // Stream 0's softmax zeroes V rows past the key range in the last tile; stream 1's
+            // PV of that tile waits for it too.
+            const bool tail = klo + nk * kTK > khi;
             bool ok = mbar_wait(&bars[kBarQFull], 0, a.err, kErrMmaTimeout);
-            auto issue_s = [&](int s, int j) -> bool {
+            auto issue_s = [&](int j) -> bool {
                 const int st = j % L::kStages;
-                if (s == 0 && !mbar_wait(&bars[kBarKvFull + st], (j / L::kStages) & 1, a.err, kErrTmaTimeout))
-                    return false;
+                if (!mbar_wait(&bars[kBarKvFull + st], (j / L::kStages) & 1, a.err, kErrTmaTimeout)) return false;
                 if (j >= 1 && !mbar_wait(&bars[kBarSFree + s], (j - 1) & 1, a.err, kErrMmaTimeout)) return false;
                 tc_fence_after();
                 const uint32_t q_base = smem_addr(sQ(s)), k_base = smem_addr(sK(st));
@@ -195,9 +201,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_commit(&bars[kBarSFull + s]);
                 return true;
             };
-            auto issue_pv = [&](int s, int j) -> bool {
+            auto issue_pv = [&](int j) -> bool {
                 const int st = j % L::kStages;
                 if (!mbar_wait(&bars[kBarPFull + s], j & 1, a.err, kErrMmaTimeout)) return false;
+                if (s == 1 && tail && j == nk - 1 && !mbar_wait(&bars[kBarPFull], j & 1, a.err, kErrMmaTimeout))
+                    return false;
                 tc_fence_after();
                 const uint32_t p_base = smem_addr(sP(s)), v_base = smem_addr(sV(st));
 #pragma unroll
@@ -209,21 +217,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_commit(&bars[kBarODone + s]);
                 return true;
             };
-            // S_s(j+1) only needs the softmax to have read S_s(j) (SFree), not its P: issuing both
-            // streams' next QK^T before their PV lets it run under the softmax of tile j.
-            if (ok) ok = issue_s(0, 0) && (ns < 2 || issue_s(1, 0));
+            // S_s(j+1) only needs the softmax to have read S_s(j) (SFree), not its P: issuing it
+            // before PV_s(j) lets it run under the softmax of tile j.
+            if (ok) ok = issue_s(0);
             for (int j = 0; ok && j < nk; ++j) {
-                if (j + 1 < nk) {
-                    if (!issue_s(0, j + 1)) break;
-                    if (ns == 2 && !issue_s(1, j + 1)) break;
-                }
-                if (!issue_pv(0, j)) break;
-                if (ns == 2 && !issue_pv(1, j)) break;
+                if (j + 1 < nk && !issue_s(j + 1)) break;
+                if (!issue_pv(j)) break;
                 tc_commit(&bars[kBarKvEmpty + j % L::kStages]);
             }
             // Every MMA this thread issued must finish before TMEM is released.
-            tc_commit(&bars[kBarMmaDone]);
-            mbar_wait(&bars[kBarMmaDone], 0, a.err, kErrMmaTimeout);
+            tc_commit(&bars[kBarMmaDone + s]);
+            mbar_wait(&bars[kBarMmaDone + s], 0, a.err, kErrMmaTimeout);
         }
         __syncwarp();
     } else {
