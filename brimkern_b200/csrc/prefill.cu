@@ -12,11 +12,12 @@
 //   warp 9 / 10      MMA issuer of stream 0 / 1 (one lane each); warp 9 also allocates TMEM.
 // Per 64-key tile j and stream s: S_s = Q_s K_j^T (tcgen05.mma, M 128, N 64, fp16 -> fp32 in
 // TMEM); the stream's warpgroup reads S_s once, masks (causal offset pastLen, window) only on
-// boundary tiles, and writes P_s = exp2(s - m) as fp16 to shared memory; the MMA warp
-// accumulates O_s += P_s V_j in TMEM.  The running max m is only raised (and O_s rescaled in
+// boundary tiles, and writes P_s = exp2(s - m) as fp16 pairs into TMEM; the MMA warp
+// accumulates O_s += P_s V_j in TMEM with P_s as the MMA's TMEM A operand.  The running max m is only raised (and O_s rescaled in
 // TMEM) when a tile's max exceeds it by more than 2^8, so P stays <= 256 and rescaling is rare.
 // The tensor core alternates between the streams: while one warpgroup works on its scores the
-// other stream's MMAs run.
+// other stream's MMAs run.  Stream 1 starts one tile late, which keeps the two warpgroups'
+// exponential phases (MUFU-bound) apart.
 #include <math_constants.h>
 
 #include "common.cuh"
@@ -46,16 +47,16 @@ struct PrefillLayout {
     static constexpr uint32_t kKVBlock = kTK * 128;            // [64 keys][64] fp16
     static constexpr uint32_t kQBytes = kBlocks * kQBlock;     // one stream's q
     static constexpr uint32_t kTileBytes = kBlocks * kKVBlock; // one K (or V) tile
-    static constexpr uint32_t kPBytes = kTQ * 128;             // [128 rows][64 keys] fp16
     static constexpr uint32_t kOffQ = 0;                       // 2 streams
     static constexpr uint32_t kOffKV = 2 * kQBytes;            // kStages x (K, V)
     static_assert(kStages <= 6, "barrier slots");
-    static constexpr uint32_t kOffP = kOffKV + kStages * 2 * kTileBytes;  // 2 streams
-    static constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;
+    static constexpr uint32_t kOffBar = kOffKV + kStages * 2 * kTileBytes;
     static constexpr uint32_t kNumBars = 24;
     static constexpr uint32_t kSmemBytes = 1024 + kOffBar + kNumBars * 8 + 16;
     static_assert(kSmemBytes <= 232448, "more than 227 KB of shared memory per CTA");
-    static constexpr uint32_t kColS = 0, kColO = 2 * kTK;     // TMEM columns: S_s at s*64, O_s at 128 + s*D
+    // TMEM columns: S_s (f32) at s * 64, O_s (f32) at 128 + s * D, P_s (fp16 pairs) at 128 + 2D + s * 32.
+    static constexpr uint32_t kColS = 0, kColO = 2 * kTK, kColP = 2 * kTK + 2 * D;
+    static_assert(kColP + 2 * kTK / 2 <= kTmemCols, "TMEM columns");
 };
 
 // Barrier slots.
@@ -68,6 +69,7 @@ enum : int {
     kBarODone = 18,   // [2] MMA commit (PV_s done: P_s free, O_s stable) -> softmax s
     kBarQFull = 20,   // both warpgroups staged q -> MMA
     kBarMmaDone = 21, // [2] everything an issuer issued has completed -> teardown
+    kBarStagger = 23, // stream 0's first P written -> stream 1's issuer starts
 };
 
 // Score in log2 units from a raw q.k dot product (monotonic, so maxima commute with it).
@@ -131,6 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&bars[kBarQFull], 256);
         mbar_init(&bars[kBarMmaDone], 1);
         mbar_init(&bars[kBarMmaDone + 1], 1);
+        mbar_init(&bars[kBarStagger], 128);
         fence_barrier_init();
     }
     if (warp == kMmaWarp) {
@@ -145,7 +148,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     auto sQ = [&](int s) { return smem + L::kOffQ + s * L::kQBytes; };
-    auto sP = [&](int s) { return smem + L::kOffP + s * L::kPBytes; };
     auto sK = [&](int st) { return smem + L::kOffKV + st * 2 * L::kTileBytes; };
     auto sV = [&](int st) { return smem + L::kOffKV + st * 2 * L::kTileBytes + L::kTileBytes; };
 
@@ -207,18 +209,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (s == 1 && tail && j == nk - 1 && !mbar_wait(&bars[kBarPFull], j & 1, a.err, kErrMmaTimeout))
                     return false;
                 tc_fence_after();
-                const uint32_t p_base = smem_addr(sP(s)), v_base = smem_addr(sV(st));
+                const uint32_t v_base = smem_addr(sV(st));
 #pragma unroll
                 for (int kk = 0; kk < kTK / 16; ++kk) {
-                    const uint64_t ad = sw128_desc(p_base + kk * 32, 16, 1024);
                     const uint64_t bd = sw128_desc(v_base + kk * 16 * 128, L::kKVBlock, 1024);
-                    tc_mma(tmem + L::kColO + s * D, ad, bd, idesc_pv, j > 0 || kk > 0);
+                    tc_mma_ts(tmem + L::kColO + s * D, tmem + L::kColP + s * (kTK / 2) + kk * 8, bd, idesc_pv,
+                              j > 0 || kk > 0);
                 }
                 tc_commit(&bars[kBarODone + s]);
                 return true;
             };
             // S_s(j+1) only needs the softmax to have read S_s(j) (SFree), not its P: issuing it
             // before PV_s(j) lets it run under the softmax of tile j.
+            // Stream 1 starts one tile behind stream 0, so that one warpgroup's exponentials (MUFU)
+            // overlap the other's TMEM traffic and barrier waits instead of competing with them.
+            if (ok && s == 1) ok = mbar_wait(&bars[kBarStagger], 0, a.err, kErrMmaTimeout);
             if (ok) ok = issue_s(0);
             for (int j = 0; ok && j < nk; ++j) {
                 if (j + 1 < nk && !issue_s(j + 1)) break;
@@ -237,7 +242,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         const int h = s ? head1 : head0, q0 = s ? q01 : q00, nqs = s ? nq1 : nq0;
         uint8_t *sq = sQ(s);
-        uint8_t *sp = sP(s);
         const bool row_ok = r < nqs;
         const int t = q0 + r;
         // Stage q row r as fp16 in the 128-byte swizzled K-major layout of the MMA's A operand.
@@ -374,6 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int lo_max = a.window > 0 ? past + q0 + nqs - 1 - a.window + 1 - a.kv_offset : INT_MIN;
             const uint32_t tS = tmem + L::kColS + s * kTK + lane_base;
             const uint32_t tO = tmem + L::kColO + s * D + lane_base;
+            const uint32_t tP = tmem + L::kColP + s * (kTK / 2) + lane_base;
             float m_used = -CUDART_INF_F;  // max the probabilities are relative to (log2 units)
             float l_run = 0.f;
             bool ok = true;
@@ -454,12 +459,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                 }
-#pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    *reinterpret_cast<uint4 *>(sp + sw128(r, c)) =
-                        make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+                tc_st32(tP, pk);
                 // Keys past the range end: zero their V rows so that 0 * (stale data) stays 0
-                // (one warpgroup does it; PV of both streams waits for both P_s arrivals).
+                // (stream 0's warpgroup does it; stream 1's PV of this tile also waits for P_0).
                 if (s == 0 && kbase + kTK > khi && r < kTK && kbase + r >= khi) {
                     if (!mbar_wait(&bars[kBarKvFull + j % L::kStages], (j / L::kStages) & 1, a.err, kErrTmaTimeout)) {
                         ok = false;
@@ -472,9 +474,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                             *reinterpret_cast<uint4 *>(sV(j % L::kStages) + blk * L::kKVBlock + sw128(r, c)) =
                                 make_uint4(0u, 0u, 0u, 0u);
                 }
-                fence_proxy_async_smem();
+                if (s == 0 && kbase + kTK > khi) fence_proxy_async_smem();  // the zeroed V rows
+                tc_wait_st();
                 tc_fence_before();
                 mbar_arrive(&bars[kBarPFull + s]);
+                if (s == 0 && j == 0) mbar_arrive(&bars[kBarStagger]);
                 l_run += rsum;
             }
             if (ok && nk > 0 && mbar_wait(&bars[kBarODone + s], (nk - 1) & 1, a.err, kErrMmaTimeout)) {

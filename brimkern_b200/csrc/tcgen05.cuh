@@ -26,6 +26,18 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16.  A (M x 16, K-major) sits in TMEM: lane = row,
+// column c = the fp16 pair (2c, 2c + 1) of that row, so one MMA reads 8 columns.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate)
+        : "memory");
+}
+
 // 32 consecutive 32-bit TMEM columns of this thread's lane (no wait).
 __device__ __forceinline__ void tc_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
