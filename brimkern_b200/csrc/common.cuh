@@ -159,6 +159,75 @@ __device__ __forceinline__ float ex2_fast(float x) {
     return y;
 }
 
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// Maximum of N registers as a tree of three-input maxima (depth log3 N instead of a chain of N).
+template <int N>
+__device__ __forceinline__ float max_tree(const float (&v)[N]) {
+    constexpr int M = (N + 2) / 3;
+    float w[M];
+#pragma unroll
+    for (int i = 0; i < M; ++i) {
+        if (3 * i + 2 < N)
+            w[i] = fmax3(v[3 * i], v[3 * i + 1], v[3 * i + 2]);
+        else if (3 * i + 1 < N)
+            w[i] = fmaxf(v[3 * i], v[3 * i + 1]);
+        else
+            w[i] = v[3 * i];
+    }
+    if constexpr (M == 1)
+        return w[0];
+    else
+        return max_tree<M>(w);
+}
+
+// Two lanes of f32 arithmetic in one instruction (sm_100 packed f32x2); each lane rounds like
+// the scalar fmaf / add.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 pa, pb, pc, pd;\n\t"
+        "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\tmov.b64 pc, {%6, %7};\n\t"
+        "fma.rn.f32x2 pd, pa, pb, pc;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 pa, pb, pd;\n\t"
+        "mov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+        "add.rn.f32x2 pd, pa, pb;\n\tmov.b64 {%0, %1}, pd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+// 2^x for two lanes on the FMA pipe, for softmax probabilities that end up as fp16: x = n + f
+// with n = round(x) (adding and subtracting 1.5 * 2^23), f in [-0.5, 0.5]; 2^f from a cubic
+// fitted to 2^f on [-0.5, 0.5] by relative-error least squares (max relative error 1.0e-4,
+// below half an fp16 ulp); n added to the exponent field.  x is clamped at -127 (result 0).
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+    constexpr float kShift = 12582912.f;  // 1.5 * 2^23
+    x.x = fmaxf(x.x, -127.f);
+    x.y = fmaxf(x.y, -127.f);
+    const float2 j = fadd2(x, make_float2(kShift, kShift));
+    const float2 n = fadd2(j, make_float2(-kShift, -kShift));
+    const float2 f = fadd2(x, make_float2(-n.x, -n.y));
+    float2 p = ffma2(make_float2(0.05500883609056473f, 0.05500883609056473f), f,
+                     make_float2(0.24221085011959076f, 0.24221085011959076f));
+    p = ffma2(p, f, make_float2(0.6932829022407532f, 0.6932829022407532f));
+    p = ffma2(p, f, make_float2(1.f, 1.f));
+    // The low bits of j hold n (two's complement); shifted into the exponent field.
+    return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(j.x) << 23)),
+                       __int_as_float(__float_as_int(p.y) + (__float_as_int(j.y) << 23)));
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&h);

@@ -35,7 +35,13 @@ constexpr int kMmaWarp = 9;   // stream 0's MMA issuer (and the TMEM allocator)
 constexpr int kMmaWarp1 = 10; // stream 1's MMA issuer
 constexpr int kThreads = 11 * 32;
 constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O0 | O1
-constexpr float kRescaleLog2 = 8.f;  // raise the running max only when a tile exceeds it by 2^8
+constexpr float kRescaleLog2 = 8.f;
+#ifndef BRK_PF_EMU
+#define BRK_PF_EMU 0
+#endif
+#ifndef BRK_PF_ILP
+#define BRK_PF_ILP 0
+#endif  // raise the running max only when a tile exceeds it by 2^8
 
 template <int D>
 struct PrefillLayout {
@@ -97,15 +103,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = a.Hq / a.Hkv;
     const int T = a.T;
-    const int b = blockIdx.z;
+    const int b = blockIdx.y;
     const int past = a.past_len[b];
     const int ntq = (T + kTQ - 1) / kTQ;
     // Streams: two heads of one kv group sharing a query tile, or (odd group) two query tiles of
-    // one head.  Heaviest (latest) query tiles are scheduled first.
+    // one head.  Heaviest (latest) query tiles are scheduled first: the tile index is the grid's
+    // slowest dimension (blocks start in x, y, z order), so every sequence's heaviest tiles
+    // start before any lighter tile.
     const bool pair_heads = G % 2 == 0;
     const int head0 = pair_heads ? 2 * (int)blockIdx.x : (int)blockIdx.x;
     const int head1 = pair_heads ? head0 + 1 : head0;
-    const int q00 = pair_heads ? (ntq - 1 - (int)blockIdx.y) * kTQ : 2 * ((ntq + 1) / 2 - 1 - (int)blockIdx.y) * kTQ;
+    const int q00 = pair_heads ? (ntq - 1 - (int)blockIdx.z) * kTQ : 2 * ((ntq + 1) / 2 - 1 - (int)blockIdx.z) * kTQ;
     const int q01 = pair_heads ? q00 : q00 + kTQ;
     const int kvh = head0 / G;
     const int nq0 = max(0, min(kTQ, T - q00)), nq1 = max(0, min(kTQ, T - q01));
@@ -406,9 +414,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         v[i] = (key <= hi && key >= lo && key < khi) ? v[i] : -CUDART_INF_F;
                     }
                 }
+#if BRK_PF_ILP
+                const float mraw = max_tree(v);
+#else
                 float mraw = -CUDART_INF_F;
 #pragma unroll
                 for (int i = 0; i < 64; ++i) mraw = fmaxf(mraw, v[i]);
+#endif
                 const float mt = mraw == -CUDART_INF_F ? -CUDART_INF_F : score_log2<CAP>(mraw, a);
                 bool waited_o = false;
                 if (mt > m_used + kRescaleLog2 || (m_used == -CUDART_INF_F && mt != -CUDART_INF_F)) {
@@ -438,8 +450,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float m_eff = m_used == -CUDART_INF_F ? 0.f : m_used;
                 // P_s as packed fp16 in registers first, so that the exponentials overlap the
                 // tensor core's PV_s(j-1); only the stores wait for it to stop reading P_s.
-                float rsum = 0.f;
+                float2 acc[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) acc[k] = make_float2(0.f, 0.f);
                 uint32_t pk[32];
+                const float2 sc2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(-m_eff, -m_eff);
 #pragma unroll
                 for (int u = 0; u < 32; ++u) {
                     float p0, p1;
@@ -447,12 +462,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                         p0 = v[2 * u] == -CUDART_INF_F ? 0.f : ex2_fast(score_log2<CAP>(v[2 * u], a) - m_eff);
                         p1 = v[2 * u + 1] == -CUDART_INF_F ? 0.f : ex2_fast(score_log2<CAP>(v[2 * u + 1], a) - m_eff);
                     } else {
-                        p0 = ex2_fast(fmaf(v[2 * u], a.scale_log2, -m_eff));
-                        p1 = ex2_fast(fmaf(v[2 * u + 1], a.scale_log2, -m_eff));
+#if BRK_PF_ILP
+                        const float2 x = ffma2(make_float2(v[2 * u], v[2 * u + 1]), sc2, nm2);
+#else
+                        const float2 x = make_float2(fmaf(v[2 * u], a.scale_log2, -m_eff), fmaf(v[2 * u + 1], a.scale_log2, -m_eff));
+#endif
+                        if ((u % 8) < BRK_PF_EMU) {
+                            const float2 e = ex2_poly2(x);
+                            p0 = e.x;
+                            p1 = e.y;
+                        } else {
+                            p0 = ex2_fast(x.x);
+                            p1 = ex2_fast(x.y);
+                        }
                     }
-                    rsum += p0 + p1;
+#if BRK_PF_ILP
+                    acc[u & 3] = fadd2(acc[u & 3], make_float2(p0, p1));
+#else
+                    acc[0].x += p0 + p1;
+#endif
                     pk[u] = pack_half2(p0, p1);
                 }
+#if BRK_PF_ILP
+                const float2 acc01 = fadd2(acc[0], acc[1]), acc23 = fadd2(acc[2], acc[3]);
+                const float rsum = (acc01.x + acc01.y) + (acc23.x + acc23.y);
+#else
+                const float rsum = acc[0].x;
+#endif
                 if (j >= 1 && !waited_o) {
                     if (!mbar_wait(&bars[kBarODone + s], (j - 1) & 1, a.err, kErrMmaTimeout)) {
                         ok = false;
@@ -524,7 +560,7 @@ cudaError_t launch_prefill_t(const CUtensorMap &tmk, const CUtensorMap &tmv, con
     }
     const int G = a.Hq / a.Hkv;
     const int ntq = (a.T + kTQ - 1) / kTQ;
-    const dim3 grid(G % 2 == 0 ? a.Hq / 2 : a.Hq, G % 2 == 0 ? ntq : (ntq + 1) / 2, a.B);
+    const dim3 grid(G % 2 == 0 ? a.Hq / 2 : a.Hq, a.B, G % 2 == 0 ? ntq : (ntq + 1) / 2);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kThreads);
