@@ -36,12 +36,9 @@ constexpr int kMmaWarp1 = 10; // stream 1's MMA issuer
 constexpr int kThreads = 11 * 32;
 constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O0 | O1
 constexpr float kRescaleLog2 = 8.f;
-#ifndef BRK_PF_EMU
-#define BRK_PF_EMU 0
-#endif
-#ifndef BRK_PF_ILP
-#define BRK_PF_ILP 0
-#endif  // raise the running max only when a tile exceeds it by 2^8
+// Of every 8 pairs of a row's probabilities, this many take 2^x on the FMA pipe (ex2_poly2)
+// instead of the MUFU unit, which the exponentials otherwise saturate.
+constexpr int kPolyPairsPer8 = 2;  // raise the running max only when a tile exceeds it by 2^8
 
 template <int D>
 struct PrefillLayout {
@@ -414,13 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         v[i] = (key <= hi && key >= lo && key < khi) ? v[i] : -CUDART_INF_F;
                     }
                 }
-#if BRK_PF_ILP
                 const float mraw = max_tree(v);
-#else
-                float mraw = -CUDART_INF_F;
-#pragma unroll
-                for (int i = 0; i < 64; ++i) mraw = fmaxf(mraw, v[i]);
-#endif
                 const float mt = mraw == -CUDART_INF_F ? -CUDART_INF_F : score_log2<CAP>(mraw, a);
                 bool waited_o = false;
                 if (mt > m_used + kRescaleLog2 || (m_used == -CUDART_INF_F && mt != -CUDART_INF_F)) {
@@ -450,6 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float m_eff = m_used == -CUDART_INF_F ? 0.f : m_used;
                 // P_s as packed fp16 in registers first, so that the exponentials overlap the
                 // tensor core's PV_s(j-1); only the stores wait for it to stop reading P_s.
+                // Packed f32x2 arithmetic and four independent row sums keep dependency chains short.
                 float2 acc[4];
 #pragma unroll
                 for (int k = 0; k < 4; ++k) acc[k] = make_float2(0.f, 0.f);
@@ -462,12 +454,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         p0 = v[2 * u] == -CUDART_INF_F ? 0.f : ex2_fast(score_log2<CAP>(v[2 * u], a) - m_eff);
                         p1 = v[2 * u + 1] == -CUDART_INF_F ? 0.f : ex2_fast(score_log2<CAP>(v[2 * u + 1], a) - m_eff);
                     } else {
-#if BRK_PF_ILP
                         const float2 x = ffma2(make_float2(v[2 * u], v[2 * u + 1]), sc2, nm2);
-#else
-                        const float2 x = make_float2(fmaf(v[2 * u], a.scale_log2, -m_eff), fmaf(v[2 * u + 1], a.scale_log2, -m_eff));
-#endif
-                        if ((u % 8) < BRK_PF_EMU) {
+                        if ((u % 8) < kPolyPairsPer8) {
                             const float2 e = ex2_poly2(x);
                             p0 = e.x;
                             p1 = e.y;
@@ -476,19 +464,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                             p1 = ex2_fast(x.y);
                         }
                     }
-#if BRK_PF_ILP
                     acc[u & 3] = fadd2(acc[u & 3], make_float2(p0, p1));
-#else
-                    acc[0].x += p0 + p1;
-#endif
                     pk[u] = pack_half2(p0, p1);
                 }
-#if BRK_PF_ILP
                 const float2 acc01 = fadd2(acc[0], acc[1]), acc23 = fadd2(acc[2], acc[3]);
                 const float rsum = (acc01.x + acc01.y) + (acc23.x + acc23.y);
-#else
-                const float rsum = acc[0].x;
-#endif
                 if (j >= 1 && !waited_o) {
                     if (!mbar_wait(&bars[kBarODone + s], (j - 1) & 1, a.err, kErrMmaTimeout)) {
                         ok = false;
