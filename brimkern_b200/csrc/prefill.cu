@@ -54,7 +54,7 @@ struct PrefillLayout {
     static constexpr uint32_t kOffKV = 2 * kQBytes;            // kStages x (K, V)
     static_assert(kStages <= 6, "barrier slots");
     static constexpr uint32_t kOffBar = kOffKV + kStages * 2 * kTileBytes;
-    static constexpr uint32_t kNumBars = 24;
+    static constexpr uint32_t kNumBars = 25;
     static constexpr uint32_t kSmemBytes = 1024 + kOffBar + kNumBars * 8 + 16;
     static_assert(kSmemBytes <= 232448, "more than 227 KB of shared memory per CTA");
     // TMEM columns: S_s (f32) at s * 64, O_s (f32) at 128 + s * D, P_s (fp16 pairs) at 128 + 2D + s * 32.
@@ -70,9 +70,10 @@ enum : int {
     kBarSFree = 14,   // [2] softmax s (S_s read) -> MMA
     kBarPFull = 16,   // [2] softmax s (P_s written, O_s rescaled) -> MMA
     kBarODone = 18,   // [2] MMA commit (PV_s done: P_s free, O_s stable) -> softmax s
-    kBarQFull = 20,   // both warpgroups staged q -> MMA
+    kBarQFull = 20,   // stream 0's q staged (by all eight softmax warps) -> MMA
     kBarMmaDone = 21, // [2] everything an issuer issued has completed -> teardown
     kBarStagger = 23, // stream 0's first P written -> stream 1's issuer starts
+    kBarQFull1 = 24,  // stream 1's q staged -> MMA
 };
 
 // Score in log2 units from a raw q.k dot product (monotonic, so maxima commute with it).
@@ -136,6 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars[kBarODone + s], 1);
         }
         mbar_init(&bars[kBarQFull], 256);
+        mbar_init(&bars[kBarQFull1], 256);
         mbar_init(&bars[kBarMmaDone], 1);
         mbar_init(&bars[kBarMmaDone + 1], 1);
         mbar_init(&bars[kBarStagger], 128);
@@ -192,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Stream 0's softmax zeroes V rows past the key range in the last tile; stream 1's
             // PV of that tile waits for it too.
             const bool tail = klo + nk * kTK > khi;
-            bool ok = mbar_wait(&bars[kBarQFull], 0, a.err, kErrMmaTimeout);
+            bool ok = mbar_wait(&bars[s ? kBarQFull1 : kBarQFull], 0, a.err, kErrMmaTimeout);
             auto issue_s = [&](int j) -> bool {
                 const int st = j % L::kStages;
                 if (!mbar_wait(&bars[kBarKvFull + st], (j / L::kStages) & 1, a.err, kErrTmaTimeout)) return false;
@@ -246,10 +248,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = threadIdx.x & 127;
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         const int h = s ? head1 : head0, q0 = s ? q01 : q00, nqs = s ? nq1 : nq0;
-        uint8_t *sq = sQ(s);
         const bool row_ok = r < nqs;
         const int t = q0 + r;
-        // Stage q row r as fp16 in the 128-byte swizzled K-major layout of the MMA's A operand.
+        // Stage both streams' q rows as fp16 in the 128-byte swizzled K-major layout of the MMA's
+        // A operand.
         if (a.q_raw) {
             // Fused q prologue: the per-head RMSNorm and NeoX rotation of the stream's query rows
             // (rmsnormCpu kernels.ts:3395, ropeCpu :3445) in f32 with the f32 copy of the table.
@@ -258,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // rotation pairs (i, i + D/2) for i in [l*P, l*P + P), so every load is coalesced and
             // the sum of squares is a warp reduction.
             constexpr int H2 = D / 2, P = H2 / 32;
-            const int wl = warp & 3, i0 = lane * P;
+            const int i0 = lane * P;
             float g0[P], g1[P];
 #pragma unroll
             for (int p = 0; p < P; ++p) {
@@ -266,112 +268,122 @@ __global__ void __launch_bounds__(kThreads, 1)
                 g0[p] = a.q_norm && a.one_plus ? 1.f + w0 : w0;
                 g1[p] = a.q_norm && a.one_plus ? 1.f + w1 : w1;
             }
-            // Rows wl, wl + 4, ... in batches of kB: all loads of a batch are issued before its
-            // first shared-memory store (stores through the generic pointer would otherwise keep
-            // later loads behind them).  (16-row batches measured slower here: 12.48 against
-            // 12.41 ms per prefill step.)
+            // Stream 0's rows first, then stream 1's, each by all eight warps (rows w, w + 8, ...),
+            // so that stream 0's MMAs start after half the staging.  Batches of kB rows: all loads
+            // of a batch are issued before its first shared-memory store (stores through the
+            // generic pointer would otherwise keep later loads behind them).  (16-row batches
+            // measured slower here: 12.48 against 12.41 ms per prefill step.)
             constexpr int kB = 8;
 #pragma unroll 1
-            for (int rb = 0; rb < kTQ / 4; rb += kB) {
-                float x0[kB][P], x1[kB][P], c[kB][P], sn[kB][P];
+            for (int sg = 0; sg < 2; ++sg) {
+                const int hs = sg ? head1 : head0, qs0 = sg ? q01 : q00, nqss = sg ? nq1 : nq0;
+                uint8_t *sqs = sQ(sg);
+#pragma unroll 1
+                for (int rb = 0; rb < kTQ / 8; rb += kB) {
+                    float x0[kB][P], x1[kB][P], c[kB][P], sn[kB][P];
 #pragma unroll
-                for (int u = 0; u < kB; ++u) {
-                    const int rr = wl + 4 * (rb + u);
-                    const bool ok_r = rr < nqs;
-                    const int tr = q0 + rr;
-                    const float *src = a.q_raw + (((size_t)b * T + (ok_r ? tr : 0)) * a.Hq + h) * D;
+                    for (int u = 0; u < kB; ++u) {
+                        const int rr = warp + 8 * (rb + u);
+                        const bool ok_r = rr < nqss;
+                        const int tr = qs0 + rr;
+                        const float *src = a.q_raw + (((size_t)b * T + (ok_r ? tr : 0)) * a.Hq + hs) * D;
 #pragma unroll
-                    for (int p = 0; p < P; ++p) x0[u][p] = x1[u][p] = 0.f, c[u][p] = 1.f, sn[u][p] = 0.f;
-                    if (ok_r) {
-                        if constexpr (P == 2) {
-                            const float2 lo = *reinterpret_cast<const float2 *>(src + i0);
-                            const float2 hi = *reinterpret_cast<const float2 *>(src + i0 + H2);
-                            x0[u][0] = lo.x, x0[u][1] = lo.y, x1[u][0] = hi.x, x1[u][1] = hi.y;
-                            if (a.rope) {
-                                const float4 e = *reinterpret_cast<const float4 *>(a.rope + (size_t)(past + tr) * H2 + i0);
-                                c[u][0] = e.x, sn[u][0] = e.y, c[u][1] = e.z, sn[u][1] = e.w;
-                            }
-                        } else {
-#pragma unroll
-                            for (int p = 0; p < P; ++p) {
-                                x0[u][p] = src[i0 + p], x1[u][p] = src[i0 + p + H2];
+                        for (int p = 0; p < P; ++p) x0[u][p] = x1[u][p] = 0.f, c[u][p] = 1.f, sn[u][p] = 0.f;
+                        if (ok_r) {
+                            if constexpr (P == 2) {
+                                const float2 lo = *reinterpret_cast<const float2 *>(src + i0);
+                                const float2 hi = *reinterpret_cast<const float2 *>(src + i0 + H2);
+                                x0[u][0] = lo.x, x0[u][1] = lo.y, x1[u][0] = hi.x, x1[u][1] = hi.y;
                                 if (a.rope) {
-                                    const float2 e = a.rope[(size_t)(past + tr) * H2 + i0 + p];
-                                    c[u][p] = e.x, sn[u][p] = e.y;
+                                    const float4 e = *reinterpret_cast<const float4 *>(a.rope + (size_t)(past + tr) * H2 + i0);
+                                    c[u][0] = e.x, sn[u][0] = e.y, c[u][1] = e.z, sn[u][1] = e.w;
+                                }
+                            } else {
+#pragma unroll
+                                for (int p = 0; p < P; ++p) {
+                                    x0[u][p] = src[i0 + p], x1[u][p] = src[i0 + p + H2];
+                                    if (a.rope) {
+                                        const float2 e = a.rope[(size_t)(past + tr) * H2 + i0 + p];
+                                        c[u][p] = e.x, sn[u][p] = e.y;
+                                    }
                                 }
                             }
                         }
                     }
+#pragma unroll
+                    for (int u = 0; u < kB; ++u) {
+                        const int rr = warp + 8 * (rb + u);
+                        float inv = 1.f;
+                        if (a.q_norm) {
+                            float ss = 0.f;
+#pragma unroll
+                            for (int p = 0; p < P; ++p) ss = fmaf(x0[u][p], x0[u][p], fmaf(x1[u][p], x1[u][p], ss));
+#pragma unroll
+                            for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+                            inv = 1.f / sqrtf(ss / (float)D + a.eps);
+                        }
+                        float o0[P], o1[P];
+#pragma unroll
+                        for (int p = 0; p < P; ++p) {
+                            const float y0 = x0[u][p] * inv * g0[p], y1 = x1[u][p] * inv * g1[p];
+                            o0[p] = fmaf(y0, c[u][p], -(y1 * sn[u][p]));
+                            o1[p] = fmaf(y1, c[u][p], y0 * sn[u][p]);
+                        }
+                        // Elements i0.. and i0 + D/2..: pieces of the row's swizzled 16-byte chunks.
+                        const int j0 = i0 + H2;
+                        uint8_t *d0 = sqs + (i0 >> 6) * L::kQBlock + sw128(rr, (i0 & 63) >> 3) + (i0 & 7) * 2;
+                        uint8_t *d1 = sqs + (j0 >> 6) * L::kQBlock + sw128(rr, (j0 & 63) >> 3) + (j0 & 7) * 2;
+                        if constexpr (P == 2) {
+                            *reinterpret_cast<uint32_t *>(d0) = pack_half2(o0[0], o0[1]);
+                            *reinterpret_cast<uint32_t *>(d1) = pack_half2(o1[0], o1[1]);
+                        } else {
+                            *reinterpret_cast<__half *>(d0) = __float2half_rn(o0[0]);
+                            *reinterpret_cast<__half *>(d1) = __float2half_rn(o1[0]);
+                        }
+                    }
                 }
-#pragma unroll
-                for (int u = 0; u < kB; ++u) {
-                    const int rr = wl + 4 * (rb + u);
-                    float inv = 1.f;
-                    if (a.q_norm) {
-                        float ss = 0.f;
-#pragma unroll
-                        for (int p = 0; p < P; ++p) ss = fmaf(x0[u][p], x0[u][p], fmaf(x1[u][p], x1[u][p], ss));
-#pragma unroll
-                        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-                        inv = 1.f / sqrtf(ss / (float)D + a.eps);
-                    }
-                    float o0[P], o1[P];
-#pragma unroll
-                    for (int p = 0; p < P; ++p) {
-                        const float y0 = x0[u][p] * inv * g0[p], y1 = x1[u][p] * inv * g1[p];
-                        o0[p] = fmaf(y0, c[u][p], -(y1 * sn[u][p]));
-                        o1[p] = fmaf(y1, c[u][p], y0 * sn[u][p]);
-                    }
-                    // Elements i0.. and i0 + D/2..: pieces of the row's swizzled 16-byte chunks.
-                    const int j0 = i0 + H2;
-                    uint8_t *d0 = sq + (i0 >> 6) * L::kQBlock + sw128(rr, (i0 & 63) >> 3) + (i0 & 7) * 2;
-                    uint8_t *d1 = sq + (j0 >> 6) * L::kQBlock + sw128(rr, (j0 & 63) >> 3) + (j0 & 7) * 2;
-                    if constexpr (P == 2) {
-                        *reinterpret_cast<uint32_t *>(d0) = pack_half2(o0[0], o0[1]);
-                        *reinterpret_cast<uint32_t *>(d1) = pack_half2(o1[0], o1[1]);
-                    } else {
-                        *reinterpret_cast<__half *>(d0) = __float2half_rn(o0[0]);
-                        *reinterpret_cast<__half *>(d1) = __float2half_rn(o1[0]);
-                    }
-                }
+                fence_proxy_async_smem();
+                mbar_arrive(&bars[sg ? kBarQFull1 : kBarQFull]);
             }
-            fence_proxy_async_smem();
-            mbar_arrive(&bars[kBarQFull]);
         } else {
             // Pre-rotated f32 q: one warp per row (lane l: elements 4l.. of each 128-wide half),
-            // batches of 16 rows loaded before their shared-memory stores.
+            // stream by stream as above, 16 rows per warp loaded before their shared-memory stores.
             constexpr int kB = 16, PE = D / 32;  // elements per lane
-            const int wl = warp & 3;
 #pragma unroll 1
-            for (int rb = 0; rb < kTQ / 4; rb += kB) {
-                float x[kB][PE];
+            for (int sg = 0; sg < 2; ++sg) {
+                const int hs = sg ? head1 : head0, qs0 = sg ? q01 : q00, nqss = sg ? nq1 : nq0;
+                uint8_t *sqs = sQ(sg);
+#pragma unroll 1
+                for (int rb = 0; rb < kTQ / 8; rb += kB) {
+                    float x[kB][PE];
 #pragma unroll
-                for (int u = 0; u < kB; ++u) {
-                    const int rr = wl + 4 * (rb + u);
-                    const bool ok_r = rr < nqs;
-                    const float *src = a.q + (((size_t)b * T + (ok_r ? q0 + rr : 0)) * a.Hq + h) * D;
-                    if constexpr (PE == 4) {
-                        const float4 v4 = ok_r ? *reinterpret_cast<const float4 *>(src + 4 * lane)
-                                               : make_float4(0.f, 0.f, 0.f, 0.f);
-                        x[u][0] = v4.x, x[u][1] = v4.y, x[u][2] = v4.z, x[u][3] = v4.w;
-                    } else {
-                        const float2 v2 = ok_r ? *reinterpret_cast<const float2 *>(src + 2 * lane) : make_float2(0.f, 0.f);
-                        x[u][0] = v2.x, x[u][1] = v2.y;
+                    for (int u = 0; u < kB; ++u) {
+                        const int rr = warp + 8 * (rb + u);
+                        const bool ok_r = rr < nqss;
+                        const float *src = a.q + (((size_t)b * T + (ok_r ? qs0 + rr : 0)) * a.Hq + hs) * D;
+                        if constexpr (PE == 4) {
+                            const float4 v4 = ok_r ? *reinterpret_cast<const float4 *>(src + 4 * lane)
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+                            x[u][0] = v4.x, x[u][1] = v4.y, x[u][2] = v4.z, x[u][3] = v4.w;
+                        } else {
+                            const float2 v2 = ok_r ? *reinterpret_cast<const float2 *>(src + 2 * lane) : make_float2(0.f, 0.f);
+                            x[u][0] = v2.x, x[u][1] = v2.y;
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < kB; ++u) {
+                        const int rr = warp + 8 * (rb + u);
+                        const int i = PE * lane;  // first element of this lane
+                        uint8_t *d = sqs + (i >> 6) * L::kQBlock + sw128(rr, (i & 63) >> 3) + (i & 7) * 2;
+                        if constexpr (PE == 4)
+                            *reinterpret_cast<uint2 *>(d) = make_uint2(pack_half2(x[u][0], x[u][1]), pack_half2(x[u][2], x[u][3]));
+                        else
+                            *reinterpret_cast<uint32_t *>(d) = pack_half2(x[u][0], x[u][1]);
                     }
                 }
-#pragma unroll
-                for (int u = 0; u < kB; ++u) {
-                    const int rr = wl + 4 * (rb + u);
-                    const int i = PE * lane;  // first element of this lane
-                    uint8_t *d = sq + (i >> 6) * L::kQBlock + sw128(rr, (i & 63) >> 3) + (i & 7) * 2;
-                    if constexpr (PE == 4)
-                        *reinterpret_cast<uint2 *>(d) = make_uint2(pack_half2(x[u][0], x[u][1]), pack_half2(x[u][2], x[u][3]));
-                    else
-                        *reinterpret_cast<uint32_t *>(d) = pack_half2(x[u][0], x[u][1]);
-                }
+                fence_proxy_async_smem();
+                mbar_arrive(&bars[sg ? kBarQFull1 : kBarQFull]);
             }
-            fence_proxy_async_smem();
-            mbar_arrive(&bars[kBarQFull]);
         }
         if (s == 1 && !active1) {
             // Nothing to do for an empty second stream (odd group, last tile pair).
