@@ -12,7 +12,13 @@ value   = KV bytes read per step (fp16, all layers, all sequences, all ranks) / 
 e2e     = the same metric through the public host API with the step's q/k/v inputs copied from
           pinned host memory and the attention outputs copied back inside the timed region; the
           copies of layer l run on copy streams, overlapped with the attention of other layers.
-N > 1   = weak scaling: every rank runs the full per-GPU batch, no communication on the path.
+N > 1   = strong scaling (default): the global batch (64 for the default workload) is split
+          over the N ranks, B/N independent sequences per GPU, no communication on the path;
+          --weak gives every rank the full batch instead.  value and tokens/s are whole-job
+          figures (all ranks' KV bytes or tokens over the max-over-ranks step time).
+prefill = at N = 1 the default run also measures BASELINE config 3 (Qwen3-4B chunked prefill on
+          the tensor-core kernel) and reports it, with its own roofline and CPU baseline, under
+          the line's "prefill" key (--no-prefill skips it).
 
 --impl reference times the reference's CPU attention (the C restatement of attentionCpu in
 oracle/, the reference itself being TypeScript with no JavaScript runtime on the box) on the
@@ -123,9 +129,40 @@ def load_tflops_peak():
         return 1400.0, 1590.0, "fallback"
 
 
-def run_prefill(args, c, workload):
+def cpu_prefill_sample(c, target_s, seed=13):
+    """Time the CPU attention (oracle restatement of attentionCpu) on a bounded sample of the
+    prefill workload: the last chunk of one sequence of one layer (its queries attend the whole
+    prompt so far), repeated for about target_s seconds.  Returns (TFLOP/s, threads, desc) with the
+    FLOPs counted causal-exact like the GPU line."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(seed)
+    P, T, Hq, Hkv, D = c["L"], c["chunk"], c["Hq"], c["Hkv"], c["D"]
+    past = P - T
+    k = rng.standard_normal(P * Hkv * D, dtype=np.float32)
+    v = rng.standard_normal(P * Hkv * D, dtype=np.float32)
+    q = rng.standard_normal(T * Hq * D, dtype=np.float32)
+    flops = 4 * D * sum(past + t + 1 for t in range(T)) * Hq
+    t0 = time.perf_counter()
+    _, used = O.attention_batch(q, k, v, 1, P * Hkv * D, T, Hq, Hkv, D, [past], c["scale"], c["softcap"], 0, 0)
+    reps = max(1, int(target_s / max(time.perf_counter() - t0, 1e-3)))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.attention_batch(q, k, v, 1, P * Hkv * D, T, Hq, Hkv, D, [past], c["scale"], c["softcap"], 0, 0)
+    dt = time.perf_counter() - t0
+    desc = (f"{reps} x the last {T}-token chunk of one sequence and layer (past {past}, {Hq}q/{Hkv}kv, D {D}), "
+            f"JS-faithful double arithmetic over f32 q/K/V, {used} threads, {dt:.1f} s; FLOPs counted "
+            f"causal-exact as on the GPU")
+    return reps * flops / dt / 1e12, used, desc
+
+
+def run_prefill(args, c, workload, eng=None, emit=True):
     """Prefill bench: a step is the whole prompt through every layer, chunk by chunk: append
-    (QK-norm + RoPE + fp16 store) then the tensor-core prefill kernel over the cache so far."""
+    (QK-norm + RoPE + fp16 store) then the tensor-core prefill kernel over the cache so far.
+    With `eng` (the default decode run at N = 1) it reuses that engine and returns its line
+    instead of printing it."""
     import torch
     import torch.distributed as dist
 
@@ -134,7 +171,8 @@ def run_prefill(args, c, workload):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
+    own_engine = eng is None
+    if world > 1 and own_engine:
         import datetime
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
@@ -143,7 +181,8 @@ def run_prefill(args, c, workload):
     B, P, CH, layers = args.batch, c["L"], c["chunk"], c["layers"]
     Hq, Hkv, D = c["Hq"], c["Hkv"], c["D"]
     nch = (P + CH - 1) // CH
-    eng = AttentionEngine(local)
+    if own_engine:
+        eng = AttentionEngine(local)
     rope = RopeTable(eng.ctx, D, c["base"], None, P)
     gen = torch.Generator(device=dev)
     gen.manual_seed(2000 + rank)
@@ -255,6 +294,11 @@ def run_prefill(args, c, workload):
         e2e = {"value": round(world * step_flops / (e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                "h2d_bytes_per_step": int((hq.numel() + hk.numel() + hv.numel()) * 4),
                "d2h_bytes_per_step": int(hout.numel() * 4), "ms_per_step": round(e_ms, 3)}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        tf, used, desc = cpu_prefill_sample(c, 8.0)
+        cpu = {"value": round(tf, 6), "unit": "TFLOP/s", "cores": used, "kind": "port", "sample": desc}
+    line = None
     if rank == 0:
         line = {
             "metric": "prefill-attn TFLOP/s (causal-exact)", "value": round(value, 2), "unit": "TFLOP/s",
@@ -270,9 +314,14 @@ def run_prefill(args, c, workload):
                          "traffic": None, "peak_kind": kind + " sustained bf16 (fp16 runs at the same rate)",
                          "kernel": "prefill_attn_kernel", "timing": f"CUDA events around each prefill launch, {rsteps} steps",
                          "flops_per_step": step_flops, "kernel_ms_per_step": round(kern_ms, 4)},
-            "cpu_baseline": None, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
         }
-        print(json.dumps(line), flush=True)
+        if emit:
+            print(json.dumps(line), flush=True)
+    kv.close()
+    rope.close()
+    if not own_engine:
+        return line
     eng.close()
     if world > 1:
         dist.destroy_process_group()
@@ -753,6 +802,22 @@ def run_slice(args, c, workload):
     return 0
 
 
+def decode_config(c, workload, B, world, scaling, launch=None):
+    """The `config` object of a decode line, shared by this build's arm and the reference arm so
+    that both name the same workload."""
+    bytes_step = kv_bytes_per_step(c, B)
+    q8 = c.get("kv") == "q8"
+    cfg = {"workload": workload, "kv_cache": "int8" if q8 else "fp16", "global_batch": B * world,
+           "batch_per_gpu": B, "kv_len": c["L"], "layers": c["layers"], "heads": f"{c['Hq']}q/{c['Hkv']}kv",
+           "head_dim": c["D"],
+           "parallelism": (f"batch-sharded x{world}: {B} of {B * world} sequences per GPU, no communication "
+                           f"({scaling} scaling)"),
+           "l2": f"no flush: each step streams {bytes_step / 1e9:.1f} GB of KV per GPU > 126 MB L2"}
+    if launch:
+        cfg["launch"] = launch
+    return cfg
+
+
 def run_reference(args, c, workload):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -764,20 +829,31 @@ def run_reference(args, c, workload):
         if i >= args.warmup:
             vals.append(gbs)
     value = sum(vals) / len(vals)
+    world = max(1, args.gpus)
     tok_s = value * 1e9 / (kv_bytes_per_step(c, 1))
     line = {
         "metric": "decode-attn KV-read GB/s", "value": round(value, 4), "unit": "GB/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(kv_bytes_per_step(c, args.batch) / (value * 1e9) * 1e3, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": workload, "global_batch": args.batch * args.gpus, "kv_len": c["L"],
-                   "layers": c["layers"], "parallelism": "cpu"},
+        # A whole step of the workload would take minutes on the host cores: each of the `steps`
+        # timed samples runs ~2 s of whole (layer, sequence) units, and the per-step time is the
+        # workload's bytes at the sampled rate.
+        "ms_per_step": round(kv_bytes_per_step(c, args.batch * world) / (value * 1e9) * 1e3, 3),
+        "ms_per_step_kind": "extrapolated from the sampled rate (whole steps are not run on the CPU)",
+        "sampled": {"seconds_per_step": per_step_s, "rates_gbs": [round(v, 4) for v in vals]},
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic",
+        "config": decode_config(c, workload, args.batch, world, args.scaling),
         "tokens_per_s": round(tok_s, 3),
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": used, "kind": "port", "sample": desc},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def workload_sharded(workload):
+    # The long-context workload shards the KV sequence over the ranks (config 5).
+    return workload == "llama3.2-1b-long"
 
 
 def main():
@@ -787,7 +863,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=list(CONFIGS), default="qwen3-4b")
-    ap.add_argument("--batch", type=int, default=None, help="sequences per GPU")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="decode: global batch split over the GPUs (per GPU with --weak); prefill: per GPU")
+    ap.add_argument("--weak", action="store_true",
+                    help="decode on N GPUs: every GPU runs the full batch (weak scaling) instead of 1/N of it")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="default decode run: skip the embedded config-3 prefill measurement")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count (tests only)")
     ap.add_argument("--kv-len", type=int, default=None, help="override the KV length (tests only)")
     ap.add_argument("--softcap", type=float, default=None, help="override the logit softcap (diagnostics)")
@@ -814,10 +895,22 @@ def main():
         c["softcap"] = args.softcap
     if args.window is not None:
         c["window_even"] = args.window
-    args.batch = args.batch or c["batch"]
-    args.warmup = max(args.warmup, 3)
     c["kv"] = args.kv
     workload = args.workload
+    world = int(os.environ.get("WORLD_SIZE", str(max(1, args.gpus) if args.impl == "reference" else 1)))
+    decode = not c.get("prefill") and not args.slice and not (workload_sharded(workload) and world > 1)
+    if decode and not args.weak:
+        # Strong scaling: the global batch is split over the ranks.
+        glob = args.batch or c["batch"]
+        if glob % world:
+            print(json.dumps({"error": f"global batch {glob} is not a multiple of {world} GPUs (use --weak)"}))
+            return 2
+        args.batch = glob // world
+        args.scaling = "strong"
+    else:
+        args.batch = args.batch or c["batch"]
+        args.scaling = "weak"
+    args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args, c, workload)
     if c.get("prefill"):
@@ -918,6 +1011,12 @@ def main():
         return g
 
     graph = None if args.eager else capture(step)
+    import ctypes
+
+    from brimkern_b200 import _lib as L
+    _p = cfgs[-1].params()
+    nsplit = L.lib().brk_attn_decode_splits(eng.ctx.handle, kv.handle, ctypes.byref(_p), B, 1,
+                                            (ctypes.c_int32 * B)(*past))
     vis = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
     phys = int(vis[local]) if len(vis) > local and vis[local].strip().isdigit() else local
     sampler = ClockSampler(phys)
@@ -1042,24 +1141,35 @@ def main():
         gbs, used, desc = cpu_reference_sample(c, B, 10.0)
         cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": used, "kind": "port", "sample": desc}
 
+    line = None
     if rank == 0:
         line = {
             "metric": "decode-attn KV-read GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
+            "scaling": args.scaling, "vs_baseline": None,
             "dtype": "int8 KV + f32 row scales / f32 accumulate" if q8 else "f16 KV / f32 accumulate",
             "data": "synthetic",
-            "config": {"workload": workload, "kv_cache": "int8" if q8 else "fp16", "global_batch": B * world,
-                       "batch_per_gpu": B, "kv_len": Lkv,
-                       "layers": layers, "heads": f"{Hq}q/{Hkv}kv", "head_dim": D,
-                       "parallelism": f"batch-sharded x{world} (no communication)",
-                       "launch": "host launches" if args.eager else "CUDA-graph replay of the step",
-                       "l2": f"no flush: each step streams {bytes_step / 1e9:.1f} GB of KV > 126 MB L2"},
+            "config": decode_config(c, workload, B, world, args.scaling,
+                                    "host launches" if args.eager else "CUDA-graph replay of the step"),
             "tokens_per_s": round(tok_s, 1),
             "frac_of_measured_hbm": round(value / world / peak, 4),
+            "decode_splits": nsplit,
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
             "clocks": clocks,
         }
+    if world == 1 and not args.no_prefill and not q8 and workload == "qwen3-4b" and args.batch == 64:
+        # BASELINE config 3 in the same run: the tensor-core prefill, with its own roofline and CPU
+        # baseline, nested under "prefill" (the decode step's buffers are released first).
+        if graph is not None:
+            del graph
+        kv.close()
+        del q_in, k_in, v_in, q_work, out
+        torch.cuda.empty_cache()
+        pc = dict(CONFIGS["qwen3-4b-prefill"])
+        pargs = argparse.Namespace(**vars(args))
+        pargs.batch, pargs.steps, pargs.warmup, pargs.no_e2e = pc["batch"], 5, 3, args.no_e2e
+        line["prefill"] = run_prefill(pargs, pc, "qwen3-4b-prefill", eng=eng, emit=False)
+    if rank == 0:
         print(json.dumps(line), flush=True)
     eng.close()
     if world > 1:

@@ -71,7 +71,7 @@ SIGNATURES = [
     ("brk_kv_destroy", _i, [_vp]),
     ("brk_kv_capacity", _i, [_vp]),
     ("brk_kv_grow", _i, [_vp, _i, _vp]),
-    ("brk_kv_reset", _i, [_vp, _vp]),
+    ("brk_kv_reset", _i, [_vp, _i, _vp]),
     ("brk_kv_write_rows", _i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     ("brk_kv_read_rows", _i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp]),
     ("brk_kv_write_codes", _i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp]),
@@ -80,6 +80,7 @@ SIGNATURES = [
     ("brk_attn_step", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp, _vp, _vp, _vp]),
     ("brk_attn_forward", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp]),
     ("brk_attn_decode", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp]),
+    ("brk_attn_decode_splits", _i, [_vp, _vp, _PARAMS, _i, _i, _i32p]),
     ("brk_attn_decode_static", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp]),
     ("brk_attn_prefill", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp]),
     ("brk_attn_prefill_step", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp, _vp, _vp]),

@@ -236,9 +236,56 @@ int choose_splits(const brk_ctx *ctx, int head_dim, bool q8, int units, int span
     return best_n;
 }
 
+// Split plan of a decode call: the longest attended range over the batch (rows beyond the cache
+// capacity are an error unless clamp_rows), the split count and the keys per split (a multiple
+// of the ring's stage keys).
+int decode_split_plan(const brk_ctx *ctx, const brk_kv *kv, const brk_attn_params *p, int batch, int n_tokens,
+                      const int32_t *past_len, bool clamp_rows, int *nsplit_out, int *keys_per_split_out) {
+    const int D = p->head_dim;
+    const int window = p->window > 0 ? p->window : 0;
+    int span = 1;
+    for (int b = 0; b < batch; ++b) {
+        int hi = past_len[b] + n_tokens - p->kv_offset;
+        if (hi > kv->cap) {
+            if (!clamp_rows)
+                return fail(BRK_ERR_CAPACITY, "sequence %d needs %d cache rows, capacity is %d (grow the cache)", b, hi,
+                            kv->cap);
+            hi = kv->cap;
+        }
+        int lo = window > 0 ? std::max(0, past_len[b] - window + 1 - p->kv_offset) : 0;
+        span = std::max(span, hi - lo);
+    }
+    const int G = p->n_heads / p->n_kv_heads;
+    const int rt = brk::decode_rows_per_tile();
+    const int units = batch * p->n_kv_heads * ((n_tokens * G + rt - 1) / rt);
+    int nsplit = choose_splits(ctx, D, kv->q8(), units, span);
+    const int tk = brk::decode_stage_keys(D);
+    const int kps = ((span + nsplit - 1) / nsplit + tk - 1) / tk * tk;
+    *keys_per_split_out = kps;
+    *nsplit_out = (span + kps - 1) / kps;
+    return BRK_OK;
+}
+
 // The decode path (final output or a partial), splitting the key range over CTAs.
-// Split-KV scratch layout: arrival counters (kept zero between launches), then the partials.
+// Static split-KV scratch layout: arrival counters (cleared by each call), then the partials.
 size_t counters_bytes(int units) { return ((size_t)units * sizeof(int) + 255) / 256 * 256; }
+
+// Split-KV arrival counters for at least n tiles (zeroed; a larger buffer replaces a smaller one
+// after the device is idle, so that no queued kernel still counts in the old one).
+constexpr size_t kInitialCounters = 1u << 16;
+int ensure_counters(brk_ctx *ctx, size_t n) {
+    if (n <= ctx->counters_n) return BRK_OK;
+    const size_t want = std::max(n, 2 * ctx->counters_n);
+    DeviceGuard g(ctx->device);
+    BRK_CUDA(cudaDeviceSynchronize());
+    cudaFree(ctx->counters);
+    ctx->counters = nullptr;
+    ctx->counters_n = 0;
+    BRK_CUDA(cudaMalloc(&ctx->counters, want * sizeof(int)));
+    BRK_CUDA(cudaMemset(ctx->counters, 0, want * sizeof(int)));
+    ctx->counters_n = want;
+    return BRK_OK;
+}
 
 // fixed_ws / fixed_bytes: when set, the split-KV scratch goes there and nothing is allocated
 // (brk_attn_decode_static); otherwise the context workspace is used and grown on demand.
@@ -271,24 +318,11 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
         a.cap_k1 = (float)(2.0 * (double)a.scale * log2e / (double)a.softcap);
         a.cap_k2 = (float)((double)a.softcap * log2e);
     }
-    int span = 1;
-    for (int b = 0; b < batch; ++b) {
-        a.past_len[b] = past_len[b];
-        int hi = past_len[b] + n_tokens - p->kv_offset;
-        if (hi > kv->cap) {
-            if (!clamp_rows)
-                return fail(BRK_ERR_CAPACITY, "sequence %d needs %d cache rows, capacity is %d (grow the cache)", b, hi,
-                            kv->cap);
-            hi = kv->cap;
-        }
-        int lo = a.window > 0 ? std::max(0, past_len[b] - a.window + 1 - p->kv_offset) : 0;
-        span = std::max(span, hi - lo);
-    }
+    for (int b = 0; b < batch; ++b) a.past_len[b] = past_len[b];
+    int nsplit = 1;
+    int rc = decode_split_plan(ctx, kv, p, batch, n_tokens, past_len, clamp_rows, &nsplit, &a.keys_per_split);
+    if (rc) return rc;
     const int units = batch * p->n_kv_heads * a.mtiles;
-    int nsplit = choose_splits(ctx, D, kv->q8(), units, span);
-    const int tk = brk::decode_stage_keys(D);
-    a.keys_per_split = ((span + nsplit - 1) / nsplit + tk - 1) / tk * tk;
-    nsplit = (span + a.keys_per_split - 1) / a.keys_per_split;
     a.nsplit = nsplit;
     const int rows = batch * n_tokens * p->n_heads;
 
@@ -297,12 +331,14 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
         a.part_ml = part_ml;
         a.part_o = part_o;
     } else {
-        const size_t cbytes = counters_bytes(batch * p->n_kv_heads * a.mtiles);
         // (m, l) pairs, then the outputs from a 16-byte boundary (the merge reads them as float4).
         const size_t ml_floats = ((size_t)nsplit * rows * 2 + 3) / 4 * 4;
-        const size_t need = cbytes + (ml_floats + (size_t)nsplit * rows * D) * sizeof(float);
+        const size_t part_bytes = (ml_floats + (size_t)nsplit * rows * D) * sizeof(float);
         char *ws;
         if (fixed_ws) {
+            // The static array holds the counters too, cleared by every call.
+            const size_t cbytes = counters_bytes(units);
+            const size_t need = cbytes + part_bytes;
             if (need > fixed_bytes)
                 return fail(BRK_ERR_CAPACITY,
                             "%d-way split-KV partials of %d rows need %zu bytes of scratch; the library's static "
@@ -312,15 +348,19 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
             // The counters must start at zero; the array keeps whatever the last call left.
             cudaError_t e = cudaMemsetAsync(ws, 0, cbytes, stream);
             if (e != cudaSuccess) return cuda_fail(e, "clearing the static split counters");
+            a.counters = reinterpret_cast<int *>(ws);
+            ws += cbytes;
         } else {
-            if (need > ctx->ws_bytes) {
-                int rc = brk_ctx_reserve(ctx, need);
+            if (part_bytes > ctx->ws_bytes) {
+                rc = brk_ctx_reserve(ctx, part_bytes);
                 if (rc) return rc;
             }
+            rc = ensure_counters(ctx, (size_t)units);
+            if (rc) return rc;
             ws = static_cast<char *>(ctx->ws);
+            a.counters = ctx->counters;
         }
-        a.counters = reinterpret_cast<int *>(ws);
-        a.part_ml = reinterpret_cast<float *>(ws + cbytes);
+        a.part_ml = reinterpret_cast<float *>(ws);
         a.part_o = a.part_ml + ml_floats;
         a.out = out;
         a.res_ml = part_ml;
@@ -402,8 +442,28 @@ int brk_ctx_create(int device, brk_ctx **out) {
     cudaError_t e = cudaMalloc(&c->d_err, sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, sizeof(int));
     if (e != cudaSuccess) {
+        cudaFree(c->d_err);
         delete c;
         return cuda_fail(e, "context error word");
+    }
+    // Everything brk_attn_decode_static needs on this device is taken here, so that its calls
+    // allocate nothing: the decode kernels are loaded (lazy module loading would load them, and
+    // take their device memory, at the first launch) and the static scratch array's module is
+    // loaded (its BRK_DECODE_STATIC_SCRATCH_BYTES are taken then) with its address cached.
+    e = brk::preload_decode_kernels();
+    if (e != cudaSuccess) {
+        cudaFree(c->d_err);
+        delete c;
+        return cuda_fail(e, "loading the decode kernels");
+    }
+    void *scratch = nullptr;
+    int rc = static_scratch_address(&scratch);
+    if (rc == BRK_OK) rc = ensure_counters(c, kInitialCounters);
+    if (rc) {
+        cudaFree(c->counters);
+        cudaFree(c->d_err);
+        delete c;
+        return rc;
     }
     *out = c;
     return BRK_OK;
@@ -414,6 +474,7 @@ int brk_ctx_destroy(brk_ctx *ctx) {
     DeviceGuard g(ctx->device);
     cudaDeviceSynchronize();
     cudaFree(ctx->d_err);
+    cudaFree(ctx->counters);
     cudaFree(ctx->ws);
     cudaFree(ctx->stage);
     cudaFree(ctx->act);
@@ -430,7 +491,7 @@ int brk_ctx_check(brk_ctx *ctx, void *stream) {
     if (err) {
         BRK_CUDA(cudaMemset(ctx->d_err, 0, sizeof(int)));
         // A kernel that gave up may have left split counters mid-count: start them from zero.
-        if (ctx->ws) BRK_CUDA(cudaMemset(ctx->ws, 0, ctx->ws_bytes));
+        if (ctx->counters) BRK_CUDA(cudaMemset(ctx->counters, 0, ctx->counters_n * sizeof(int)));
         return fail(BRK_ERR_DEVICE, "a kernel gave up on a bounded wait (code %d)", err);
     }
     return BRK_OK;
@@ -447,7 +508,6 @@ int brk_ctx_reserve(brk_ctx *ctx, size_t bytes) {
     ctx->ws = nullptr;
     ctx->ws_bytes = 0;
     BRK_CUDA(cudaMalloc(&ctx->ws, bytes));
-    BRK_CUDA(cudaMemset(ctx->ws, 0, bytes));  // split counters start at zero
     ctx->ws_bytes = bytes;
     return BRK_OK;
 }
@@ -614,11 +674,35 @@ int brk_kv_grow(brk_kv *kv, int rows, void *stream) {
     return kv_build_maps(kv);
 }
 
-int brk_kv_reset(brk_kv *kv, void *stream) {
+int brk_kv_reset(brk_kv *kv, int seq, void *stream) {
     if (!kv) return fail(BRK_ERR_INVALID, "null kv");
+    const brk_kv_desc &d = kv->desc;
+    if (seq < -1 || seq >= d.batch) return fail(BRK_ERR_INVALID, "sequence %d outside [-1, %d)", seq, d.batch);
     DeviceGuard g(kv->ctx->device);
-    cudaError_t e = kv_zero(kv, static_cast<cudaStream_t>(stream));
-    return e == cudaSuccess ? BRK_OK : cuda_fail(e, "kv reset");
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (seq < 0) {
+        cudaError_t e = kv_zero(kv, s);
+        return e == cudaSuccess ? BRK_OK : cuda_fail(e, "kv reset");
+    }
+    // One sequence: for every layer its n_kv_heads segments are contiguous, [layer][seq][head]
+    // -> a 2-D memset with one row per layer, pitched by the batch's segments.
+    const size_t esz = kv->q8() ? 1 : sizeof(__half);
+    const size_t width = (size_t)d.n_kv_heads * kv->cap * d.head_dim * esz;
+    const size_t pitch = width * d.batch;
+    const size_t off = width * seq;
+    cudaError_t e;
+    if (kv->q8()) {
+        e = cudaMemset2DAsync(kv->k8 + off, pitch, 0x80, width, d.n_layers, s);
+        if (e == cudaSuccess) e = cudaMemset2DAsync(kv->v8 + off, pitch, 0x80, width, d.n_layers, s);
+        const size_t swidth = (size_t)d.n_kv_heads * 2 * kv->scale_pitch * sizeof(float);
+        if (e == cudaSuccess)
+            e = cudaMemset2DAsync(reinterpret_cast<char *>(kv->scales) + swidth * seq, swidth * d.batch, 0, swidth,
+                                  d.n_layers, s);
+    } else {
+        e = cudaMemset2DAsync(reinterpret_cast<char *>(kv->k) + off, pitch, 0, width, d.n_layers, s);
+        if (e == cudaSuccess) e = cudaMemset2DAsync(reinterpret_cast<char *>(kv->v) + off, pitch, 0, width, d.n_layers, s);
+    }
+    return e == cudaSuccess ? BRK_OK : cuda_fail(e, "kv reset of one sequence");
 }
 
 static int check_rows(const brk_kv *kv, int layer, int seq, int row0, int n_rows) {
@@ -793,6 +877,15 @@ int brk_attn_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_pa
     DeviceGuard g(ctx->device);
     return run_decode(ctx, kv, layer, p, batch, n_tokens, past_len, q, out, nullptr, nullptr, false,
                       static_cast<cudaStream_t>(stream));
+}
+
+int brk_attn_decode_splits(brk_ctx *ctx, const brk_kv *kv, const brk_attn_params *p, int batch, int n_tokens,
+                           const int32_t *past_len) {
+    int rc = check_call(ctx, kv, 0, p, batch, n_tokens, past_len);
+    if (rc) return rc;
+    int nsplit = 1, kps = 0;
+    rc = decode_split_plan(ctx, kv, p, batch, n_tokens, past_len, false, &nsplit, &kps);
+    return rc ? rc : nsplit;
 }
 
 // No-allocation variant of brk_attn_decode (declared in brk_attn.h with the reasons).

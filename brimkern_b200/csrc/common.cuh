@@ -208,10 +208,12 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
     return d;
 }
 
-// 2^x for two lanes on the FMA pipe, for softmax probabilities that end up as fp16: x = n + f
-// with n = round(x) (adding and subtracting 1.5 * 2^23), f in [-0.5, 0.5]; 2^f from a cubic
-// fitted to 2^f on [-0.5, 0.5] by relative-error least squares (max relative error 1.0e-4,
-// below half an fp16 ulp); n added to the exponent field.  x is clamped at -127 (result 0).
+// 2^x for two lanes on the FMA pipe, for softmax probabilities that end up as fp16.  The method
+// is the textbook range reduction of exp2 (as in Cody and Waite's elementary-function
+// algorithms) followed by a minimax-style polynomial: x = n + f with n = round(x) (adding and
+// subtracting 1.5 * 2^23), f in [-0.5, 0.5]; 2^f from a cubic fitted here to 2^f on
+// [-0.5, 0.5] by relative-error least squares (max relative error 1.0e-4, below half an fp16
+// ulp); n added to the exponent field.  x is clamped at -127 (result 0).
 __device__ __forceinline__ float2 ex2_poly2(float2 x) {
     constexpr float kShift = 12582912.f;  // 1.5 * 2^23
     x.x = fmaxf(x.x, -127.f);

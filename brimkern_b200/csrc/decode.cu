@@ -612,6 +612,21 @@ int ctas_t() {
 
 int decode_rows_per_tile() { return kRT; }
 
+cudaError_t preload_decode_kernels() {
+    // With lazy module loading a kernel's code is loaded, and its device memory taken, at the
+    // first launch; asking for its attributes loads it now.
+    const void *fns[] = {(const void *)decode_kernel<false, 64>, (const void *)decode_kernel<false, 128>,
+                         (const void *)decode_kernel<false, 256>, (const void *)decode_kernel<true, 64>,
+                         (const void *)decode_kernel<true, 128>,  (const void *)decode_kernel<true, 256>,
+                         (const void *)combine_kernel,            (const void *)combine_peers_kernel};
+    for (const void *f : fns) {
+        cudaFuncAttributes fa;
+        cudaError_t e = cudaFuncGetAttributes(&fa, f);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
 int decode_ctas_per_sm(int head_dim, bool q8) {
     switch (head_dim) {
         case 64: return q8 ? ctas_t<true, 64>() : ctas_t<false, 64>();

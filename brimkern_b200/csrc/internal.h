@@ -15,8 +15,14 @@ struct brk_ctx {
     int device = 0;
     int num_sms = 0;
     int *d_err = nullptr;      // device error word written by bounded waits (brk::DeviceError)
-    void *ws = nullptr;        // split-KV workspace
+    void *ws = nullptr;        // split-KV partials: (m, l) pairs, then the outputs
     size_t ws_bytes = 0;
+    // Split-KV arrival counters, one per (sequence, kv head, row tile) of a launch; each launch's
+    // last arriver puts its counter back to zero.  A buffer of their own: were they part of the
+    // partials' workspace, a launch with fewer tiles would write partials over the counters of
+    // tiles that a later, larger launch counts on being zero.
+    int *counters = nullptr;
+    size_t counters_n = 0;
     void *stage = nullptr;     // fp16 staging of an int8 cache layer for the prefill kernel
     size_t stage_bytes = 0;
     void *act = nullptr;       // fp16 activations of the projection GEMMs
@@ -164,6 +170,8 @@ cudaError_t launch_decode(bool q8, int head_dim, const CUtensorMap &tmk, const C
                           const CUtensorMap &tms, const DecodeArgs &a, int grid_x, int grid_y, int grid_z,
                           cudaStream_t s, bool pdl);
 int decode_rows_per_tile();
+// Loads every decode / combine kernel on the current device now instead of at its first launch.
+cudaError_t preload_decode_kernels();
 cudaError_t launch_combine(const CombineArgs &a, cudaStream_t s);
 // Combine after a bounded wait (wait_ns) until flags[p] == epoch for every p < world.
 cudaError_t launch_combine_peers(const CombineArgs &a, const unsigned *flags, int world, unsigned epoch,

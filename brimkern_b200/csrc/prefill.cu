@@ -35,10 +35,11 @@ constexpr int kMmaWarp = 9;   // stream 0's MMA issuer (and the TMEM allocator)
 constexpr int kMmaWarp1 = 10; // stream 1's MMA issuer
 constexpr int kThreads = 11 * 32;
 constexpr uint32_t kTmemCols = 512;  // S0 | S1 | O0 | O1
+// Raise the running max (and rescale O) only when a tile's max exceeds it by more than 2^8.
 constexpr float kRescaleLog2 = 8.f;
 // Of every 8 pairs of a row's probabilities, this many take 2^x on the FMA pipe (ex2_poly2)
 // instead of the MUFU unit, which the exponentials otherwise saturate.
-constexpr int kPolyPairsPer8 = 2;  // raise the running max only when a tile exceeds it by 2^8
+constexpr int kPolyPairsPer8 = 2;
 
 template <int D>
 struct PrefillLayout {

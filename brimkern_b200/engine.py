@@ -145,8 +145,9 @@ class KvCache:
         """ensureKv growth rule: capacity -> max(rows, capacity + 1024, 1024) when rows > capacity."""
         check(L.lib().brk_kv_grow(self.handle, int(rows), _stream_ptr(stream)))
 
-    def reset(self, stream=None) -> None:
-        check(L.lib().brk_kv_reset(self.handle, _stream_ptr(stream)))
+    def reset(self, seq: int = -1, stream=None) -> None:
+        """Zero sequence `seq`'s rows in every layer (all sequences when seq == -1)."""
+        check(L.lib().brk_kv_reset(self.handle, int(seq), _stream_ptr(stream)))
 
     def write_rows(self, layer: int, seq: int, row0: int, k: torch.Tensor, v: torch.Tensor, stream=None) -> None:
         """f32 rows [n, n_kv_heads, D] stored as fp16, or quantised (quantize_kv) in an int8 cache."""
@@ -262,6 +263,7 @@ class AttentionEngine:
         self.kvGpu: Optional[KvCache] = None
         self.lfm2KvGpu: dict = {}  # LFM2 attention layer -> its own cache (kernels.ts:1990)
         self.kvSession = ""
+        self.seqSessions: dict = {}  # sequence -> session id (batched caches, session(seq=...))
         self.kvQuant = False
 
     # ---- plumbing ---------------------------------------------------------------------
@@ -437,6 +439,7 @@ class AttentionEngine:
             kv.close()
         self.lfm2KvGpu = {}
         self.kvSession = ""
+        self.seqSessions = {}
 
     def clearKvCache(self) -> None:
         self.resetKvGpu()
@@ -489,10 +492,24 @@ class AttentionEngine:
         return self.prefillChunked(kv, 0, cfg, q_in, k_in, v_in, base, chunk=chunk or self.LFM2_PREFILL_CHUNK,
                                    stream=stream)
 
-    def session(self, session_id: str, past_len) -> None:
+    def session(self, session_id: str, past_len, seq: Optional[int] = None) -> None:
         """runDecodeGpu's session rule (kernels.ts:1817-1825): a new session id or pastLen 0
-        resets the cache; pastLen > 0 on an unknown session means the cache is lost (raised)."""
+        resets the cache; pastLen > 0 on an unknown session means the cache is lost (raised).
+
+        With ``seq`` the rule applies to one sequence of the batched cache (one session per
+        sequence): only that sequence's rows are cleared (brk_kv_reset(kv, seq)), the others
+        keep theirs."""
         first = int(past_len) if np.isscalar(past_len) else int(min(past_len))
+        if seq is not None:
+            seq = int(seq)
+            if session_id != self.seqSessions.get(seq) or first == 0:
+                if first > 0:
+                    raise BrkError(L.BRK_ERR_INVALID, f'session "{session_id}" unknown on sequence {seq} with '
+                                                      f'pastLen={first}: cache lost, restart at 0')
+                if self.kvGpu is not None:
+                    self.kvGpu.reset(seq)
+                self.seqSessions[seq] = session_id
+            return
         if session_id != self.kvSession or first == 0:
             if first > 0:
                 raise BrkError(L.BRK_ERR_INVALID,

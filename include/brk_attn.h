@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define BRK_ABI_VERSION 1
+#define BRK_ABI_VERSION 2
 #define BRK_MAX_BATCH 512 /* sequences per call (positions travel in the kernel parameters) */
 
 enum {
@@ -116,8 +116,12 @@ int brk_kv_capacity(const brk_kv *kv);
 /* ensureKv (kernels.ts:1782-1806): if rows > capacity, grow to max(rows, capacity+1024, 1024)
  * with a device-side copy of the existing rows. */
 int brk_kv_grow(brk_kv *kv, int rows, void *stream);
-/* clearKvCache (kernels.ts:1777): zero every row. */
-int brk_kv_reset(brk_kv *kv, void *stream);
+/* clearKvCache / resetKvGpu (kernels.ts:1766-1777) and the session restart of runDecodeGpu
+ * (kernels.ts:1817-1825: a new session or pastLen 0 starts the cache over): zero the rows of
+ * sequence `seq` in every layer, leaving the other sequences' rows untouched, or of every
+ * sequence when seq == -1 (the reference holds a single session; a batch holds one per
+ * sequence).  Stream-ordered, no allocation. */
+int brk_kv_reset(brk_kv *kv, int seq, void *stream);
 /* Plain row store, no norm or rotation: the f32 copy of kernels.ts:1729-1730 for callers that
  * already hold final K/V, f32 -> fp16 (round to nearest even); for an int8 cache the quantize_kv
  * pass of recQuantizeKv (kernels.ts:1644-1648).  k, v: [n_rows][n_kv_heads][D] f32 (either may
@@ -169,6 +173,13 @@ int brk_attn_forward(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_p
 int brk_attn_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p,
                     int batch, int n_tokens, const int32_t *past_len, const float *q, float *out,
                     void *stream);
+/* The number of key-range splits (CTAs per (sequence, kv head, row tile)) that brk_attn_decode
+ * and brk_attn_step pick for this call: an automatic choice from the GPU's CTA slots and the
+ * longest attended range, or BRK_DECODE_SPLITS when set.  Returns the count (>= 1) or a
+ * negative BRK_ERR_* code.  Launches nothing (diagnostics, tests and benchmarks).  No reference
+ * counterpart (the reference never splits the key range). */
+int brk_attn_decode_splits(brk_ctx *ctx, const brk_kv *kv, const brk_attn_params *p, int batch,
+                           int n_tokens, const int32_t *past_len);
 /* No-allocation variant of brk_attn_decode.  No counterpart in the reference: it exists for
  * callers of this library that cannot allocate device memory while they run attention -- for
  * example serving hosts that hand nearly all of HBM to their own KV-cache pool at start-up (a
@@ -178,16 +189,21 @@ int brk_attn_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_pa
  * the partials in a fixed array compiled into the library and calls no allocator.
  *   - Same arguments, outputs and split choice as brk_attn_decode.  The caller still provides
  *     q and out.
- *   - The array holds BRK_DECODE_STATIC_SCRATCH_BYTES.  A call whose split-KV partials need
- *     more (nsplit * batch * n_tokens * n_heads * (head_dim + 2) * 4 bytes) fails with
- *     BRK_ERR_CAPACITY and a message giving both sizes.
- *   - Every GPU that loads the library holds one such array until the process exits.
- *   - The first call on each device looks up the array's device address (with that device
- *     current); make that first call before any stream capture.
+ *   - The array holds BRK_DECODE_STATIC_SCRATCH_BYTES.  A call that splits the key range
+ *     (brk_attn_decode_splits > 1) needs, with rows = batch * n_tokens * n_heads and
+ *     tiles = batch * n_kv_heads * ceil(n_tokens * n_heads / n_kv_heads / 8):
+ *       round_up(4 * tiles, 256) + 4 * (round_up(2 * nsplit * rows, 4) + nsplit * rows * head_dim)
+ *     bytes (arrival counters, (m, l) pairs, partial outputs); a call that needs more fails with
+ *     BRK_ERR_CAPACITY and a message giving both sizes.  A one-split call uses none of it.
+ *   - The array and the decode kernels are loaded on a device by the first brk_ctx_create for
+ *     that device (the array's memory is taken then and held until the process exits), so
+ *     create the context before handing the rest of HBM to a pool; the calls themselves do no
+ *     set-up and allocate nothing.
  *   - All calls on a device share the array and it keeps the last call's contents.  Each call
- *     writes every partial it reads before reading it, so nothing needs clearing, but calls
- *     whose kernels overlap on the GPU (other streams, other contexts on the same device) race
- *     on it: serialise them. */
+ *     clears its arrival counters with one cudaMemsetAsync on the caller's stream before the
+ *     kernel, and the kernel writes every partial before reading it.  Calls whose kernels
+ *     overlap on the GPU (other streams, other contexts on the same device) race on the array:
+ *     serialise them. */
 #define BRK_DECODE_STATIC_SCRATCH_BYTES (8u << 20)
 int brk_attn_decode_static(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p,
                            int batch, int n_tokens, const int32_t *past_len, const float *q,

@@ -1,8 +1,9 @@
 """Generate golden fixtures by executing the reference's own CPU functions.
 
-Run here, where the reference is mounted (default ``/root/reference``, or ``$BRK_REFERENCE``):
+Run where the reference source tree is checked out, naming its root (the directory that holds
+``src/lib/webgpu/kernels.ts``) as the argument or in ``$BRK_REFERENCE``:
 
-    python tests/golden/gen_golden.py
+    python tests/golden/gen_golden.py <path-to-Brimkern-checkout>
 
 It extracts ``attentionCpu``, ``ropeCpu``, ``ropeFactorsCpu`` and ``rmsnormCpu`` verbatim from
 ``src/lib/webgpu/kernels.ts`` (lines 3395-3495), and the inline reference loop of the
@@ -27,7 +28,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 import jsmini  # noqa: E402
 
-REF = os.environ.get("BRK_REFERENCE", "/root/reference")
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("BRK_REFERENCE", "")
 KERNELS_TS = os.path.join(REF, "src", "lib", "webgpu", "kernels.ts")
 FUNCS = ["rmsnormCpu", "ropeFactorsCpu", "ropeCpu", "attentionCpu"]
 
@@ -145,6 +146,9 @@ def run_case(interp, c):
 
 
 def main():
+    if not REF or not os.path.isfile(KERNELS_TS):
+        sys.exit("usage: gen_golden.py <Brimkern checkout> (or set BRK_REFERENCE); "
+                 f"no src/lib/webgpu/kernels.ts under {REF!r}")
     src = open(KERNELS_TS, encoding="utf-8").read()
     interp = jsmini.Interpreter()
     for f in FUNCS:

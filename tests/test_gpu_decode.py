@@ -99,7 +99,7 @@ def test_ragged_lengths(eng, past):
     _run_decode(eng, f"ragged{past}", 14, 2, 64, [past])
 
 
-@pytest.mark.parametrize("splits", [1, 2, 3, 16])
+@pytest.mark.parametrize("splits", [1, 2, 3, 4, 16])
 def test_forced_splits(eng, splits):
     _run_decode(eng, f"split{splits}", 32, 8, 128, [2047, 999], splits=splits)
 

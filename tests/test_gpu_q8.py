@@ -188,7 +188,7 @@ def test_q8_ragged(eng, past):
     _run_q8(eng, f"q8_ragged{past}", 14, 2, 64, [past])
 
 
-@pytest.mark.parametrize("splits", [1, 3, 16])
+@pytest.mark.parametrize("splits", [1, 3, 4, 16])
 def test_q8_forced_splits(eng, splits):
     _run_q8(eng, f"q8_split{splits}", 32, 8, 128, [2047, 999], splits=splits)
 
