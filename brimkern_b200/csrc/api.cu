@@ -204,8 +204,15 @@ float effective_scale(const brk_attn_params *p) {
     return p->scale > 0.f ? p->scale : (float)(1.0 / std::sqrt((double)p->head_dim));
 }
 
-// Splits of the key range per (sequence, kv head, row tile): enough CTAs to fill the GPU's
-// concurrent slots without leaving a mostly-empty last wave; BRK_DECODE_SPLITS overrides.
+// Splits of the key range per (sequence, kv head, row tile); BRK_DECODE_SPLITS overrides.
+//  - Grids of one wave or less: a CTA streams its range at a bounded rate (its ring holds a few
+//    stages), so the grid needs about 1.5 CTAs per SM in flight to keep HBM busy, and every CTA
+//    beyond that only adds fixed cost (ring ramp, partial, merge).  The fewest splits that reach
+//    that many CTAs, within one wave.  Measured on B200 (Qwen3-4B shapes, head_dim 128, L 4096,
+//    cluster merge): B 8 kernel 30.4 / 28.0 / 24.8 / 26.8 us at 2 / 3 / 4 / 6 splits; B 16 44.0 /
+//    44.8 / 53.6 us at 2 / 3 / 4 splits.
+//  - Larger grids: enough CTAs to fill the GPU's concurrent slots without leaving a mostly-empty
+//    last wave, each CTA's fixed cost counted as four stages.
 int choose_splits(const brk_ctx *ctx, int head_dim, bool q8, int units, int span) {
     const int tk = brk::decode_stage_keys(head_dim);
     const int max_split = std::max(1, std::min(64, (span + tk - 1) / tk));
@@ -218,6 +225,16 @@ int choose_splits(const brk_ctx *ctx, int head_dim, bool q8, int units, int span
     // (pipeline ramp, partial write, its share of the merge).  Measured on B200 at B 1, L 4096,
     // head_dim 128: 16 splits of 256 keys ran 1.51 TB/s, 32 of 128 keys 1.40, 64 of 64 keys 0.93.
     const int max_auto = std::max(1, std::min(max_split, span / (4 * tk)));
+    // int8 caches are issue-bound (a CTA converts every code), so their CTAs stream slowly and the
+    // multi-wave model below suits them at every size; head_dim 256 splits the head dim over warp
+    // pairs and streams slower per CTA than 64 / 128 (Gemma-2 B 32: 3 splits 6554 GB/s, 2 splits
+    // 6428 GB/s).
+    if (units < slots && !q8) {
+        const long long target = head_dim > 128 ? (5LL * ctx->num_sms + 1) / 2 : (3LL * ctx->num_sms + 1) / 2;
+        int n = (int)std::min<long long>(max_auto, (target + units - 1) / units);
+        while (n > 1 && (long long)units * n > slots) --n;
+        return std::max(1, n);
+    }
     double best = 1e30;
     int best_n = 1;
     for (int n = 1; n <= max_auto; ++n) {
@@ -290,10 +307,17 @@ int ensure_counters(brk_ctx *ctx, size_t n) {
 // fixed_ws / fixed_bytes: when set, the split-KV scratch goes there and nothing is allocated
 // (brk_attn_decode_static); otherwise the context workspace is used and grown on demand.
 // pdl: the decode kernel is a programmatic dependent of the append launched just before it.
+// The append fused into the decode launch (brk_attn_step with one token): raw projections in,
+// rotated q out.
+struct FusedAppend {
+    const float *q_in, *k_in, *v_in;
+    float *q_work;
+};
+
 int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
                const int32_t *past_len, const float *q, float *out, float *part_ml, float *part_o, bool clamp_rows,
                cudaStream_t stream, void *fixed_ws = nullptr, size_t fixed_bytes = 0, bool pdl = false,
-               brk_peer *push = nullptr, uint32_t epoch = 0) {
+               brk_peer *push = nullptr, uint32_t epoch = 0, const FusedAppend *fused = nullptr) {
     const int D = p->head_dim, G = p->n_heads / p->n_kv_heads;
     brk::DecodeArgs a;
     memset(&a, 0, sizeof(a));
@@ -326,10 +350,20 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
     a.nsplit = nsplit;
     const int rows = batch * n_tokens * p->n_heads;
 
+    // Small grids (every CTA resident at once) merge their splits through a thread-block cluster
+    // instead of global partials and a last-arriver merge; the static entry point keeps the
+    // workspace merge (its scratch array is what it is for), and so do push launches.
+    const bool cluster = nsplit > 1 && nsplit <= 16 && !fixed_ws && !push && !getenv("BRK_DECODE_NO_CLUSTER") &&
+                         units <= brk::decode_max_clusters(D, kv->q8(), nsplit);
     if (nsplit == 1) {
         a.out = out;  // final output, or (out == nullptr) the caller's partial buffer directly
         a.part_ml = part_ml;
         a.part_o = part_o;
+    } else if (cluster) {
+        a.cluster = 1;
+        a.out = out;
+        a.res_ml = part_ml;
+        a.res_o = part_o;
     } else {
         // (m, l) pairs, then the outputs from a 16-byte boundary (the merge reads them as float4).
         const size_t ml_floats = ((size_t)nsplit * rows * 2 + 3) / 4 * 4;
@@ -365,6 +399,26 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
         a.out = out;
         a.res_ml = part_ml;
         a.res_o = part_o;
+    }
+    if (fused) {
+        a.fuse = 1;
+        a.q = fused->q_work;
+        a.q_rot = fused->q_work;
+        a.q_in = fused->q_in;
+        a.k_in = fused->k_in;
+        a.v_in = fused->v_in;
+        a.kc = kv->k;
+        a.vc = kv->v;
+        a.kc8 = kv->k8;
+        a.vc8 = kv->v8;
+        a.scales = kv->scales;
+        a.scale_pitch = kv->scale_pitch;
+        a.rope = p->rope ? p->rope->table : nullptr;
+        a.rope32 = p->rope ? p->rope->table32 : nullptr;
+        a.q_norm = p->q_norm;
+        a.k_norm = p->k_norm;
+        a.eps = p->eps;
+        a.one_plus = p->norm_one_plus ? 1 : 0;
     }
     if (push) {
         // This rank's block (parity epoch & 1, source `rank`) of every rank's exchange area.
@@ -862,6 +916,21 @@ int brk_attn_step(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p,
         if (past_len[b] + n_tokens - p->kv_offset > kv->cap)
             return fail(BRK_ERR_CAPACITY, "sequence %d needs %d cache rows, capacity is %d (grow the cache)", b,
                         past_len[b] + n_tokens - p->kv_offset, kv->cap);
+    if (n_tokens == 1 && (p->head_dim != 256 || p->n_heads / p->n_kv_heads <= 4)) {
+        // One token: the append runs inside the decode launch (no second kernel, no dependency
+        // between launches; head_dim 256 stages up to 4 q rows per tile); the same checks as
+        // brk_attn_append.
+        if (p->rope && (p->rope->head_dim != p->head_dim || p->rope->ctx != ctx))
+            return fail(BRK_ERR_INVALID, "rope table head_dim %d != %d", p->rope->head_dim, p->head_dim);
+        for (int b = 0; b < batch; ++b)
+            if (p->rope && past_len[b] + 1 > p->rope->max_pos)
+                return fail(BRK_ERR_CAPACITY, "position %d beyond the rope table (%d positions)", past_len[b],
+                            p->rope->max_pos);
+        DeviceGuard g(ctx->device);
+        const FusedAppend f{q_in, k_in, v_in, q_work};
+        return run_decode(ctx, kv, layer, p, batch, n_tokens, past_len, q_work, out, nullptr, nullptr, false,
+                          static_cast<cudaStream_t>(stream), nullptr, 0, true, nullptr, 0, &f);
+    }
     rc = append_impl(ctx, kv, layer, p, batch, n_tokens, past_len, q_in, k_in, v_in, q_work, stream, true);
     if (rc) return rc;
     DeviceGuard g(ctx->device);

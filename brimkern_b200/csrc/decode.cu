@@ -30,6 +30,7 @@
 // Tiles whose keys every row of the tile may attend (all but the causal / window edges and the
 // range end) skip the per-score masks.
 #include "decode_common.cuh"
+#include "kv_q8.cuh"
 
 namespace brk {
 
@@ -86,13 +87,112 @@ struct DecodeLayout {
     static constexpr uint32_t kStageBytes = (kLoadBytes + 1023) / 1024 * 1024;
     static constexpr uint32_t kRingBytes = C::kStages * kStageBytes;
     // Score swap of the head-dim halves: [key group][parity][half][lane][4] floats.
-    static constexpr uint32_t kXBytes = kDS > 1 ? kKG * 2 * 2 * 32 * 4 * 4 : 0;
-    static constexpr uint32_t kBarBytes = 2 * C::kStages * 8;
-    static constexpr uint32_t kSmemBytes = 1024 + kRingBytes + kXBytes + kBarBytes;
+    static constexpr uint32_t kSwapBytes = kDS > 1 ? kKG * 2 * 2 * 32 * 4 * 4 : 0;
+    // Fused append: the tile's rotated q rows [kQRows][D + 8] f32 (padded against bank conflicts),
+    // in the same bytes as the score swap (used only before the main loop).  head_dim 256 stages
+    // up to 4 rows (GQA groups up to 4 fuse), the others a whole tile.
+    static constexpr int kQRows = D == 256 ? 4 : 8;
+    static constexpr uint32_t kQStride = D + 8;
+    static constexpr uint32_t kQBytes = kQRows * kQStride * 4;
+    static constexpr uint32_t kXBytes = kSwapBytes > kQBytes ? kSwapBytes : kQBytes;
+    // Fused append into an int8 cache: the new K and V rows in f32, quantised from here.
+    static constexpr uint32_t kNewRowBytes = Q8 ? 2 * D * 4 : 0;
+    static constexpr uint32_t kBarBytes = 2 * C::kStages * 8;  // full, empty
+    static constexpr uint32_t kSmemBytes = 1024 + kRingBytes + kXBytes + kNewRowBytes + kBarBytes;
     static_assert(decode_epilogue_bytes<D, kKG, kRT>() <= kRingBytes, "merge buffers must fit in the ring");
 };
 
+// rmsnormCpu + ropeCpu (kernels.ts:3395, 3445) of one head row by one warp, in the append
+// kernel's fp64 operations (append.cu; the same bits): the ordered sum of squares by lane 0, then
+// per pair (i, i + D/2) with i = lane + 32 u: y = f32(x * inv * g), rotated in double, rounded to
+// f32 into o0 / o1.  gain == nullptr: no norm; cs == nullptr: no rotation.
+template <int D>
+__device__ __forceinline__ void rotate_row_warp(const float *src, const float *gain, double eps, int one_plus,
+                                                const double2 *cs, int lane, float (&o0)[D / 64], float (&o1)[D / 64]) {
+    constexpr int H2 = D / 2, NP = D / 64;
+    double y0[NP], y1[NP];
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+        y0[u] = src[lane + 32 * u];
+        y1[u] = src[lane + 32 * u + H2];
+    }
+    if (gain) {
+        double inv = 0.0;
+        if (lane == 0) {
+            double ss = 0.0;
+#pragma unroll 16
+            for (int d = 0; d < D; ++d) {
+                const double xd = (double)src[d];
+                ss = __fma_rn(xd, xd, ss);  // x^2 is exact in double: one rounding, as ss + x*x
+            }
+            inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)D), eps)));
+        }
+        inv = __shfl_sync(0xffffffffu, inv, 0);
+#pragma unroll
+        for (int u = 0; u < NP; ++u) {
+            const int i = lane + 32 * u;
+            const double w0 = gain[i], w1 = gain[i + H2];
+            const double g0 = one_plus ? __dadd_rn(1.0, w0) : w0, g1 = one_plus ? __dadd_rn(1.0, w1) : w1;
+            y0[u] = (double)(float)__dmul_rn(__dmul_rn(y0[u], inv), g0);
+            y1[u] = (double)(float)__dmul_rn(__dmul_rn(y1[u], inv), g1);
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+        if (cs) {
+            const double2 e = cs[lane + 32 * u];
+            o0[u] = (float)__dsub_rn(__dmul_rn(y0[u], e.x), __dmul_rn(y1[u], e.y));
+            o1[u] = (float)__dadd_rn(__dmul_rn(y1[u], e.x), __dmul_rn(y0[u], e.y));
+        } else {
+            o0[u] = (float)y0[u];
+            o1[u] = (float)y1[u];
+        }
+    }
+}
+
+// The new token's K (QK-norm + RoPE with the append kernel's fp64 operations, hence its bits) and
+// V rows of the fused append, computed and stored in the cache by the producer warp (after it
+// has put the first ring stages in flight, before the stage that holds the new row): fp16
+// rounded to nearest even, or quantised as quantize_kv does.  Each lane fences its stores for
+// the async proxy, which the warp's next TMA load of that row requires.
 template <bool Q8, int D>
+__device__ __noinline__ void fused_kv_rows(const DecodeArgs &a, int b, int kvh, int past, int seg, float *newrow,
+                                           int lane) {
+    constexpr int H2 = D / 2, NP = D / 64;
+    const double2 *cs = a.rope ? a.rope + (size_t)past * H2 : nullptr;
+    const size_t crow = (size_t)seg * a.cap + (size_t)(past - a.kv_offset);
+#pragma unroll 1
+    for (int which = 0; which < 2; ++which) {
+        const bool is_k = which == 0;
+        const float *src = (is_k ? a.k_in : a.v_in) + ((size_t)b * a.Hkv + kvh) * D;
+        float o0[NP], o1[NP];
+        rotate_row_warp<D>(src, is_k ? a.k_norm : nullptr, a.eps, a.one_plus, is_k ? cs : nullptr, lane, o0, o1);
+        if constexpr (Q8) {
+            float *x = newrow + which * D;
+#pragma unroll
+            for (int u = 0; u < NP; ++u) {
+                x[lane + 32 * u] = o0[u];
+                x[lane + 32 * u + H2] = o1[u];
+            }
+            __syncwarp();
+            quantize_row_warp(x, D, (is_k ? a.kc8 : a.vc8) + crow * D,
+                              a.scales + ((size_t)seg * 2 + which) * a.scale_pitch + (size_t)(past - a.kv_offset),
+                              lane);
+        } else {
+            __half *dst = (is_k ? a.kc : a.vc) + crow * D;
+#pragma unroll
+            for (int u = 0; u < NP; ++u) {
+                dst[lane + 32 * u] = __float2half_rn(o0[u]);
+                dst[lane + 32 * u + H2] = __float2half_rn(o1[u]);
+            }
+        }
+    }
+    fence_proxy_async_global();
+}
+
+// F: the fused-append form (brk_attn_step with one token); a separate instantiation, so that the
+// plain kernel's code and registers stay as they are.
+template <bool Q8, int D, bool F>
 __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D>::kMinBlocks)
     decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                    const __grid_constant__ CUtensorMap tms, const __grid_constant__ DecodeArgs a) {
@@ -114,7 +214,8 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *ring = smem;
     float *xbuf = reinterpret_cast<float *>(ring + L::kRingBytes);
-    uint64_t *full = reinterpret_cast<uint64_t *>(ring + L::kRingBytes + L::kXBytes);
+    float *newrow = reinterpret_cast<float *>(ring + L::kRingBytes + L::kXBytes);  // int8: [2][D]
+    uint64_t *full = reinterpret_cast<uint64_t *>(ring + L::kRingBytes + L::kXBytes + L::kNewRowBytes);
     uint64_t *empty = full + S;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -131,6 +232,10 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
     const KeyRange kr = decode_key_range(a, past, row0, nrows, split, SK, Q8 ? 4 : 1, kRT);
     const int k_begin = kr.k_begin, k_end = kr.k_end, ntiles = kr.ntiles;
     const int seg = (a.layer * a.B + b) * a.Hkv + kvh;
+    // Fused append: this CTA writes the new token's K / V rows (cache row past - kv_offset) when
+    // its key range holds them, before its ring loads that row.
+    const int new_row = past - a.kv_offset;
+    const bool writes_row = F && new_row >= k_begin && new_row < k_end;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -143,23 +248,19 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
 
     if (warp == NC) {
         // ---- producer: one elected lane streams the stages through the ring.
-        if (lane == 0 && ntiles > 0) {
-            tma_prefetch_desc(&tmk);
-            tma_prefetch_desc(&tmv);
-            if constexpr (Q8) tma_prefetch_desc(&tms);
-            int issued = 0;
-            bool waited = false;
-            // Rows from dep_row on may be written by a preceding kernel (the append, when this
-            // launch is its programmatic dependent): stages touching them wait for it to finish.
-            const int dep_row = past - a.kv_offset;
-            for (int i = 0; i < ntiles; ++i) {
+        // Fused append: the warp pauses after the first ring stages (or before the stage holding
+        // the new row, if that comes first) to compute and store the new K / V rows.
+        const int pause = writes_row ? min(S, (new_row - k_begin) / SK) : ntiles;
+        int issued = 0;
+        bool ok = true;
+        auto issue = [&](int i_end) {
+            for (int i = issued; i < i_end && ok; ++i) {
                 const int s = i % S;
                 const int key = k_begin + i * SK;
-                if (!waited && key + SK > dep_row) {
-                    griddep_wait();
-                    waited = true;
+                if (i >= S && !mbar_wait(&empty[s], ((i / S) - 1) & 1, a.err, kErrSlotTimeout)) {
+                    ok = false;
+                    break;
                 }
-                if (i >= S && !mbar_wait(&empty[s], ((i / S) - 1) & 1, a.err, kErrSlotTimeout)) break;
                 mbar_arrive_expect_tx(&full[s], L::kLoadBytes);
                 uint8_t *st = ring + s * L::kStageBytes;
                 const int y = seg * a.cap + key;
@@ -171,24 +272,102 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
                 if constexpr (Q8) tma_load_2d(st + 2 * L::kTileBytes, &tms, key, seg * 2, &full[s]);
                 issued = i + 1;
             }
-            // Before leaving, make sure every copy this lane started has landed (bounded).
-            for (int i = issued > S ? issued - S : 0; i < issued; ++i)
-                mbar_wait(&full[i % S], (i / S) & 1, a.err, kErrTmaTimeout);
+        };
+        if (ntiles > 0) {
+            if (lane == 0) {
+                tma_prefetch_desc(&tmk);
+                tma_prefetch_desc(&tmv);
+                if constexpr (Q8) tma_prefetch_desc(&tms);
+            }
+            // As a programmatic dependent this CTA may start before the preceding kernel has
+            // finished; cache rows (and the fused append's inputs) may come from it or, as kernels
+            // that trigger their dependents early wait for their own predecessors before they
+            // finish, from anything the stream ran before.  The CTA's set-up has overlapped it.
+            griddep_wait();
+            if (lane == 0) issue(pause);
+            if constexpr (F) {
+                if (writes_row) {
+                    __syncwarp();
+                    fused_kv_rows<Q8, D>(a, b, kvh, past, seg, newrow, lane);
+                    __syncwarp();  // every lane's row stores and proxy fence before the row's load
+                }
+            }
+            if (lane == 0) {
+                issue(ntiles);
+                // Before leaving, make sure every copy this lane started has landed (bounded).
+                for (int i = issued > S ? issued - S : 0; i < issued; ++i)
+                    mbar_wait(&full[i % S], (i / S) & 1, a.err, kErrTmaTimeout);
+            }
+        }
+        if (a.cluster) {
+            __syncwarp();
+            decode_cluster_idle();  // the cluster merge's two barriers count every thread
         }
         return;
     }
 
-    griddep_wait();  // q comes from the preceding append when launched as its dependent
+    griddep_wait();  // q (or, fused, q_in / k_in / v_in) may come from the preceding kernel
     const int kg = warp % KG;  // key group: keys [16 kg, 16 kg + 16) of every stage
     const int dh = warp / KG;  // head-dim slice [DH dh, DH dh + DH)
     const int qr = lane >> 2, qc = lane & 3;
 
-    // Q^T fragments (B operand, column qr = query row row0 + qr), fp32 -> fp16 from global memory.
+    if constexpr (F) {
+        // Fused append: the tile's q rows rotated from the raw projection (QK-norm + RoPE in f32:
+        // q only becomes the fp16 tensor-core operand), a warp per row, into shared memory; split 0
+        // also writes them to q_rot (the caller's q_work).
+        constexpr int H2 = D / 2;
+        float *qstage = xbuf;
+        const int nvalid = min(kRT, nrows - row0);
+        const float2 *cs = a.rope32 ? a.rope32 + (size_t)past * H2 : nullptr;
+        for (int j = warp; j < nvalid; j += NC) {
+            const size_t R = (size_t)b * a.Hq + kvh * G + (row0 + j) % G;  // one token
+            const float *src = a.q_in + R * D;
+            float x0[H2 / 32], x1[H2 / 32];
+            float ss = 0.f;
+#pragma unroll
+            for (int u = 0; u < H2 / 32; ++u) {
+                x0[u] = src[lane + 32 * u];
+                x1[u] = src[lane + 32 * u + H2];
+                ss = fmaf(x0[u], x0[u], fmaf(x1[u], x1[u], ss));
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+            const float inv = a.q_norm ? 1.f / sqrtf(ss / (float)D + (float)a.eps) : 1.f;
+            float *dst = qstage + j * L::kQStride;
+#pragma unroll
+            for (int u = 0; u < H2 / 32; ++u) {
+                const int i = lane + 32 * u;
+                float y0 = x0[u], y1 = x1[u];
+                if (a.q_norm) {
+                    y0 *= inv * (a.one_plus ? 1.f + a.q_norm[i] : a.q_norm[i]);
+                    y1 *= inv * (a.one_plus ? 1.f + a.q_norm[i + H2] : a.q_norm[i + H2]);
+                }
+                float o0 = y0, o1 = y1;
+                if (cs) {
+                    const float2 c = cs[i];
+                    o0 = y0 * c.x - y1 * c.y;
+                    o1 = y1 * c.x + y0 * c.y;
+                }
+                dst[i] = o0;
+                dst[i + H2] = o1;
+                if (split == 0) {
+                    a.q_rot[R * D + i] = o0;
+                    a.q_rot[R * D + i + H2] = o1;
+                }
+            }
+        }
+        named_barrier_sync(1, NC * 32);
+    }
+
+    // Q^T fragments (B operand, column qr = query row row0 + qr), fp32 -> fp16: from global
+    // memory, or (fused) from the staged rows.
     uint32_t qf[KS][2];
     {
         const int rq = row0 + qr;
-        const float *qrow =
-            rq < nrows ? a.q + (((size_t)b * T + rq / G) * a.Hq + kvh * G + rq % G) * D + dh * DH : nullptr;
+        const float *qrow = nullptr;
+        if (rq < nrows)
+            qrow = F ? xbuf + qr * L::kQStride + dh * DH
+                     : a.q + (((size_t)b * T + rq / G) * a.Hq + kvh * G + rq % G) * D + dh * DH;
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
             if constexpr (Q8) {
@@ -205,6 +384,7 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
             }
         }
     }
+    if constexpr (F) named_barrier_sync(1, NC * 32);  // the staging bytes become the score swap
 
     // int8: 1152 * (sum of the fp16 q over this slice) for rows 2qc, 2qc + 1 -- the bias of the
     // raw scores against biased codes.
@@ -499,7 +679,10 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
     }
     named_barrier_sync(1, NC * 32);
 
-    decode_epilogue<D, KG, NC, kRT>(a, ring, row0, nrows, kvh, mtile, b, split);
+    if (a.cluster)
+        decode_epilogue_cluster<D, KG, NC, kRT>(a, ring, row0, nrows, kvh, b, split);
+    else
+        decode_epilogue<D, KG, NC, kRT>(a, ring, row0, nrows, kvh, mtile, b, split);
 }
 
 // Log-sum-exp merge of one row's partials by one warp (brk_attn_combine: partials gathered from
@@ -569,15 +752,17 @@ __global__ void combine_peers_kernel(const __grid_constant__ CombineArgs a, cons
     if (row < a.rows) combine_row(a, row, lane);
 }
 
-template <bool Q8, int D>
+template <bool Q8, int D, bool F>
 cudaError_t launch_t(const CUtensorMap &tmk, const CUtensorMap &tmv, const CUtensorMap &tms, const DecodeArgs &a,
                       dim3 grid, cudaStream_t s, bool pdl) {
     static unsigned long long configured = 0;  // one bit per device: the opt-in is per device
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 64 || !(configured & (1ull << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(decode_kernel<Q8, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(decode_kernel<Q8, D, F>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              DecodeLayout<Q8, D>::kSmemBytes);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(decode_kernel<Q8, D, F>,
+                                                       cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
         if (dev < 64) configured |= 1ull << dev;
     }
@@ -586,21 +771,39 @@ cudaError_t launch_t(const CUtensorMap &tmk, const CUtensorMap &tmv, const CUten
     cfg.blockDim = dim3(DecodeLayout<Q8, D>::kThreads);
     cfg.dynamicSmemBytes = DecodeLayout<Q8, D>::kSmemBytes;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    if (pdl) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n++].val.programmaticStreamSerializationAllowed = 1;
+    }
+    if (a.cluster) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = grid.x;  // the splits of a tile
+        attr[n].val.clusterDim.y = 1;
+        attr[n++].val.clusterDim.z = 1;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, decode_kernel<Q8, D>, tmk, tmv, tms, a);
+    cfg.numAttrs = n;
+    return cudaLaunchKernelEx(&cfg, decode_kernel<Q8, D, F>, tmk, tmv, tms, a);
+}
+
+template <int D>
+cudaError_t launch_dt(bool q8, bool fused, const CUtensorMap &tmk, const CUtensorMap &tmv, const CUtensorMap &tms,
+                      const DecodeArgs &a, dim3 grid, cudaStream_t s, bool pdl) {
+    if (q8) return fused ? launch_t<true, D, true>(tmk, tmv, tms, a, grid, s, pdl)
+                         : launch_t<true, D, false>(tmk, tmv, tms, a, grid, s, pdl);
+    return fused ? launch_t<false, D, true>(tmk, tmv, tms, a, grid, s, pdl)
+                 : launch_t<false, D, false>(tmk, tmv, tms, a, grid, s, pdl);
 }
 
 template <bool Q8, int D>
 int ctas_t() {
     static int n = 0;
     if (n == 0) {
-        cudaFuncSetAttribute(decode_kernel<Q8, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(decode_kernel<Q8, D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              DecodeLayout<Q8, D>::kSmemBytes);
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<Q8, D>, DecodeLayout<Q8, D>::kThreads,
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<Q8, D, false>, DecodeLayout<Q8, D>::kThreads,
                                                           DecodeLayout<Q8, D>::kSmemBytes) != cudaSuccess ||
             n < 1)
             n = 1;
@@ -612,12 +815,55 @@ int ctas_t() {
 
 int decode_rows_per_tile() { return kRT; }
 
+namespace {
+template <bool Q8, int D>
+int clusters_t(int size) {
+    static int cache[17] = {};  // per cluster size; the GPU's partition into GPCs is fixed
+    if (size < 2 || size > 16) return 0;
+    if (cache[size] == 0) {
+        cudaFuncSetAttribute(decode_kernel<Q8, D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             DecodeLayout<Q8, D>::kSmemBytes);
+        cudaFuncSetAttribute(decode_kernel<Q8, D, false>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(size, 64, 1);
+        cfg.blockDim = dim3(DecodeLayout<Q8, D>::kThreads);
+        cfg.dynamicSmemBytes = DecodeLayout<Q8, D>::kSmemBytes;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = size;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, decode_kernel<Q8, D, false>, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        cache[size] = n > 0 ? n : -1;
+    }
+    return cache[size] > 0 ? cache[size] : 0;
+}
+}  // namespace
+
+int decode_max_clusters(int head_dim, bool q8, int size) {
+    switch (head_dim) {
+        case 64: return q8 ? clusters_t<true, 64>(size) : clusters_t<false, 64>(size);
+        case 128: return q8 ? clusters_t<true, 128>(size) : clusters_t<false, 128>(size);
+        case 256: return q8 ? clusters_t<true, 256>(size) : clusters_t<false, 256>(size);
+        default: return 0;
+    }
+}
+
 cudaError_t preload_decode_kernels() {
     // With lazy module loading a kernel's code is loaded, and its device memory taken, at the
     // first launch; asking for its attributes loads it now.
-    const void *fns[] = {(const void *)decode_kernel<false, 64>, (const void *)decode_kernel<false, 128>,
-                         (const void *)decode_kernel<false, 256>, (const void *)decode_kernel<true, 64>,
-                         (const void *)decode_kernel<true, 128>,  (const void *)decode_kernel<true, 256>,
+    const void *fns[] = {(const void *)decode_kernel<false, 64, false>, (const void *)decode_kernel<false, 128, false>,
+                         (const void *)decode_kernel<false, 256, false>, (const void *)decode_kernel<true, 64, false>,
+                         (const void *)decode_kernel<true, 128, false>,  (const void *)decode_kernel<true, 256, false>,
+                         (const void *)decode_kernel<false, 64, true>,  (const void *)decode_kernel<false, 128, true>,
+                         (const void *)decode_kernel<false, 256, true>, (const void *)decode_kernel<true, 64, true>,
+                         (const void *)decode_kernel<true, 128, true>,  (const void *)decode_kernel<true, 256, true>,
                          (const void *)combine_kernel,            (const void *)combine_peers_kernel};
     for (const void *f : fns) {
         cudaFuncAttributes fa;
@@ -645,12 +891,9 @@ cudaError_t launch_decode(bool q8, int head_dim, const CUtensorMap &tmk, const C
                   "stage keys must match decode_stage_keys()");
     const dim3 grid(grid_x, grid_y, grid_z);
     switch (head_dim) {
-        case 64: return q8 ? launch_t<true, 64>(tmk, tmv, tms, a, grid, s, pdl)
-                           : launch_t<false, 64>(tmk, tmv, tms, a, grid, s, pdl);
-        case 128: return q8 ? launch_t<true, 128>(tmk, tmv, tms, a, grid, s, pdl)
-                            : launch_t<false, 128>(tmk, tmv, tms, a, grid, s, pdl);
-        case 256: return q8 ? launch_t<true, 256>(tmk, tmv, tms, a, grid, s, pdl)
-                            : launch_t<false, 256>(tmk, tmv, tms, a, grid, s, pdl);
+        case 64: return launch_dt<64>(q8, a.fuse != 0, tmk, tmv, tms, a, grid, s, pdl);
+        case 128: return launch_dt<128>(q8, a.fuse != 0, tmk, tmv, tms, a, grid, s, pdl);
+        case 256: return launch_dt<256>(q8, a.fuse != 0, tmk, tmv, tms, a, grid, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

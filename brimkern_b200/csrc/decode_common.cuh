@@ -199,11 +199,88 @@ __device__ __forceinline__ void decode_epilogue(const DecodeArgs &a, uint8_t *ri
     if (a.push_world) push_finish<NC>(a);
 }
 
-// Bytes of `ring` the epilogue needs: cm, cl, co, the flag word and the split-merge rows
-// (up to 64 splits).
+// Split-KV merge across a thread-block cluster (the splits of one (sequence, kv head, row
+// tile) launched as one cluster, split = rank): each CTA keeps its split's (m, l, o) rows in its
+// own shared memory behind cm / cl / co, the cluster synchronises, every CTA merges a slice of
+// the tile's (row, head-dim) elements reading all splits' partials through distributed shared
+// memory and writes them, and a second cluster barrier keeps every CTA's shared memory alive
+// until the last remote read.  No global partials, no fences or arrival counters, and the merge
+// is spread over the cluster instead of falling to one last CTA.  Called by the NC consumer
+// warps; the producer warp takes the two cluster barriers on its own (decode_cluster_idle).
+template <int D, int KG, int NC, int RT>
+__device__ __forceinline__ void decode_epilogue_cluster(const DecodeArgs &a, uint8_t *ring, int row0, int nrows,
+                                                        int kvh, int b, int split) {
+    const float *cm = reinterpret_cast<const float *>(ring);
+    const float *cl = cm + KG * RT;
+    const float *co = cl + KG * RT;
+    float *sp_ml = const_cast<float *>(co) + KG * RT * D;  // [RT][2] this split's (m log2 units, l)
+    float *sp_o = sp_ml + 2 * RT;                          // [RT][D] this split's unnormalised o
+    const int G = a.G, T = a.T;
+    const int nvalid = min(RT, nrows - row0);
+    for (int idx = threadIdx.x; idx < nvalid * D; idx += NC * 32) {
+        const int r = idx / D, d = idx % D;
+        float M = -CUDART_INF_F;
+#pragma unroll
+        for (int w = 0; w < KG; ++w) M = fmaxf(M, cm[w * RT + r]);
+        float Lsum = 0.f, O = 0.f;
+        if (M != -CUDART_INF_F) {
+#pragma unroll
+            for (int w = 0; w < KG; ++w) {
+                const float f = exp2f(cm[w * RT + r] - M);
+                Lsum += cl[w * RT + r] * f;
+                O += co[(w * RT + r) * D + d] * f;
+            }
+        }
+        sp_o[r * D + d] = O;
+        if (d == 0) {
+            sp_ml[2 * r] = M;
+            sp_ml[2 * r + 1] = Lsum;
+        }
+    }
+    griddep_launch_dependents();
+    cluster_sync_all();  // every split's partial is in its CTA's shared memory
+    const int nsplit = a.nsplit;
+    for (int idx = split * NC * 32 + threadIdx.x; idx < nvalid * D; idx += nsplit * NC * 32) {
+        const int r = idx / D, d = idx % D;
+        float M = -CUDART_INF_F;
+        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, ld_cluster_f32(sp_ml + 2 * r, sp));
+        float Lsum = 0.f, O = 0.f;
+        if (M != -CUDART_INF_F) {
+            for (int sp = 0; sp < nsplit; ++sp) {
+                const float m = ld_cluster_f32(sp_ml + 2 * r, sp);
+                const float w = m == -CUDART_INF_F ? 0.f : exp2f(m - M);
+                Lsum += w * ld_cluster_f32(sp_ml + 2 * r + 1, sp);
+                O += w * ld_cluster_f32(sp_o + r * D + d, sp);
+            }
+        }
+        const int rr = row0 + r;
+        const size_t R = ((size_t)b * T + rr / G) * a.Hq + kvh * G + rr % G;
+        if (a.out) {
+            a.out[R * D + d] = O / Lsum;
+        } else {
+            a.res_o[R * D + d] = O;
+            if (d == 0) {
+                a.res_ml[R * 2] = M == -CUDART_INF_F ? -CUDART_INF_F : M * kLn2;
+                a.res_ml[R * 2 + 1] = Lsum;
+            }
+        }
+    }
+    cluster_sync_all();  // no CTA leaves while another may still read its shared memory
+}
+
+// The producer warp's part of decode_epilogue_cluster: the same two cluster barriers.
+__device__ __forceinline__ void decode_cluster_idle() {
+    cluster_sync_all();
+    cluster_sync_all();
+}
+
+// Bytes of `ring` the epilogue needs: cm, cl, co, then the larger of the flag word with the
+// split-merge rows (up to 64 splits, global merge) and the split's partial (cluster merge).
 template <int D, int KG, int RT>
 constexpr uint32_t decode_epilogue_bytes() {
-    return KG * RT * D * 4 + 2 * KG * RT * 4 + 16 + 2 * RT * 4 + RT * 64 * 4;
+    return KG * RT * D * 4 + 2 * KG * RT * 4 +
+           (16 + 2 * RT * 4 + RT * 64 * 4 > 2 * RT * 4 + RT * D * 4 ? 16 + 2 * RT * 4 + RT * 64 * 4
+                                                                     : 2 * RT * 4 + RT * D * 4);
 }
 
 }  // namespace brk

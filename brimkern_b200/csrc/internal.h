@@ -109,6 +109,9 @@ struct DecodeArgs {
     // Push mode (push_world > 0, partial mode only): the final partial of every row goes to
     // push_ml[p] / push_o[p] on each of the push_world ranks; the last tile of the launch to
     // finish then stores `epoch` into push_flag[p] on every rank (system-scope release).
+    // Split-KV merge through a thread-block cluster (the nsplit CTAs of a tile are one cluster):
+    // no workspace partials or counters (decode_epilogue_cluster).
+    int cluster;
     int push_world;
     unsigned epoch;
     int push_tiles;         // tiles of this launch (B * Hkv * mtiles)
@@ -116,6 +119,24 @@ struct DecodeArgs {
     float *push_ml[8];
     float *push_o[8];
     unsigned *push_flag[8];
+    // Fused append (fuse != 0, one new token per sequence, brk_attn_step): every CTA rotates the
+    // q rows of its tile from q_in (QK-norm + RoPE in f32: q only feeds the fp16 operand) straight
+    // into its fragments, split 0 also writing them to q_rot (the caller's q_work), and the CTA
+    // whose key range holds position past_len[b] computes that position's K / V rows from
+    // k_in / v_in (the append's fp64 operations) and stores them in the cache before its ring
+    // loads them.
+    int fuse;
+    float *q_rot;           // = q, the rotated rows' destination
+    const float *q_in, *k_in, *v_in;
+    __half *kc, *vc;        // fp16 cache, or
+    uint8_t *kc8, *vc8;     //   int8 codes (biased) and
+    float *scales;          //   [seg][2][scale_pitch] scales
+    int scale_pitch;
+    const double2 *rope;    // [positions][D/2] (cos, sin) in double (the K row), or nullptr
+    const float2 *rope32;   // the same rounded to f32 (the q rows)
+    const float *q_norm, *k_norm;
+    double eps;
+    int one_plus;
     int past_len[BRK_MAX_BATCH];
 };
 
@@ -170,6 +191,9 @@ cudaError_t launch_decode(bool q8, int head_dim, const CUtensorMap &tmk, const C
                           const CUtensorMap &tms, const DecodeArgs &a, int grid_x, int grid_y, int grid_z,
                           cudaStream_t s, bool pdl);
 int decode_rows_per_tile();
+// How many clusters of `size` decode CTAs fit on the GPU at once (0: clusters of that size cannot
+// be launched).
+int decode_max_clusters(int head_dim, bool q8, int size);
 // Loads every decode / combine kernel on the current device now instead of at its first launch.
 cudaError_t preload_decode_kernels();
 cudaError_t launch_combine(const CombineArgs &a, cudaStream_t s);
