@@ -680,8 +680,10 @@ def run_slice(args, c, workload):
         stream.wait_stream(side)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
+        n0 = eng.ctx.launches
         with torch.cuda.graph(g):
             fn()
+        g.launches = eng.ctx.launches - n0  # kernels one replay launches
         g.replay()
         torch.cuda.synchronize()
         eng.ctx.check()
@@ -711,7 +713,7 @@ def run_slice(args, c, workload):
     e1.record(stream)
     torch.cuda.synchronize()
     # Per layer: cast + GEMM for q/k/v, append + decode, cast + GEMM for the output.
-    launches = eng.ctx.launches - n0 if graph is None else args.steps * 6 * layers
+    launches = eng.ctx.launches - n0 if graph is None else args.steps * graph.launches
     clocks = sampler.stop()
     eng.ctx.check()
     ms_step = e0.elapsed_time(e1) / args.steps
@@ -1003,8 +1005,10 @@ def main():
         stream.wait_stream(side)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
+        n0 = eng.ctx.launches
         with torch.cuda.graph(g):
             fn()
+        g.launches = eng.ctx.launches - n0  # kernels one replay launches
         g.replay()
         torch.cuda.synchronize()
         eng.ctx.check()
@@ -1033,7 +1037,7 @@ def main():
     stop.record(stream)
     torch.cuda.synchronize()
     # Kernels launched in the timed region (a replay launches the captured step's kernels).
-    launches = eng.ctx.launches - n0 if graph is None else (eng.ctx.launches - n0) + args.steps * 2 * layers
+    launches = eng.ctx.launches - n0 if graph is None else args.steps * graph.launches
     clocks = sampler.stop()
     eng.ctx.check()
     barrier()

@@ -95,6 +95,7 @@ SIGNATURES = [
     ("brk_peer_attach", _i, [_vp, _i, _vp]),
     ("brk_peer_destroy", _i, [_vp]),
     ("brk_attn_decode_push", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, ctypes.c_uint32, _vp]),
+    ("brk_attn_step_push", _i, [_vp, _vp, _i, _PARAMS, _i, _i32p, _vp, _vp, _vp, _vp, _vp, ctypes.c_uint32, _vp]),
     ("brk_attn_combine_peers", _i, [_vp, _vp, _i, ctypes.c_uint32, _d, _vp, _vp]),
 ]
 

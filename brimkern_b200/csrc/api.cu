@@ -1408,6 +1408,38 @@ int brk_attn_decode_push(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_at
                       static_cast<cudaStream_t>(stream), nullptr, 0, false, peer, epoch);
 }
 
+int brk_attn_step_push(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, int batch,
+                       const int32_t *past_len, const float *q_in, const float *k_in, const float *v_in,
+                       float *q_work, brk_peer *peer, uint32_t epoch, void *stream) {
+    int rc = check_call(ctx, kv, layer, p, batch, 1, past_len);
+    if (rc) return rc;
+    if (!q_in || !q_work || !peer) return fail(BRK_ERR_INVALID, "null q_in, q_work or peer area");
+    if (peer->ctx != ctx) return fail(BRK_ERR_INVALID, "peer area belongs to another context");
+    if (epoch == 0) return fail(BRK_ERR_INVALID, "epoch 0 is reserved (flags start at 0)");
+    if (p->head_dim == 256 && p->n_heads / p->n_kv_heads > 4)
+        return fail(BRK_ERR_UNSUPPORTED, "head_dim 256 with a GQA group above 4: use brk_attn_append + decode_push");
+    const long long rows = (long long)batch * p->n_heads;
+    if (rows > peer->max_rows || p->head_dim != peer->head_dim)
+        return fail(BRK_ERR_INVALID, "%lld rows of head_dim %d exceed the peer area (%d rows of %d)", rows, p->head_dim,
+                    peer->max_rows, peer->head_dim);
+    for (int r = 0; r < peer->world; ++r)
+        if (!peer->peers[r]) return fail(BRK_ERR_INVALID, "rank %d's area is not mapped (brk_peer_open)", r);
+    if (p->rope && (p->rope->head_dim != p->head_dim || p->rope->ctx != ctx))
+        return fail(BRK_ERR_INVALID, "rope table head_dim %d != %d", p->rope->head_dim, p->head_dim);
+    for (int b = 0; b < batch; ++b) {
+        if (p->rope && past_len[b] + 1 > p->rope->max_pos)
+            return fail(BRK_ERR_CAPACITY, "position %d beyond the rope table (%d positions)", past_len[b],
+                        p->rope->max_pos);
+        // This rank stores the new row when its cache holds that position (the last shard).
+        if (past_len[b] - p->kv_offset < kv->cap && (!k_in || !v_in))
+            return fail(BRK_ERR_INVALID, "sequence %d's new position is in this cache: k_in and v_in are needed", b);
+    }
+    DeviceGuard g(ctx->device);
+    const FusedAppend f{q_in, k_in, v_in, q_work};
+    return run_decode(ctx, kv, layer, p, batch, 1, past_len, q_work, nullptr, nullptr, nullptr, true,
+                      static_cast<cudaStream_t>(stream), nullptr, 0, false, peer, epoch, &f);
+}
+
 int brk_attn_combine_peers(brk_ctx *ctx, brk_peer *peer, int rows, uint32_t epoch, double timeout_s, float *out,
                            void *stream) {
     if (!ctx || !peer || !out) return fail(BRK_ERR_INVALID, "null argument");

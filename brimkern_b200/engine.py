@@ -648,6 +648,18 @@ class AttentionEngine:
         check(L.lib().brk_attn_decode_push(self.ctx.handle, kv.handle, layer, ctypes.byref(p), B, T, pos, _ptr(q),
                                            peer.handle, int(epoch), _stream_ptr(stream)))
 
+    def stepPush(self, kv: KvCache, layer: int, cfg: AttnConfig, q_in: torch.Tensor, k_in: Optional[torch.Tensor],
+                 v_in: Optional[torch.Tensor], q_work: torch.Tensor, peer: PeerArea, epoch: int, past_len,
+                 stream=None) -> None:
+        """decodePush for one token with the append fused into the launch: q_in raw (rotated into
+        q_work), K / V stored by the rank whose cache holds the new position (others pass None)."""
+        B = kv.batch
+        p = cfg.params()
+        pos = _positions(past_len, B)
+        check(L.lib().brk_attn_step_push(self.ctx.handle, kv.handle, layer, ctypes.byref(p), B, pos, _ptr(q_in),
+                                         _ptr(k_in), _ptr(v_in), _ptr(q_work), peer.handle, int(epoch),
+                                         _stream_ptr(stream)))
+
     def combinePeers(self, peer: PeerArea, rows: int, epoch: int, out: torch.Tensor, timeout_s: float = 2.0,
                      stream=None) -> torch.Tensor:
         """Waits for every rank's partials of `epoch`, then their log-sum-exp combine -> out."""

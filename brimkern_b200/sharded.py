@@ -111,10 +111,17 @@ class ShardedDecoder:
         owns = p.owner(position) == p.rank
         B = self.batch
         pos = [position] * B
+        rows = B * cfg.n_heads
+        q_tokens = q_in.numel() // (B * cfg.n_heads * cfg.head_dim)
+        if self.fused and q_tokens == 1 and (cfg.head_dim != 256 or cfg.n_heads // cfg.n_kv_heads <= 4):
+            # One launch: q rotation, the owner's K/V append and the partials pushed to every rank.
+            self.epoch += 1
+            self.engine.stepPush(self.kv, layer, shard_cfg, q_in, k_in if owns else None, v_in if owns else None,
+                                 q_work, self.peer, self.epoch, pos, stream)
+            return self.engine.combinePeers(self.peer, rows, self.epoch, out, stream=stream)
         # q rotation everywhere; K/V stored only by the owner of this position.
         self.engine.appendKv(self.kv, layer, shard_cfg, q_in, k_in if owns else None, v_in if owns else None, q_work,
                              pos, stream)
-        rows = B * cfg.n_heads
         if self.fused:
             self.epoch += 1
             self.engine.decodePush(self.kv, layer, shard_cfg, q_work, self.peer, self.epoch, pos, stream)

@@ -299,6 +299,14 @@ int brk_peer_destroy(brk_peer *peer);
 int brk_attn_decode_push(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p,
                          int batch, int n_tokens, const int32_t *past_len, const float *q,
                          brk_peer *peer, uint32_t epoch, void *stream);
+/* brk_attn_decode_push for one new token per sequence with the append fused into the launch, as
+ * brk_attn_step does it: q_in is the raw q projection (rotated in the kernel; q_work receives the
+ * rotated q), and the rank whose cache holds position past_len[b] (row past_len[b] - kv_offset
+ * below the capacity) stores that position's K / V rows from k_in / v_in, which the other ranks
+ * may pass as NULL.  Extension, no reference counterpart. */
+int brk_attn_step_push(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, int batch,
+                       const int32_t *past_len, const float *q_in, const float *k_in, const float *v_in,
+                       float *q_work, brk_peer *peer, uint32_t epoch, void *stream);
 /* Waits (at most timeout_s) for every rank's partials of `epoch`, then out [rows][head_dim] =
  * their log-sum-exp combine. */
 int brk_attn_combine_peers(brk_ctx *ctx, brk_peer *peer, int rows, uint32_t epoch, double timeout_s,

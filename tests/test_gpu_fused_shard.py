@@ -113,3 +113,66 @@ def test_missing_rank_times_out(eng):
     a1.close()
     for kv, _ in kvs:
         kv.close()
+
+
+@pytest.mark.parametrize("N,q8", [(2, False), (4, True)])
+def test_step_push_emulated_ranks(eng, N, q8):
+    """brk_attn_step_push: the append fused into the push launch.  Every rank rotates the raw q
+    (QK-norm + RoPE); the rank whose shard holds the new position stores its K / V row (the others
+    pass none); the combine equals the oracle chain over the whole context plus the new token."""
+    import torch
+    from brimkern_b200.engine import AttnConfig, KvCache, PeerArea, RopeTable
+    rng = np.random.default_rng(40 + N)
+    Hq, Hkv, D, B, ctx_len = 32, 8, 64, 2, 3000
+    base = 5e5
+    k, v = normal(rng, B, ctx_len, Hkv, D), normal(rng, B, ctx_len, Hkv, D)
+    shard = (ctx_len + N - 1) // N
+    kvs = []
+    for r in range(N):
+        lo, hi = r * shard, min(ctx_len, (r + 1) * shard)
+        kv = KvCache(eng.ctx, 1, B, Hkv, D, hi - lo + (1 if r == N - 1 else 0), q8=q8)
+        for b in range(B):
+            kv.write_rows(0, b, 0, torch.from_numpy(k[b, lo:hi].copy()).to(eng.device),
+                          torch.from_numpy(v[b, lo:hi].copy()).to(eng.device))
+        kvs.append((kv, lo))
+    rows = B * Hq
+    areas = [PeerArea(eng.ctx, N, r, rows, D) for r in range(N)]
+    for r in range(N):
+        for p in range(N):
+            if p != r:
+                areas[r].attach(p, areas[p])
+    qg = (1 + 0.02 * rng.standard_normal(D)).astype(np.float32)
+    kg = (1 + 0.02 * rng.standard_normal(D)).astype(np.float32)
+    rope = RopeTable(eng.ctx, D, base, None, ctx_len + 1)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(eng.device)  # noqa: E731
+    q_in, k_in, v_in = normal(rng, B, 1, Hq, D), normal(rng, B, 1, Hkv, D), normal(rng, B, 1, Hkv, D)
+    past = [ctx_len] * B
+    works = [torch.empty((B, 1, Hq, D), device=eng.device) for _ in range(N)]
+    for r, (kv, lo) in enumerate(kvs):
+        cfg = AttnConfig(Hq, Hkv, D, q_norm=t(qg), k_norm=t(kg), rope=rope, kv_offset=lo)
+        owner = r == N - 1
+        eng.stepPush(kv, 0, cfg, t(q_in), t(k_in) if owner else None, t(v_in) if owner else None, works[r],
+                     areas[r], 1, past)
+    outs = []
+    for r in range(N):
+        out = torch.full((rows, D), float("nan"), dtype=torch.float32, device=eng.device)
+        eng.combinePeers(areas[r], rows, 1, out)
+        outs.append(out)
+    eng.ctx.check()
+    got = [o.cpu().numpy() for o in outs]
+    for r in range(1, N):
+        assert np.array_equal(got[r], got[0]), f"rank {r} differs from rank 0"
+    for b in range(B):
+        q_ref = O.rope(O.rmsnorm(q_in[b].ravel(), qg, Hq, D, 1e-6), Hq, D, Hq, ctx_len, base)
+        k_new = O.rope(O.rmsnorm(k_in[b].ravel(), kg, Hkv, D, 1e-6), Hkv, D, Hkv, ctx_len, base).reshape(1, Hkv, D)
+        kd = np.concatenate([_deq(k[b, r * shard:min(ctx_len, (r + 1) * shard)], q8) for r in range(N)] +
+                            [_deq(k_new, q8)])
+        vd = np.concatenate([_deq(v[b, r * shard:min(ctx_len, (r + 1) * shard)], q8) for r in range(N)] +
+                            [_deq(v_in[b], q8)])
+        ref = O.attention(q_ref, kd, vd, 1, Hq, Hkv, D, ctx_len)
+        assert_close(got[0].reshape(B, Hq, D)[b].ravel(), ref, what=f"step_push N={N} seq {b}")
+    for a in areas:
+        a.close()
+    for kv, _ in kvs:
+        kv.close()
+    rope.close()

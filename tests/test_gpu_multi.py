@@ -69,7 +69,7 @@ def _rank(rank, world, port, context, B, Hq, Hkv, D, path, fused):
 
 
 @pytest.mark.parametrize("fused", [False, True])
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_sequence_sharded_decode(tmp_path, world, fused):
     torch = pytest.importorskip("torch")
     if torch.cuda.device_count() < world:
