@@ -24,10 +24,12 @@ constexpr int kRowsPerBlock = 4;  // one warp per head-vector row
 // DT: the head dim as a compile-time constant (64 / 128 / 256), or 0 for any other even size.
 template <int DT>
 __global__ void __launch_bounds__(kRowsPerBlock * 32) append_kernel(const __grid_constant__ AppendArgs a) {
-    // The dependent decode may be scheduled now (it waits for this grid before reading q or the
-    // new rows); this grid itself waits for whatever the stream ran before it.
-    griddep_launch_dependents();
+    // This grid waits for whatever the stream ran before it, then lets its dependent (the decode
+    // or prefill kernel of the same step) be scheduled: that kernel may read what the earlier
+    // kernels wrote (the q projection, cache rows) before this grid finishes, and waits for this
+    // grid only before the rows it writes.
     griddep_wait();
+    griddep_launch_dependents();
     extern __shared__ double sq_all[];  // per warp: D squares (double), then D values (float)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int D = DT ? DT : a.D, half = D >> 1;
@@ -145,8 +147,8 @@ __global__ void __launch_bounds__(kRowsPerBlock * 32) append_kernel(const __grid
 // so the outputs are the same bits.
 template <int D, int ROWS>
 __global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant__ AppendArgs a) {
+    griddep_wait();  // then the dependent may start (see append_kernel)
     griddep_launch_dependents();
-    griddep_wait();
     constexpr int kStride = D + 1;
     constexpr int H2 = D / 2;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -300,8 +302,8 @@ __global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant
 // row bookkeeping).
 template <int D>
 __global__ void __launch_bounds__(256) kv_append_kernel(const __grid_constant__ AppendArgs a) {
+    griddep_wait();  // then the dependent may start (see append_kernel)
     griddep_launch_dependents();
-    griddep_wait();
     constexpr int TT = 32, RPW = TT / 8;         // tokens per block, rows per warp
     constexpr int H2 = D / 2, NP = H2 / 32;      // rotation pairs per lane
     constexpr int C4 = D / 4 >= 32 ? D / 128 : 1;  // float4 per lane per row

@@ -163,8 +163,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0 && nk > 0) {
             tma_prefetch_desc(&tmk);
             tma_prefetch_desc(&tmv);
-            // Launched right behind the append of this chunk's K/V (programmatic dependent launch):
-            // only these cache reads depend on it; the q prologue already overlaps the append.
+            // Launched right behind the append of this chunk's K/V (programmatic dependent launch,
+            // scheduled once the append has waited for its own predecessors, so the q projection
+            // the prologue reads is complete): only these cache reads wait for the append.
             griddep_wait();
             int issued = 0;
             for (int j = 0; j < nk; ++j) {
