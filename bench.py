@@ -189,7 +189,8 @@ def run_prefill(args, c, workload, eng=None, emit=True):
     qn = (1 + 0.02 * torch.randn(D, generator=gen, device=dev)).float()
     kn = (1 + 0.02 * torch.randn(D, generator=gen, device=dev)).float()
     cfg = AttnConfig(Hq, Hkv, D, q_norm=qn, k_norm=kn, rope=rope)
-    kv = KvCache(eng.ctx, layers, B, Hkv, D, P)
+    q8 = c.get("kv") == "q8"
+    kv = KvCache(eng.ctx, layers, B, Hkv, D, P, q8=q8)
     q_in = torch.randn((layers, nch, B, CH, Hq, D), generator=gen, device=dev)
     k_in = torch.randn((layers, nch, B, CH, Hkv, D), generator=gen, device=dev)
     v_in = torch.randn((layers, nch, B, CH, Hkv, D), generator=gen, device=dev)
@@ -303,9 +304,12 @@ def run_prefill(args, c, workload, eng=None, emit=True):
         line = {
             "metric": "prefill-attn TFLOP/s (causal-exact)", "value": round(value, 2), "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 in / f32 accumulate",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": ("int8 KV codes dequantized to an fp16 stage per call, f16 MMA / f32 accumulate" if q8 else
+                      "f16 in / f32 accumulate"),
             "data": "synthetic",
-            "config": {"workload": workload, "global_batch": B * world, "prompt": P, "chunk": CH, "layers": layers,
+            "config": {"workload": workload, "kv_cache": "int8" if q8 else "fp16", "global_batch": B * world,
+                       "prompt": P, "chunk": CH, "layers": layers,
                        "heads": f"{Hq}q/{Hkv}kv", "head_dim": D, "parallelism": f"batch-sharded x{world}",
                        "l2": "no flush: KV + inputs of a step are 4.2 GB > L2"},
             "tokens_per_s": round(world * B * P / (ms_step * 1e-3), 1),

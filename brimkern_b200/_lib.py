@@ -62,6 +62,7 @@ SIGNATURES = [
     ("brk_ctx_destroy", _i, [_vp]),
     ("brk_ctx_check", _i, [_vp, _vp]),
     ("brk_ctx_reserve", _i, [_vp, _sz]),
+    ("brk_ctx_reserve_stage", _i, [_vp, _sz]),
     ("brk_ctx_launches", ctypes.c_uint64, [_vp]),
     ("brk_rope_create", _i, [_vp, _i, _d, _f32p, _i, _pp]),
     ("brk_rope_destroy", _i, [_vp]),

@@ -566,6 +566,16 @@ int brk_ctx_reserve(brk_ctx *ctx, size_t bytes) {
     return BRK_OK;
 }
 
+namespace {
+int ensure_stage(brk_ctx *ctx, size_t bytes);
+}  // namespace
+
+int brk_ctx_reserve_stage(brk_ctx *ctx, size_t bytes) {
+    if (!ctx) return fail(BRK_ERR_INVALID, "null context");
+    DeviceGuard g(ctx->device);
+    return ensure_stage(ctx, bytes);
+}
+
 int brk_rope_create(brk_ctx *ctx, int head_dim, double base, const float *ff_host, int max_positions,
                     brk_rope **out) {
     if (!ctx || !out) return fail(BRK_ERR_INVALID, "null argument");

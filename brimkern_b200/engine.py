@@ -72,6 +72,10 @@ class Context:
     def reserve(self, nbytes: int) -> None:
         check(L.lib().brk_ctx_reserve(self.handle, int(nbytes)))
 
+    def reserve_stage(self, nbytes: int) -> None:
+        """Pre-size the fp16 staging buffer (int8-cache prefill, non-causal attention)."""
+        check(L.lib().brk_ctx_reserve_stage(self.handle, int(nbytes)))
+
     def close(self) -> None:
         if self.handle:
             L.lib().brk_ctx_destroy(self.handle)

@@ -88,6 +88,15 @@ int brk_ctx_destroy(brk_ctx *ctx);
 int brk_ctx_check(brk_ctx *ctx, void *stream);
 /* Pre-sizes the split-KV workspace (bytes) so that later calls allocate nothing. */
 int brk_ctx_reserve(brk_ctx *ctx, size_t bytes);
+/* Pre-sizes the context's fp16 staging buffer (bytes), which two paths fill per call: prefill
+ * over an int8 cache stages the layer's dequantised rows, 2 * batch * n_kv_heads * rows *
+ * head_dim * 2 bytes with rows = max over the batch of past_len + n_tokens - kv_offset; non-
+ * causal attention stages its K/V (and, for head dims other than 64 / 128 / 256, q and out):
+ * 4 * batch * n_kv_heads * kv_len * Dp + 8 * batch * n_tokens * n_heads * Dp + 256 bytes with
+ * Dp the head dim rounded up to 64 / 128 / 256 (the q term only when Dp != head_dim).  A call
+ * whose staging fits allocates nothing; one that does not grows the buffer (after a device
+ * synchronise, as queued kernels may still read it). */
+int brk_ctx_reserve_stage(brk_ctx *ctx, size_t bytes);
 /* Number of kernels this context has launched so far (diagnostics / benchmarks). */
 uint64_t brk_ctx_launches(const brk_ctx *ctx);
 

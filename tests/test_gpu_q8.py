@@ -302,3 +302,45 @@ def test_q8_grow_keeps_rows_and_engine_mode(eng):
     assert eng.kvGpu is None
     assert not eng.ensureKv(1, 10, 1, 2, 64).q8
     eng.resetKvGpu()
+
+
+def test_q8_prefill_reserved_stage_allocates_nothing(eng):
+    """With the staging buffer reserved by brk_ctx_reserve_stage's documented size (2 * batch *
+    n_kv_heads * rows * head_dim * 2 bytes), int8-cache prefill calls of that size or smaller
+    leave device free memory unchanged, and still match attentionCpu over the dequantised codes."""
+    import ctypes
+
+    import torch
+    from brimkern_b200 import _lib as L
+    from brimkern_b200.engine import AttnConfig, Context, KvCache
+    rng = np.random.default_rng(4711)
+    Hq, Hkv, D, T = 16, 4, 128, 256
+    pasts = [768, 100]
+    B, rows = len(pasts), max(pasts) + T
+    ctx = Context(0)
+    kv = KvCache(ctx, 1, B, Hkv, D, rows, q8=True)
+    ks, vs = _fill_q8(eng, kv, 0, rng, rows)
+    ctx.reserve_stage(2 * B * Hkv * rows * D * 2)
+    cfg = AttnConfig(Hq, Hkv, D)
+    q = torch.from_numpy(normal(rng, B, T, Hq, D)).to(eng.device)
+    out = torch.full((B, T, Hq, D), float("nan"), dtype=torch.float32, device=eng.device)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info(eng.device)[0]
+    p = cfg.params()
+    for call_pasts in (pasts, [pasts[0] - 64, pasts[1]], pasts):
+        pos = (ctypes.c_int32 * B)(*call_pasts)
+        rc = L.lib().brk_attn_prefill(ctx.handle, kv.handle, 0, ctypes.byref(p), B, T, pos, q.data_ptr(),
+                                      out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, L.lib().brk_last_error()
+    ctx.check()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(eng.device)[0] == free0, "an int8 prefill call allocated device memory"
+    got = out.cpu().numpy()
+    per_row = Hkv * D
+    qh = q.cpu().numpy()
+    for b, past in enumerate(pasts):
+        n = past + T
+        ref = O.attention(qh[b].ravel(), ks[b][:n * per_row], vs[b][:n * per_row], T, Hq, Hkv, D, past)
+        assert_close(got[b].ravel(), ref, what=f"reserved-stage int8 prefill seq {b}")
+    kv.close()
+    ctx.close()
