@@ -446,16 +446,27 @@ def load_peak():
         return 6650.0, "fallback"
 
 
-def read_traffic(workload):
-    """dram bytes per decode launch from the committed ncu summary, if one exists."""
-    path = os.path.join(ROOT, "profiles", f"decode_{workload}.md")
-    try:
-        for line in open(path):
-            if line.startswith("dram_bytes_per_launch:"):
-                return float(line.split(":", 1)[1].strip().split()[0])
-    except OSError:
-        pass
-    return None
+def read_traffic(workload, batch, bytes_launch):
+    """DRAM bytes per decode launch from the committed ncu summary of this workload: the capture at
+    this batch if one exists, else the default capture scaled by the algorithmic bytes (the
+    kernel's traffic grows with the KV it streams).  Returns (bytes or None, note)."""
+    for name in (f"decode_{workload}_b{batch}.md", f"decode_{workload}.md"):
+        path = os.path.join(ROOT, "profiles", name)
+        dram = alg = None
+        try:
+            for line in open(path):
+                if line.startswith("dram_bytes_per_launch:"):
+                    dram = float(line.split(":", 1)[1].strip().split()[0])
+                elif line.startswith("algorithmic_bytes_per_launch:"):
+                    alg = float(line.split(":", 1)[1].strip().split()[0])
+        except OSError:
+            continue
+        if dram is None or alg is None:
+            continue
+        if abs(alg - bytes_launch) < 1:
+            return dram, f"ncu capture profiles/{name}"
+        return round(dram * bytes_launch / alg), f"ncu capture profiles/{name} scaled by algorithmic bytes"
+    return None, "no ncu capture of this workload"
 
 
 class ClockSampler:
@@ -1088,9 +1099,10 @@ def main():
     attn_avg_ms = sum(attn_ms) / len(attn_ms)
     bytes_launch = bytes_step / layers
     achieved = bytes_launch / (attn_avg_ms * 1e-3) / 1e9
-    traffic = read_traffic(workload + ("-q8" if q8 else ""))
+    traffic, traffic_src = read_traffic(workload + ("-q8" if q8 else ""), B, bytes_launch)
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_source": traffic_src,
+                "peak_kind": peak_kind,
                 "kernel": "decode_kernel<int8>" if q8 else "decode_kernel<fp16>",
                 "timing": (f"CUDA events around each host-launched decode kernel, {rsteps} steps" if args.eager else
                            f"CUDA events around {rsteps} replays of a graph of the {layers} layers' decode launches"),
