@@ -164,6 +164,21 @@ __device__ __forceinline__ float ex2_fast(float x) {
     return y;
 }
 
+// Hardware reciprocal (MUFU; ~1 ulp, flushes subnormals; 1/inf = 0).
+__device__ __forceinline__ float rcp_fast(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Logit softcap c * tanh(s / c) (shaders.ts:1490) in log2 units, from tanh(z) = 1 - 2 / (1 + e^{2z})
+// with k1 = 2 * scale * log2(e) / c and k2 = c * log2(e): one MUFU exponential and one MUFU
+// reciprocal, saturating to +-k2 for large |z|.  The tanh comes out within a few 1e-7 absolute
+// (near z = 0 the subtraction cancels, which costs relative but not absolute precision).
+__device__ __forceinline__ float softcap_log2(float s, float k1, float k2) {
+    return k2 * (1.f - 2.f * rcp_fast(1.f + ex2_fast(s * k1)));
+}
+
 // Three-input maximum (one instruction on sm_100).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float d;

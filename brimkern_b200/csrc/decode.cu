@@ -503,10 +503,7 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
             float x = sacc[e];
             if constexpr (Q8) x *= ksc[e >> 1];
             if (use_cap) {
-                // c*tanh(s/c) (shaders.ts:1490) in log2 units, tanh(z) = 1 - 2/(1 + e^{2z}): one
-                // exp2 and one reciprocal, saturating to +-1 for large |z|.
-                const float e2z = exp2f(x * a.cap_k1);
-                x = a.cap_k2 * (1.f - 2.f * __frcp_rn(1.f + e2z));
+                x = softcap_log2(x, a.cap_k1, a.cap_k2);
             } else {
                 x *= a.scale_log2;
             }
@@ -573,7 +570,6 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
         const uint32_t pb1 = movmatrix_t(pt1);
 
         // ---- O^T += V^T P^T over the warp's head-dim slice.
-        bool tail = false;
         if constexpr (Q8) {
             const uint8_t *vb = vt + dh * L::kBoxBytes;
             const int vr = kg * 16 + 2 * qc;
@@ -603,7 +599,7 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
         } else {
             // Keys past the range end get zero V (in this warp's slice), so that 0 * (whatever
             // the tile holds there) stays 0.
-            tail = key0 + 16 > k_end;
+            const bool tail = key0 + 16 > k_end;
             if (tail) {
                 const int first = max(k_end - key0, 0);
                 for (int idx = lane; idx < (16 - first) * (DH / 8); idx += 32) {
@@ -623,7 +619,12 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
                 mma_16816(o[m], a0, a1, a2, a3, pb0, pb1);
             }
         }
-        if (tail) fence_proxy_async_smem();  // generic writes before the next TMA into this slot
+        // Every lane's reads of this slot (and the tail's zero stores) are generic-proxy accesses;
+        // the next TMA into the slot writes through the async proxy, which the mbarrier's
+        // release / acquire alone does not order after them.  Without this fence, int8 launches
+        // with two or more CTAs per SM read bytes of the following tile now and then (whole
+        // (sequence, kv head) outputs off by 1e-3..3e-2, different from launch to launch).
+        fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }

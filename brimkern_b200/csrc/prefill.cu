@@ -81,9 +81,7 @@ enum : int {
 template <bool CAP>
 __device__ __forceinline__ float score_log2(float dot, const PrefillArgs &a) {
     if constexpr (CAP) {
-        // c*tanh(s/c) (shaders.ts:1490) with tanh z = 1 - 2/(1 + e^{2z}), in log2 units.
-        const float e2z = exp2f(dot * a.cap_k1);
-        return a.cap_k2 * (1.f - 2.f * __frcp_rn(1.f + e2z));
+        return softcap_log2(dot, a.cap_k1, a.cap_k2);
     } else {
         return dot * a.scale_log2;
     }
