@@ -184,3 +184,22 @@ def test_split_counters_survive_shape_changes(eng):
         assert_close(o[B - 1].cpu().numpy().ravel(), ref, what=f"batch {B} last sequence")
     for kv in caches:
         kv.close()
+
+
+@pytest.mark.parametrize("splits,no_cluster", [(32, False), (16, True), (16, False)])
+def test_q8_d256_full_residency_repeats(eng, splits, no_cluster):
+    """int8 head_dim 256 with every SM holding several CTAs at once (4 sequences x 4 kv heads x
+    16-32 splits), the configuration in which a ring slot's generic-proxy reads, not fenced
+    against the next TMA write into the slot, let consumers see bytes of the following tile now
+    and then: the outputs of 24 launches must agree bit for bit."""
+    old = os.environ.get("BRK_DECODE_NO_CLUSTER")
+    if no_cluster:
+        os.environ["BRK_DECODE_NO_CLUSTER"] = "1"
+    try:
+        test_decode_repeats_bit_identical(eng, "q8_d256", True, 8, 4, 256, 4, 8192, splits)
+    finally:
+        if no_cluster:
+            if old is None:
+                del os.environ["BRK_DECODE_NO_CLUSTER"]
+            else:
+                os.environ["BRK_DECODE_NO_CLUSTER"] = old
