@@ -103,46 +103,50 @@ struct DecodeLayout {
 };
 
 // rmsnormCpu + ropeCpu (kernels.ts:3395, 3445) of one head row by one warp, in the append
-// kernel's fp64 operations (append.cu; the same bits): the ordered sum of squares by lane 0, then
-// per pair (i, i + D/2) with i = lane + 32 u: y = f32(x * inv * g), rotated in double, rounded to
-// f32 into o0 / o1.  gain == nullptr: no norm; cs == nullptr: no rotation.
+// kernel's fp64 operations (append.cu; the same bits).  Lane l holds the row's pairs
+// (i, i + D/2), i = l + 32 u, in x0 / x1, their norm gains in g0 / g1 and their rotation in e
+// (all loaded by the caller, so that every input is in flight at once).  The sum of squares runs
+// in the oracle's order d = 0 .. D-1 on every lane (the values come by shuffle), then
+// y = f32(x * inv * g), rotated in double and rounded to f32 into o0 / o1.  has_gain false: no
+// norm; has_cs false: no rotation.
 template <int D>
-__device__ __forceinline__ void rotate_row_warp(const float *src, const float *gain, double eps, int one_plus,
-                                                const double2 *cs, int lane, float (&o0)[D / 64], float (&o1)[D / 64]) {
-    constexpr int H2 = D / 2, NP = D / 64;
+__device__ __forceinline__ void rotate_row_regs(const float (&x0)[D / 64], const float (&x1)[D / 64],
+                                                const float (&g0)[D / 64], const float (&g1)[D / 64], bool has_gain,
+                                                double eps, int one_plus, const double2 (&e)[D / 64], bool has_cs,
+                                                float (&o0)[D / 64], float (&o1)[D / 64]) {
+    constexpr int NP = D / 64;
     double y0[NP], y1[NP];
 #pragma unroll
     for (int u = 0; u < NP; ++u) {
-        y0[u] = src[lane + 32 * u];
-        y1[u] = src[lane + 32 * u + H2];
+        y0[u] = x0[u];
+        y1[u] = x1[u];
     }
-    if (gain) {
-        double inv = 0.0;
-        if (lane == 0) {
-            double ss = 0.0;
-#pragma unroll 16
-            for (int d = 0; d < D; ++d) {
-                const double xd = (double)src[d];
-                ss = __fma_rn(xd, xd, ss);  // x^2 is exact in double: one rounding, as ss + x*x
-            }
-            inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)D), eps)));
-        }
-        inv = __shfl_sync(0xffffffffu, inv, 0);
+    if (has_gain) {
+        double ss = 0.0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int u = 0; u < NP; ++u)
+#pragma unroll 8
+                for (int l = 0; l < 32; ++l) {
+                    // Element d = h * D/2 + 32 u + l, in ascending d.
+                    const double xd = (double)__shfl_sync(0xffffffffu, h ? x1[u] : x0[u], l);
+                    ss = __fma_rn(xd, xd, ss);  // x^2 is exact in double: one rounding, as ss + x*x
+                }
+        const double inv = __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(ss, (double)D), eps)));
 #pragma unroll
         for (int u = 0; u < NP; ++u) {
-            const int i = lane + 32 * u;
-            const double w0 = gain[i], w1 = gain[i + H2];
-            const double g0 = one_plus ? __dadd_rn(1.0, w0) : w0, g1 = one_plus ? __dadd_rn(1.0, w1) : w1;
-            y0[u] = (double)(float)__dmul_rn(__dmul_rn(y0[u], inv), g0);
-            y1[u] = (double)(float)__dmul_rn(__dmul_rn(y1[u], inv), g1);
+            const double w0 = g0[u], w1 = g1[u];
+            const double ga = one_plus ? __dadd_rn(1.0, w0) : w0, gb = one_plus ? __dadd_rn(1.0, w1) : w1;
+            y0[u] = (double)(float)__dmul_rn(__dmul_rn(y0[u], inv), ga);
+            y1[u] = (double)(float)__dmul_rn(__dmul_rn(y1[u], inv), gb);
         }
     }
 #pragma unroll
     for (int u = 0; u < NP; ++u) {
-        if (cs) {
-            const double2 e = cs[lane + 32 * u];
-            o0[u] = (float)__dsub_rn(__dmul_rn(y0[u], e.x), __dmul_rn(y1[u], e.y));
-            o1[u] = (float)__dadd_rn(__dmul_rn(y1[u], e.x), __dmul_rn(y0[u], e.y));
+        if (has_cs) {
+            o0[u] = (float)__dsub_rn(__dmul_rn(y0[u], e[u].x), __dmul_rn(y1[u], e[u].y));
+            o1[u] = (float)__dadd_rn(__dmul_rn(y1[u], e[u].x), __dmul_rn(y0[u], e[u].y));
         } else {
             o0[u] = (float)y0[u];
             o1[u] = (float)y1[u];
@@ -161,12 +165,27 @@ __device__ __noinline__ void fused_kv_rows(const DecodeArgs &a, int b, int kvh, 
     constexpr int H2 = D / 2, NP = D / 64;
     const double2 *cs = a.rope ? a.rope + (size_t)past * H2 : nullptr;
     const size_t crow = (size_t)seg * a.cap + (size_t)(past - a.kv_offset);
-#pragma unroll 1
+    // Every input of both rows in flight at once: the K and V pairs, k's norm gains and the
+    // rotation of this position (one round trip to memory instead of one per input).
+    const float *ksrc = a.k_in + ((size_t)b * a.Hkv + kvh) * D, *vsrc = a.v_in + ((size_t)b * a.Hkv + kvh) * D;
+    float in0[2][NP], in1[2][NP], g0[NP], g1[NP];
+    double2 e[NP];
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+        const int i = lane + 32 * u;
+        in0[0][u] = ksrc[i];
+        in1[0][u] = ksrc[i + H2];
+        in0[1][u] = vsrc[i];
+        in1[1][u] = vsrc[i + H2];
+        g0[u] = a.k_norm ? a.k_norm[i] : 0.f;
+        g1[u] = a.k_norm ? a.k_norm[i + H2] : 0.f;
+        e[u] = cs ? cs[i] : make_double2(1.0, 0.0);
+    }
+#pragma unroll
     for (int which = 0; which < 2; ++which) {
         const bool is_k = which == 0;
-        const float *src = (is_k ? a.k_in : a.v_in) + ((size_t)b * a.Hkv + kvh) * D;
         float o0[NP], o1[NP];
-        rotate_row_warp<D>(src, is_k ? a.k_norm : nullptr, a.eps, a.one_plus, is_k ? cs : nullptr, lane, o0, o1);
+        rotate_row_regs<D>(in0[which], in1[which], g0, g1, is_k && a.k_norm, a.eps, a.one_plus, e, is_k && cs, o0, o1);
         if constexpr (Q8) {
             float *x = newrow + which * D;
 #pragma unroll
@@ -319,6 +338,18 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
         float *qstage = xbuf;
         const int nvalid = min(kRT, nrows - row0);
         const float2 *cs = a.rope32 ? a.rope32 + (size_t)past * H2 : nullptr;
+        // The gains and the rotation are the same for every row of the tile (one token): loaded
+        // once, together with the first row, instead of after each row's sum of squares.
+        float gq0[H2 / 32], gq1[H2 / 32];
+        float2 cq[H2 / 32];
+#pragma unroll
+        for (int u = 0; u < H2 / 32; ++u) {
+            const int i = lane + 32 * u;
+            const float w0 = a.q_norm ? a.q_norm[i] : 1.f, w1 = a.q_norm ? a.q_norm[i + H2] : 1.f;
+            gq0[u] = a.q_norm && a.one_plus ? 1.f + w0 : w0;
+            gq1[u] = a.q_norm && a.one_plus ? 1.f + w1 : w1;
+            cq[u] = cs ? cs[i] : make_float2(1.f, 0.f);
+        }
         for (int j = warp; j < nvalid; j += NC) {
             const size_t R = (size_t)b * a.Hq + kvh * G + (row0 + j) % G;  // one token
             const float *src = a.q_in + R * D;
@@ -339,12 +370,12 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
                 const int i = lane + 32 * u;
                 float y0 = x0[u], y1 = x1[u];
                 if (a.q_norm) {
-                    y0 *= inv * (a.one_plus ? 1.f + a.q_norm[i] : a.q_norm[i]);
-                    y1 *= inv * (a.one_plus ? 1.f + a.q_norm[i + H2] : a.q_norm[i + H2]);
+                    y0 *= inv * gq0[u];
+                    y1 *= inv * gq1[u];
                 }
                 float o0 = y0, o1 = y1;
                 if (cs) {
-                    const float2 c = cs[i];
+                    const float2 c = cq[u];
                     o0 = y0 * c.x - y1 * c.y;
                     o1 = y1 * c.x + y0 * c.y;
                 }
