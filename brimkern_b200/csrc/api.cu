@@ -353,7 +353,7 @@ int run_decode(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params 
     // Small grids (every CTA resident at once) merge their splits through a thread-block cluster
     // instead of global partials and a last-arriver merge; the static entry point keeps the
     // workspace merge (its scratch array is what it is for), and so do push launches.
-    const bool cluster = nsplit > 1 && nsplit <= 16 && !fixed_ws && !push && !getenv("BRK_DECODE_NO_CLUSTER") &&
+    const bool cluster = nsplit > 1 && nsplit <= brk::kMaxClusterSplits && !fixed_ws && !push && !getenv("BRK_DECODE_NO_CLUSTER") &&
                          units <= brk::decode_max_clusters(D, kv->q8(), nsplit);
     if (nsplit == 1) {
         a.out = out;  // final output, or (out == nullptr) the caller's partial buffer directly

@@ -49,7 +49,7 @@ struct DecodeCfg<false, 64> {
 };
 template <>
 struct DecodeCfg<false, 128> {
-    static constexpr int kStages = 2, kMinBlocks = 3, kDSplit = 1, kKeyGroups = 4;
+    static constexpr int kStages = 3, kMinBlocks = 2, kDSplit = 1, kKeyGroups = 4;
 };
 template <>
 struct DecodeCfg<false, 256> {

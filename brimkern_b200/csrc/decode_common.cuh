@@ -240,17 +240,35 @@ __device__ __forceinline__ void decode_epilogue_cluster(const DecodeArgs &a, uin
     griddep_launch_dependents();
     cluster_sync_all();  // every split's partial is in its CTA's shared memory
     const int nsplit = a.nsplit;
-    for (int idx = split * NC * 32 + threadIdx.x; idx < nvalid * D; idx += nsplit * NC * 32) {
+    // Every CTA merges an equal contiguous share of the tile's elements (consecutive threads on
+    // consecutive head-dim elements: conflict-free reads of every split's shared memory), so that
+    // all of them work even when the tile has few rows.
+    const int total = nvalid * D, chunk = (total + nsplit - 1) / nsplit;
+    const int e_end = min(total, (split + 1) * chunk);
+    for (int idx = split * chunk + threadIdx.x; idx < e_end; idx += NC * 32) {
         const int r = idx / D, d = idx % D;
+        // Every split's (m, l, o) of this output requested at once: the loads cross the cluster's
+        // network, and one round trip per split in turn cost microseconds at 16 splits.
+        float mv[kMaxClusterSplits], lv[kMaxClusterSplits], ov[kMaxClusterSplits];
+#pragma unroll
+        for (int sp = 0; sp < kMaxClusterSplits; ++sp) {
+            const bool in = sp < nsplit;
+            mv[sp] = in ? ld_cluster_f32(sp_ml + 2 * r, sp) : -CUDART_INF_F;
+            lv[sp] = in ? ld_cluster_f32(sp_ml + 2 * r + 1, sp) : 0.f;
+            ov[sp] = in ? ld_cluster_f32(sp_o + r * D + d, sp) : 0.f;
+        }
         float M = -CUDART_INF_F;
-        for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, ld_cluster_f32(sp_ml + 2 * r, sp));
+#pragma unroll
+        for (int sp = 0; sp < kMaxClusterSplits; ++sp) M = fmaxf(M, mv[sp]);
         float Lsum = 0.f, O = 0.f;
         if (M != -CUDART_INF_F) {
-            for (int sp = 0; sp < nsplit; ++sp) {
-                const float m = ld_cluster_f32(sp_ml + 2 * r, sp);
-                const float w = m == -CUDART_INF_F ? 0.f : exp2f(m - M);
-                Lsum += w * ld_cluster_f32(sp_ml + 2 * r + 1, sp);
-                O += w * ld_cluster_f32(sp_o + r * D + d, sp);
+#pragma unroll
+            for (int sp = 0; sp < kMaxClusterSplits; ++sp) {
+                if (sp < nsplit) {
+                    const float w = mv[sp] == -CUDART_INF_F ? 0.f : exp2f(mv[sp] - M);
+                    Lsum += w * lv[sp];
+                    O += w * ov[sp];
+                }
             }
         }
         const int rr = row0 + r;

@@ -91,6 +91,9 @@ struct AppendArgs {
     int past_len[BRK_MAX_BATCH];
 };
 
+// Most splits of one (sequence, kv head, row tile) that merge through a thread-block cluster.
+constexpr int kMaxClusterSplits = 16;
+
 struct DecodeArgs {
     const float *q;       // [B][T][Hq][D] f32
     float *out;           // [B][T][Hq][D] f32 final output, or nullptr (partial mode)

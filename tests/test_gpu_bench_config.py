@@ -2,10 +2,11 @@
 
 BASELINE config 2 at batch 64: Qwen3-4B shape (32 q / 8 kv heads, head_dim 128, per-head q/k
 RMSNorm, NeoX RoPE theta 1e6), KV length 4096 including the token appended this step.  As in the
-benchmark, every layer goes through brk_attn_step (fused append, then the decode kernel launched
-as its programmatic dependent) with the automatic split choice (four splits per (sequence, kv
-head) on a 148-SM B200, merged in-kernel by the last CTA), and the step is replayed from a CUDA
-graph.  Two layers, so that layer 1's append follows layer 0's decode in the chain.
+benchmark, every layer goes through brk_attn_step (one launch: the append fused into the decode
+kernel, launched as a programmatic dependent of the previous layer's) with the automatic split
+choice (one split per (sequence, kv head) on a 148-SM B200), and again with four splits merged
+in-kernel by the last CTA; the step is replayed from a CUDA graph.  Two layers, so that layer 1
+follows layer 0 in the chain.
 
 Checked on a seeded sample of sequences: the appended K/V rows bit for bit against the oracle
 chain rmsnormCpu -> ropeCpu -> fp16 (kernels.ts:3395-3460), and the attention output within the
@@ -23,7 +24,21 @@ from tests.util import assert_close, bits_equal
 pytestmark = pytest.mark.gpu
 
 
-def test_bench_config_step_graph_replay(eng):
+@pytest.fixture(params=[None, 4], ids=["auto", "split4"])
+def splits(request):
+    import os
+    old = os.environ.get("BRK_DECODE_SPLITS")
+    if request.param is not None:
+        os.environ["BRK_DECODE_SPLITS"] = str(request.param)
+    yield request.param
+    if request.param is not None:
+        if old is None:
+            del os.environ["BRK_DECODE_SPLITS"]
+        else:
+            os.environ["BRK_DECODE_SPLITS"] = old
+
+
+def test_bench_config_step_graph_replay(eng, splits):
     import torch
     from brimkern_b200 import _lib as L
     from brimkern_b200.engine import AttnConfig, KvCache, RopeTable
@@ -50,13 +65,15 @@ def test_bench_config_step_graph_replay(eng):
     q_work = torch.empty_like(q_in)
     out = torch.full((layers, B, 1, Hq, D), float("nan"), device=dev)
 
-    # The split-KV path the benchmark's number comes from.
+    # The split count the benchmark's number comes from (one split -- two waves of 512 CTAs at
+    # two per SM -- on a 148-SM B200), or a forced one.
     p = cfg.params()
     pos = (ctypes.c_int32 * B)(*past)
     nsplit = L.lib().brk_attn_decode_splits(eng.ctx.handle, kv.handle, ctypes.byref(p), B, 1, pos)
-    assert nsplit > 1
-    if torch.cuda.get_device_properties(dev).multi_processor_count == 148:
-        assert nsplit == 4
+    if splits is None and torch.cuda.get_device_properties(dev).multi_processor_count == 148:
+        assert nsplit == 1
+    if splits is not None:
+        assert nsplit == splits
 
     def step():
         for layer in range(layers):
