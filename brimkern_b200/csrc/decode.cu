@@ -97,10 +97,23 @@ struct DecodeLayout {
     static constexpr uint32_t kXBytes = kSwapBytes > kQBytes ? kSwapBytes : kQBytes;
     // Fused append into an int8 cache: the new K and V rows in f32, quantised from here.
     static constexpr uint32_t kNewRowBytes = Q8 ? 2 * D * 4 : 0;
-    static constexpr uint32_t kBarBytes = 2 * C::kStages * 8;  // full, empty
-    static constexpr uint32_t kSmemBytes = 1024 + kRingBytes + kXBytes + kNewRowBytes + kBarBytes;
+    // Fused append: the new K and V rows as the cache stores them (fp16, or int8 codes and then
+    // their two scales), patched into the ring stage that holds that row.
+    static constexpr uint32_t kPatchBytes = Q8 ? 2 * D + 16 : 4 * D;
+    static constexpr uint32_t kBarBytes = (2 * C::kStages + 2) * 8;  // full, empty, row load, row done
+    static constexpr uint32_t kSmemBytes = 1024 + kRingBytes + kXBytes + kNewRowBytes + kPatchBytes + kBarBytes;
     static_assert(decode_epilogue_bytes<D, kKG, kRT>() <= kRingBytes, "merge buffers must fit in the ring");
 };
+
+// Fused append: a warp of its own computes the new rows while the producer streams (fp16 caches);
+// the int8 kernels, whose four CTAs per SM leave no registers for a sixth warp, compute them in
+// the producer warp after its first ring stages.
+template <bool Q8, bool F>
+struct DecodeRowWarp {
+    static constexpr bool value = F && !Q8;
+};
+template <bool Q8, int D, bool F>
+constexpr int decode_threads() { return DecodeLayout<Q8, D>::kThreads + (DecodeRowWarp<Q8, F>::value ? 32 : 0); }
 
 // rmsnormCpu + ropeCpu (kernels.ts:3395, 3445) of one head row by one warp, in the append
 // kernel's fp64 operations (append.cu; the same bits).  Lane l holds the row's pairs
@@ -161,7 +174,7 @@ __device__ __forceinline__ void rotate_row_regs(const float (&x0)[D / 64], const
 // the async proxy, which the warp's next TMA load of that row requires.
 template <bool Q8, int D>
 __device__ __noinline__ void fused_kv_rows(const DecodeArgs &a, int b, int kvh, int past, int seg, float *newrow,
-                                           int lane) {
+                                           uint8_t *patch, int lane) {
     constexpr int H2 = D / 2, NP = D / 64;
     const double2 *cs = a.rope ? a.rope + (size_t)past * H2 : nullptr;
     const size_t crow = (size_t)seg * a.cap + (size_t)(past - a.kv_offset);
@@ -197,22 +210,58 @@ __device__ __noinline__ void fused_kv_rows(const DecodeArgs &a, int b, int kvh, 
             quantize_row_warp(x, D, (is_k ? a.kc8 : a.vc8) + crow * D,
                               a.scales + ((size_t)seg * 2 + which) * a.scale_pitch + (size_t)(past - a.kv_offset),
                               lane);
+            quantize_row_warp(x, D, patch + which * D, reinterpret_cast<float *>(patch + 2 * D) + which, lane);
         } else {
             __half *dst = (is_k ? a.kc : a.vc) + crow * D;
+            __half *pd = reinterpret_cast<__half *>(patch) + which * D;
 #pragma unroll
             for (int u = 0; u < NP; ++u) {
-                dst[lane + 32 * u] = __float2half_rn(o0[u]);
-                dst[lane + 32 * u + H2] = __float2half_rn(o1[u]);
+                const __half h0 = __float2half_rn(o0[u]), h1 = __float2half_rn(o1[u]);
+                dst[lane + 32 * u] = h0;
+                dst[lane + 32 * u + H2] = h1;
+                pd[lane + 32 * u] = h0;
+                pd[lane + 32 * u + H2] = h1;
             }
         }
     }
-    fence_proxy_async_global();
+}
+
+// Fused append, by the producer's elected lane: the new rows from `patch` into the ring stage `st`
+// (whose copy of the cache has landed) at row `rpos`, in the stage's swizzled layouts, fp16 rows
+// or int8 codes plus their scales.
+template <bool Q8, int D>
+__device__ __forceinline__ void patch_new_row(uint8_t *st, int rpos, const uint8_t *patch) {
+    using L = DecodeLayout<Q8, D>;
+#pragma unroll 1
+    for (int which = 0; which < 2; ++which) {
+        uint8_t *base = st + which * L::kTileBytes;
+        if constexpr (Q8) {
+            for (int b0 = 0; b0 < D; b0 += 16) {
+                const int j = b0 / L::kBoxCols, cb = (b0 % L::kBoxCols) / 16;
+                const uint32_t off = L::kBoxCols == 128 ? sw128(rpos, cb) : sw64(rpos, cb);
+                *reinterpret_cast<uint4 *>(base + j * L::kBoxBytes + off) =
+                    *reinterpret_cast<const uint4 *>(patch + which * D + b0);
+            }
+        } else {
+            for (int d0 = 0; d0 < D; d0 += 8) {
+                const int j = d0 / 64, c = (d0 % 64) / 8;
+                *reinterpret_cast<uint4 *>(base + j * L::kBoxBytes + sw128(rpos, c)) =
+                    *reinterpret_cast<const uint4 *>(patch + (which * D + d0) * 2);
+            }
+        }
+    }
+    if constexpr (Q8) {
+        float *sc = reinterpret_cast<float *>(st + 2 * L::kTileBytes);
+        const float *ps = reinterpret_cast<const float *>(patch + 2 * D);
+        sc[rpos] = ps[0];
+        sc[L::kStageKeys + rpos] = ps[1];
+    }
 }
 
 // F: the fused-append form (brk_attn_step with one token); a separate instantiation, so that the
 // plain kernel's code and registers stay as they are.
 template <bool Q8, int D, bool F>
-__global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D>::kMinBlocks)
+__global__ void __launch_bounds__(decode_threads<Q8, D, F>(), DecodeCfg<Q8, D>::kMinBlocks)
     decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                    const __grid_constant__ CUtensorMap tms, const __grid_constant__ DecodeArgs a) {
     using L = DecodeLayout<Q8, D>;
@@ -234,8 +283,11 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
     uint8_t *ring = smem;
     float *xbuf = reinterpret_cast<float *>(ring + L::kRingBytes);
     float *newrow = reinterpret_cast<float *>(ring + L::kRingBytes + L::kXBytes);  // int8: [2][D]
-    uint64_t *full = reinterpret_cast<uint64_t *>(ring + L::kRingBytes + L::kXBytes + L::kNewRowBytes);
+    uint8_t *patch = ring + L::kRingBytes + L::kXBytes + L::kNewRowBytes;
+    uint64_t *full = reinterpret_cast<uint64_t *>(patch + L::kPatchBytes);
     uint64_t *empty = full + S;
+    uint64_t *rowbar = empty + S;    // fused append: the copy of the stage that holds the new row
+    uint64_t *rowdone = rowbar + 1;  // fused append: the new rows are in `patch`
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int split = blockIdx.x;
@@ -261,17 +313,24 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], NC);
         }
+        mbar_init(rowbar, 1);
+        mbar_init(rowdone, 1);
         fence_barrier_init();
     }
     __syncthreads();
 
     if (warp == NC) {
         // ---- producer: one elected lane streams the stages through the ring.
-        // Fused append: the warp pauses after the first ring stages (or before the stage holding
-        // the new row, if that comes first) to compute and store the new K / V rows.
-        const int pause = writes_row ? min(S, (new_row - k_begin) / SK) : ntiles;
+        // Fused append: the stage that holds the new row (tile rt) is loaded as usual but counted
+        // on `rowbar`; once that copy has landed and the row warp has the new rows ready, the rows
+        // are patched into the stage and only then is the stage released to the consumers.  So the
+        // copy of that stage does not wait for the new rows, and the rows do not make a round trip
+        // through memory before the consumers see them.
+        constexpr bool kRowWarp = DecodeRowWarp<Q8, F>::value;
+        const int rt = writes_row ? (new_row - k_begin) / SK : -1;
         int issued = 0;
         bool ok = true;
+        bool row_ready = kRowWarp;  // the patch may be applied as soon as the stage is issued
         auto issue = [&](int i_end) {
             for (int i = issued; i < i_end && ok; ++i) {
                 const int s = i % S;
@@ -280,16 +339,27 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&full[s], L::kLoadBytes);
+                uint64_t *bar = i == rt ? rowbar : &full[s];
+                mbar_arrive_expect_tx(bar, L::kLoadBytes);
                 uint8_t *st = ring + s * L::kStageBytes;
                 const int y = seg * a.cap + key;
 #pragma unroll
-                for (int j = 0; j < L::kBoxes; ++j) tma_load_2d(st + j * L::kBoxBytes, &tmk, j * L::kBoxElems, y, &full[s]);
+                for (int j = 0; j < L::kBoxes; ++j) tma_load_2d(st + j * L::kBoxBytes, &tmk, j * L::kBoxElems, y, bar);
 #pragma unroll
                 for (int j = 0; j < L::kBoxes; ++j)
-                    tma_load_2d(st + L::kTileBytes + j * L::kBoxBytes, &tmv, j * L::kBoxElems, y, &full[s]);
-                if constexpr (Q8) tma_load_2d(st + 2 * L::kTileBytes, &tms, key, seg * 2, &full[s]);
+                    tma_load_2d(st + L::kTileBytes + j * L::kBoxBytes, &tmv, j * L::kBoxElems, y, bar);
+                if constexpr (Q8) tma_load_2d(st + 2 * L::kTileBytes, &tms, key, seg * 2, bar);
                 issued = i + 1;
+                if constexpr (F) {
+                    if (i == rt && row_ready) {
+                        // Bounded waits; on a timeout the error word is set and the stage still
+                        // goes to the consumers (whose results are then meaningless).
+                        if ((!kRowWarp || mbar_wait(rowdone, 0, a.err, kErrMmaTimeout)) &&
+                            mbar_wait(rowbar, 0, a.err, kErrTmaTimeout))
+                            patch_new_row<Q8, D>(st, new_row - key, patch);
+                        mbar_arrive(&full[s]);
+                    }
+                }
             }
         };
         if (ntiles > 0) {
@@ -303,12 +373,21 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
             // that trigger their dependents early wait for their own predecessors before they
             // finish, from anything the stream ran before.  The CTA's set-up has overlapped it.
             griddep_wait();
-            if (lane == 0) issue(pause);
-            if constexpr (F) {
+            if constexpr (F && !kRowWarp) {
                 if (writes_row) {
+                    // The first ring stages (the new row's among them, unpatched, if it is that
+                    // early), then the rows, then the patch of that stage if it is already issued.
+                    if (lane == 0) issue(min(ntiles, S));
                     __syncwarp();
-                    fused_kv_rows<Q8, D>(a, b, kvh, past, seg, newrow, lane);
-                    __syncwarp();  // every lane's row stores and proxy fence before the row's load
+                    fused_kv_rows<Q8, D>(a, b, kvh, past, seg, newrow, patch, lane);
+                    __syncwarp();
+                    row_ready = true;
+                    if (lane == 0 && issued > rt) {
+                        uint8_t *st = ring + (rt % S) * L::kStageBytes;
+                        if (mbar_wait(rowbar, 0, a.err, kErrTmaTimeout))
+                            patch_new_row<Q8, D>(st, new_row - (k_begin + rt * SK), patch);
+                        mbar_arrive(&full[rt % S]);
+                    }
                 }
             }
             if (lane == 0) {
@@ -323,6 +402,24 @@ __global__ void __launch_bounds__(DecodeLayout<Q8, D>::kThreads, DecodeCfg<Q8, D
             decode_cluster_idle();  // the cluster merge's two barriers count every thread
         }
         return;
+    }
+    if constexpr (DecodeRowWarp<Q8, F>::value) {
+        if (warp == NC + 1) {
+            // ---- fused append: the row warp computes the new K / V rows (the append kernel's fp64
+            // operations, hence its bits), stores them in the cache for later steps and leaves them
+            // in `patch` for the producer, while the producer streams the other stages.
+            if (writes_row) {
+                griddep_wait();  // k_in / v_in may come from the preceding kernel
+                fused_kv_rows<Q8, D>(a, b, kvh, past, seg, newrow, patch, lane);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(rowdone);  // release: the patch bytes before the producer's wait
+            }
+            if (a.cluster) {
+                __syncwarp();
+                decode_cluster_idle();
+            }
+            return;
+        }
     }
 
     griddep_wait();  // q (or, fused, q_in / k_in / v_in) may come from the preceding kernel
@@ -800,7 +897,7 @@ cudaError_t launch_t(const CUtensorMap &tmk, const CUtensorMap &tmv, const CUten
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(DecodeLayout<Q8, D>::kThreads);
+    cfg.blockDim = dim3(decode_threads<Q8, D, F>());
     cfg.dynamicSmemBytes = DecodeLayout<Q8, D>::kSmemBytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
