@@ -195,6 +195,7 @@ def run_prefill(args, c, workload, eng=None, emit=True):
     k_in = torch.randn((layers, nch, B, CH, Hkv, D), generator=gen, device=dev)
     v_in = torch.randn((layers, nch, B, CH, Hkv, D), generator=gen, device=dev)
     q_work = torch.empty((B, CH, Hq, D), dtype=torch.float32, device=dev)
+    q16_work = torch.empty((B, CH, Hq, D), dtype=torch.float16, device=dev)
     out = torch.empty((layers, nch, B, CH, Hq, D), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream()
     flops = prefill_flops(c, B)
@@ -207,10 +208,16 @@ def run_prefill(args, c, workload, eng=None, emit=True):
                     # The product path: K/V append + tensor-core kernel with the q prologue fused.
                     eng.prefillStep(kv, layer, cfg, qi[layer, ci], ki[layer, ci], vi[layer, ci], oo[layer, ci], pos)
                 else:
-                    # Roofline pass: the attention kernel alone, on pre-rotated q.
+                    # Roofline pass: the attention kernel alone, on pre-rotated q -- fp16 rows loaded
+                    # with TMA as in the product path (fp16 cache), or f32 rows it stages (int8).
                     eng.appendKv(kv, layer, cfg, qi[layer, ci], ki[layer, ci], vi[layer, ci], q_work, pos)
+                    if not q8:
+                        q16_work.copy_(q_work)
                     ev[layer][ci][0].record(stream)
-                    eng.recAttention(kv, layer, cfg, q_work, oo[layer, ci], pos, kernel="prefill")
+                    if q8:
+                        eng.recAttention(kv, layer, cfg, q_work, oo[layer, ci], pos, kernel="prefill")
+                    else:
+                        eng.prefillHalfQ(kv, layer, cfg, q16_work, oo[layer, ci], pos)
                     ev[layer][ci][1].record(stream)
 
     def barrier():

@@ -84,6 +84,7 @@ SIGNATURES = [
     ("brk_attn_decode_splits", _i, [_vp, _vp, _PARAMS, _i, _i, _i32p]),
     ("brk_attn_decode_static", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp]),
     ("brk_attn_prefill", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp]),
+    ("brk_attn_prefill_h", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp]),
     ("brk_attn_prefill_step", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp, _vp, _vp]),
     ("brk_attn_full", _i, [_vp, _PARAMS, _i, _i, _i, _vp, _vp, _vp, _vp, _vp]),
     ("brk_attn_decode_partial", _i, [_vp, _vp, _i, _PARAMS, _i, _i, _i32p, _vp, _vp, _vp, _vp]),

@@ -844,8 +844,9 @@ int brk_kv_read_codes(const brk_kv *kv, int layer, int seq, int row0, int n_rows
 namespace {
 int append_impl(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
                 const int32_t *past_len, const float *q_in, const float *k_in, const float *v_in, float *q_out,
-                void *stream, bool pdl) {
-    if ((q_in == nullptr) != (q_out == nullptr)) return fail(BRK_ERR_INVALID, "q_in and q_out go together");
+                void *stream, bool pdl, __half *q16 = nullptr) {
+    if ((q_in != nullptr) != (q_out != nullptr || q16 != nullptr))
+        return fail(BRK_ERR_INVALID, "q_in and q_out go together");
     if ((k_in == nullptr) != (v_in == nullptr)) return fail(BRK_ERR_INVALID, "k_in and v_in go together");
     if (kv) {
         int rc = check_call(ctx, kv, layer, p, batch, n_tokens, past_len);
@@ -881,6 +882,8 @@ int append_impl(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, i
     a.k_in = k_in;
     a.v_in = v_in;
     a.q_out = q_out;
+    a.q16 = q16;
+    a.rope32 = q16 && p->rope ? p->rope->table32 : nullptr;
     a.kc = kv ? kv->k : nullptr;
     a.vc = kv ? kv->v : nullptr;
     a.kc8 = kv ? kv->k8 : nullptr;
@@ -999,10 +1002,10 @@ int ensure_stage(brk_ctx *ctx, size_t bytes) {
 // the non-causal path whose rows all sit at the last key.
 int prefill_impl(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
                  const int32_t *past_len, const float *q, const float *q_raw, float *out, void *stream,
-                 bool clamp_rows = false, bool pdl = false) {
+                 bool clamp_rows = false, bool pdl = false, const __half *q16 = nullptr) {
     int rc = check_call(ctx, kv, layer, p, batch, n_tokens, past_len);
     if (rc) return rc;
-    if ((!q && !q_raw) || !out) return fail(BRK_ERR_INVALID, "null q or out");
+    if ((!q && !q_raw && !q16) || !out) return fail(BRK_ERR_INVALID, "null q or out");
     if (q_raw && p->rope) {
         if (p->rope->head_dim != p->head_dim || p->rope->ctx != ctx)
             return fail(BRK_ERR_INVALID, "rope table head_dim %d != %d", p->rope->head_dim, p->head_dim);
@@ -1023,8 +1026,9 @@ int prefill_impl(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_param
     }
     if ((n_tokens + 127) / 128 > 65535) return fail(BRK_ERR_INVALID, "n_tokens %d too large", n_tokens);
     DeviceGuard g(ctx->device);
-    a.q = q_raw ? nullptr : q;
-    a.q_raw = q_raw;
+    a.q = q_raw || q16 ? nullptr : q;
+    a.q_raw = q16 ? nullptr : q_raw;
+    a.q_tma = q16 ? 1 : 0;
     a.q_norm = q_raw ? p->q_norm : nullptr;
     a.rope = q_raw && p->rope ? p->rope->table32 : nullptr;
     a.eps = (float)p->eps;
@@ -1072,7 +1076,12 @@ int prefill_impl(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_param
         ++ctx->launches;
         return BRK_OK;
     }
-    cudaError_t e = brk::launch_prefill(p->head_dim, kv->tm_pre_k, kv->tm_pre_v, a, st, pdl);
+    CUtensorMap tmq;
+    if (q16 && (rc = make_map(&tmq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sizeof(__half), q16, (uint64_t)batch * n_tokens,
+                              (uint64_t)p->n_heads * p->head_dim, 64u, (uint32_t)brk::kPrefillQRows,
+                              CU_TENSOR_MAP_SWIZZLE_128B)))
+        return rc;
+    cudaError_t e = brk::launch_prefill(p->head_dim, kv->tm_pre_k, kv->tm_pre_v, a, st, pdl, q16 ? &tmq : nullptr);
     if (e != cudaSuccess) return cuda_fail(e, "prefill kernel launch");
     ++ctx->launches;
     return BRK_OK;
@@ -1084,13 +1093,38 @@ int brk_attn_prefill(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_p
     return prefill_impl(ctx, kv, layer, p, batch, n_tokens, past_len, q, nullptr, out, stream);
 }
 
+int brk_attn_prefill_h(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
+                       const int32_t *past_len, const uint16_t *q16, float *out, void *stream) {
+    if (!q16) return fail(BRK_ERR_INVALID, "null q");
+    if (reinterpret_cast<uintptr_t>(q16) % 16) return fail(BRK_ERR_INVALID, "q must be 16-byte aligned");
+    if (kv && kv->q8()) return fail(BRK_ERR_UNSUPPORTED, "fp16 q into the prefill kernel covers fp16 caches");
+    return prefill_impl(ctx, kv, layer, p, batch, n_tokens, past_len, nullptr, nullptr, out, stream, false, false,
+                        reinterpret_cast<const __half *>(q16));
+}
+
 int brk_attn_prefill_step(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p, int batch, int n_tokens,
                           const int32_t *past_len, const float *q_in, const float *k_in, const float *v_in, float *out,
                           void *stream) {
     if (!q_in || !k_in || !v_in || !out) return fail(BRK_ERR_INVALID, "null tensor argument");
-    // K/V rows only: the q prologue runs inside the prefill kernel, launched programmatically
-    // dependent on the append so that the prologue overlaps it.
-    int rc = append_impl(ctx, kv, layer, p, batch, n_tokens, past_len, nullptr, k_in, v_in, nullptr, stream, false);
+    int rc = check_call(ctx, kv, layer, p, batch, n_tokens, past_len);
+    if (rc) return rc;
+    // fp16 caches, chunks of 8+ tokens: the K/V append kernel also rotates q (f32, the prefill
+    // kernel's own q arithmetic) into fp16 rows in the context's staging buffer, which the prefill
+    // kernel loads with TMA -- its q prologue would otherwise sit before each CTA's first MMA.
+    // Otherwise the append stores K/V only and the q prologue runs inside the prefill kernel.
+    // Either way the prefill kernel is launched as a programmatic dependent of the append.
+    if (!kv->q8() && (p->head_dim == 64 || p->head_dim == 128) && n_tokens >= 8) {
+        if (p->rope && (p->rope->head_dim != p->head_dim || p->rope->ctx != ctx))
+            return fail(BRK_ERR_INVALID, "rope table head_dim %d != %d", p->rope->head_dim, p->head_dim);
+        rc = ensure_stage(ctx, (size_t)batch * n_tokens * p->n_heads * p->head_dim * sizeof(__half));
+        if (rc) return rc;
+        __half *q16 = static_cast<__half *>(ctx->stage);
+        rc = append_impl(ctx, kv, layer, p, batch, n_tokens, past_len, q_in, k_in, v_in, nullptr, stream, false, q16);
+        if (rc) return rc;
+        return prefill_impl(ctx, kv, layer, p, batch, n_tokens, past_len, nullptr, nullptr, out, stream, false, true,
+                            q16);
+    }
+    rc = append_impl(ctx, kv, layer, p, batch, n_tokens, past_len, nullptr, k_in, v_in, nullptr, stream, false);
     if (rc) return rc;
     return prefill_impl(ctx, kv, layer, p, batch, n_tokens, past_len, nullptr, q_in, out, stream, false, true);
 }

@@ -300,6 +300,72 @@ __global__ void __launch_bounds__(256) append_block_kernel(const __grid_constant
 // double sum of squares; then a warp per K row applies the norm and the rotation with exactly
 // append_block_kernel's double operations (same bits; it only spends far fewer instructions on
 // row bookkeeping).
+//
+// With a.q16 the grid has Hq more blocks along y: those rotate the chunk's q rows instead (one
+// warp per row, RMSNorm and NeoX rotation in f32 with the f32 table, exactly the prefill kernel's
+// q prologue: q only feeds its fp16 tensor-core operand) and store them as fp16 for the prefill
+// kernel's TMA loads.
+template <int D>
+__device__ __forceinline__ void q16_rows(const AppendArgs &a, int hq, int b, int t0, int nt, int warp, int lane) {
+    constexpr int TT = 32, RPW = TT / 8, H2 = D / 2, P = H2 / 32;
+    const int i0 = lane * P;
+    const int pos0 = a.past_len[b] + t0;
+    float g0[P], g1[P];
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+        const float w0 = a.q_norm ? a.q_norm[i0 + p] : 1.f, w1 = a.q_norm ? a.q_norm[i0 + p + H2] : 1.f;
+        g0[p] = a.q_norm && a.one_plus ? 1.f + w0 : w0;
+        g1[p] = a.q_norm && a.one_plus ? 1.f + w1 : w1;
+    }
+    float x0[RPW][P], x1[RPW][P], c[RPW][P], sn[RPW][P];
+#pragma unroll
+    for (int u = 0; u < RPW; ++u) {
+        const int tl = warp + 8 * u;
+        const bool ok = tl < nt;
+        const float *src = a.q_in + ((size_t)(b * a.T + t0 + (ok ? tl : 0)) * a.Hq + hq) * D;
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+            x0[u][p] = ok ? src[i0 + p] : 0.f;
+            x1[u][p] = ok ? src[i0 + p + H2] : 0.f;
+            const float2 e = ok && a.rope32 ? a.rope32[(size_t)(pos0 + tl) * H2 + i0 + p] : make_float2(1.f, 0.f);
+            c[u][p] = e.x, sn[u][p] = e.y;
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < RPW; ++u) {
+        const int tl = warp + 8 * u;
+        float inv = 1.f;
+        if (a.q_norm) {
+            float ss = 0.f;
+#pragma unroll
+            for (int p = 0; p < P; ++p) ss = fmaf(x0[u][p], x0[u][p], fmaf(x1[u][p], x1[u][p], ss));
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+            inv = 1.f / sqrtf(ss / (float)D + (float)a.eps);
+        }
+        float o0[P], o1[P];
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+            const float y0 = x0[u][p] * inv * g0[p], y1 = x1[u][p] * inv * g1[p];
+            o0[p] = fmaf(y0, c[u][p], -(y1 * sn[u][p]));
+            o1[p] = fmaf(y1, c[u][p], y0 * sn[u][p]);
+        }
+        if (tl < nt) {
+            __half *dst = a.q16 + ((size_t)(b * a.T + t0 + tl) * a.Hq + hq) * D;
+            if constexpr (P == 2) {
+                *reinterpret_cast<uint32_t *>(dst + i0) = pack_half2(o0[0], o0[1]);
+                *reinterpret_cast<uint32_t *>(dst + i0 + H2) = pack_half2(o1[0], o1[1]);
+            } else {
+#pragma unroll
+                for (int p = 0; p < P; ++p) {
+                    dst[i0 + p] = __float2half_rn(o0[p]);
+                    dst[i0 + p + H2] = __float2half_rn(o1[p]);
+                }
+            }
+        }
+    }
+}
+
 template <int D>
 __global__ void __launch_bounds__(256) kv_append_kernel(const __grid_constant__ AppendArgs a) {
     griddep_wait();  // then the dependent may start (see append_kernel)
@@ -313,6 +379,10 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const __grid_constant__ 
     const int t0 = blockIdx.x * TT, h = blockIdx.y, b = blockIdx.z;
     const int nt = min(TT, a.T - t0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (h >= a.Hkv) {
+        q16_rows<D>(a, h - a.Hkv, b, t0, nt, warp, lane);
+        return;
+    }
     const int pos0 = a.past_len[b] + t0;
     const size_t crow0 = ((size_t)(a.layer * a.B + b) * a.Hkv + h) * a.cap + (size_t)(pos0 - a.kv_offset);
     __half *kc = a.kc + crow0 * D, *vc = a.vc + crow0 * D;
@@ -469,7 +539,7 @@ cudaError_t launch_append(const AppendArgs &a, cudaStream_t s, bool pdl) {
         rows = block_rows;
         // K / V only into an fp16 cache (prefill chunks): the dedicated kernel.
         if (!a.q_out && a.k_in && a.v_in && a.kc && a.T >= 8) {
-            cfg.gridDim = dim3((unsigned)((a.T + 31) / 32), (unsigned)a.Hkv, (unsigned)a.B);
+            cfg.gridDim = dim3((unsigned)((a.T + 31) / 32), (unsigned)(a.Hkv + (a.q16 ? a.Hq : 0)), (unsigned)a.B);
             cfg.blockDim = dim3(256);
             cfg.dynamicSmemBytes = 0;
             switch (a.D) {

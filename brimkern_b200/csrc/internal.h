@@ -88,8 +88,15 @@ struct AppendArgs {
     double eps;
     int one_plus;
     int B, T, Hq, Hkv, D, layer, cap, kv_offset;
+    // Prefill chunks into an fp16 cache: q rotated in f32 (as the prefill kernel's own q
+    // prologue does) into fp16 [B][T][Hq][D] for the prefill kernel's TMA loads, or nullptr.
+    __half *q16;
+    const float2 *rope32;
     int past_len[BRK_MAX_BATCH];
 };
+
+// Query rows per stream of the tensor-core prefill kernel (its q tiles' TMA box height).
+constexpr int kPrefillQRows = 128;
 
 // Most splits of one (sequence, kv head, row tile) that merge through a thread-block cluster.
 constexpr int kMaxClusterSplits = 16;
@@ -150,6 +157,9 @@ struct PrefillArgs {
     const float *q_raw;
     const float *q_norm;
     const float2 *rope;
+    // q already rotated to fp16 [B][T][Hq][D] (the append of the chunk wrote it): the producer
+    // loads both streams' q tiles with TMA (map `tmq`) and the softmax warps stage nothing.
+    int q_tma;
     float eps;
     int one_plus;
     int *err;
@@ -205,7 +215,7 @@ cudaError_t launch_combine_peers(const CombineArgs &a, const unsigned *flags, in
                                  unsigned long long wait_ns, int *err, cudaStream_t s);
 // Tensor-core prefill (head_dim 64 or 128); maps with prefill_tile_keys()-row boxes.
 cudaError_t launch_prefill(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const PrefillArgs &a,
-                           cudaStream_t s, bool pdl = false);
+                           cudaStream_t s, bool pdl = false, const CUtensorMap *tmq = nullptr);
 // Concurrent CTAs per SM of the decode kernel for a head dim and cache type (occupancy query).
 int decode_ctas_per_sm(int head_dim, bool q8);
 

@@ -28,7 +28,7 @@ namespace brk {
 
 namespace {
 
-constexpr int kTQ = 128;       // queries per stream (the MMA's M)
+constexpr int kTQ = kPrefillQRows;  // queries per stream (the MMA's M)
 constexpr int kTK = 64;        // keys per tile (N of QK^T, K of PV)
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;   // stream 0's MMA issuer (and the TMEM allocator)
@@ -90,6 +90,7 @@ __device__ __forceinline__ float score_log2(float dot, const PrefillArgs &a) {
 template <int D, bool CAP>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                        const __grid_constant__ CUtensorMap tmq,
                         const __grid_constant__ PrefillArgs a) {
     using L = PrefillLayout<D>;
     extern __shared__ uint8_t smem_raw[];
@@ -135,8 +136,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&bars[kBarPFull + s], 128);
             mbar_init(&bars[kBarODone + s], 1);
         }
-        mbar_init(&bars[kBarQFull], 256);
-        mbar_init(&bars[kBarQFull1], 256);
+        // q by TMA: the producer's one arrival with the copy's bytes; else all eight softmax warps.
+        mbar_init(&bars[kBarQFull], a.q_tma ? 1 : 256);
+        mbar_init(&bars[kBarQFull1], a.q_tma ? 1 : 256);
         mbar_init(&bars[kBarMmaDone], 1);
         mbar_init(&bars[kBarMmaDone + 1], 1);
         mbar_init(&bars[kBarStagger], 128);
@@ -161,10 +163,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0 && nk > 0) {
             tma_prefetch_desc(&tmk);
             tma_prefetch_desc(&tmv);
+            if (a.q_tma) tma_prefetch_desc(&tmq);
             // Launched right behind the append of this chunk's K/V (programmatic dependent launch,
             // scheduled once the append has waited for its own predecessors, so the q projection
-            // the prologue reads is complete): only these cache reads wait for the append.
+            // the prologue reads is complete): only these cache reads (and the rotated q the append
+            // wrote) wait for the append.
             griddep_wait();
+            if (a.q_tma) {
+                // Both streams' q tiles: [128 tokens][64 dims] fp16 boxes of the [B*T][Hq*D] rows,
+                // 128-byte swizzled -- the MMA's K-major A layout.  Rows past the chunk's end read
+                // the next sequence's q (or zeros past the last): rows the softmax never writes.
+#pragma unroll 1
+                for (int sg = 0; sg < (active1 ? 2 : 1); ++sg) {
+                    uint64_t *qb = &bars[sg ? kBarQFull1 : kBarQFull];
+                    const int hs = sg ? head1 : head0, qs0 = sg ? q01 : q00;
+                    mbar_arrive_expect_tx(qb, L::kQBytes);
+#pragma unroll
+                    for (int blk = 0; blk < L::kBlocks; ++blk)
+                        tma_load_2d(sQ(sg) + blk * L::kQBlock, &tmq, hs * D + blk * 64, b * T + qs0, qb);
+                }
+            }
             int issued = 0;
             for (int j = 0; j < nk; ++j) {
                 const int st = j % L::kStages;
@@ -251,8 +269,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool row_ok = r < nqs;
         const int t = q0 + r;
         // Stage both streams' q rows as fp16 in the 128-byte swizzled K-major layout of the MMA's
-        // A operand.
-        if (a.q_raw) {
+        // A operand (unless the producer loads them already rotated).
+        if (a.q_tma) {
+        } else if (a.q_raw) {
             // Fused q prologue: the per-head RMSNorm and NeoX rotation of the stream's query rows
             // (rmsnormCpu kernels.ts:3395, ropeCpu :3445) in f32 with the f32 copy of the table.
             // q only feeds the fp16 tensor-core operand, so the append's fp64 path (which the
@@ -540,7 +559,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int D, bool CAP>
-cudaError_t launch_prefill_t(const CUtensorMap &tmk, const CUtensorMap &tmv, const PrefillArgs &a, cudaStream_t s,
+cudaError_t launch_prefill_t(const CUtensorMap &tmk, const CUtensorMap &tmv, const CUtensorMap &tmq, const PrefillArgs &a,
+                             cudaStream_t s,
                              bool pdl) {
     static unsigned long long configured = 0;
     int dev = 0;
@@ -564,7 +584,7 @@ cudaError_t launch_prefill_t(const CUtensorMap &tmk, const CUtensorMap &tmv, con
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, prefill_attn_kernel<D, CAP>, tmk, tmv, a);
+    return cudaLaunchKernelEx(&cfg, prefill_attn_kernel<D, CAP>, tmk, tmv, tmq, a);
 }
 
 }  // namespace
@@ -572,14 +592,15 @@ cudaError_t launch_prefill_t(const CUtensorMap &tmk, const CUtensorMap &tmv, con
 int prefill_tile_keys() { return kTK; }
 
 cudaError_t launch_prefill(int head_dim, const CUtensorMap &tmk, const CUtensorMap &tmv, const PrefillArgs &a,
-                           cudaStream_t s, bool pdl) {
+                           cudaStream_t s, bool pdl, const CUtensorMap *tmq) {
     const bool cap = a.softcap > 0.f;
+    const CUtensorMap &q = tmq ? *tmq : tmk;  // unused unless a.q_tma
     switch (head_dim) {
         case 64:
-            return cap ? launch_prefill_t<64, true>(tmk, tmv, a, s, pdl) : launch_prefill_t<64, false>(tmk, tmv, a, s, pdl);
+            return cap ? launch_prefill_t<64, true>(tmk, tmv, q, a, s, pdl) : launch_prefill_t<64, false>(tmk, tmv, q, a, s, pdl);
         case 128:
-            return cap ? launch_prefill_t<128, true>(tmk, tmv, a, s, pdl)
-                       : launch_prefill_t<128, false>(tmk, tmv, a, s, pdl);
+            return cap ? launch_prefill_t<128, true>(tmk, tmv, q, a, s, pdl)
+                       : launch_prefill_t<128, false>(tmk, tmv, q, a, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -536,6 +536,20 @@ class AttentionEngine:
         check(fn(self.ctx.handle, kv.handle, layer, ctypes.byref(p), B, T, pos, _ptr(q), _ptr(out), _stream_ptr(stream)))
         return out
 
+    def prefillHalfQ(self, kv: KvCache, layer: int, cfg: AttnConfig, q16: torch.Tensor, out: torch.Tensor, past_len,
+                     stream=None) -> torch.Tensor:
+        """The tensor-core prefill kernel on q already rotated, as fp16 [B, T, Hq, D] (loaded with
+        TMA): the form brk_attn_prefill_step uses for fp16 caches."""
+        if q16.dtype != torch.float16:
+            raise BrkError(L.BRK_ERR_INVALID, "q16 must be float16")
+        B = kv.batch
+        T = q16.numel() // (B * cfg.n_heads * cfg.head_dim)
+        p = cfg.params()
+        pos = _positions(past_len, B)
+        check(L.lib().brk_attn_prefill_h(self.ctx.handle, kv.handle, layer, ctypes.byref(p), B, T, pos, _ptr(q16),
+                                         _ptr(out), _stream_ptr(stream)))
+        return out
+
     def appendKv(self, kv: KvCache, layer: int, cfg: AttnConfig, q_in: torch.Tensor, k_in: torch.Tensor,
                  v_in: torch.Tensor, q_out: torch.Tensor, past_len, stream=None) -> torch.Tensor:
         """QK-norm + RoPE of q and the new k, fp16 store of k and v at row pastLen

@@ -88,9 +88,11 @@ int brk_ctx_destroy(brk_ctx *ctx);
 int brk_ctx_check(brk_ctx *ctx, void *stream);
 /* Pre-sizes the split-KV workspace (bytes) so that later calls allocate nothing. */
 int brk_ctx_reserve(brk_ctx *ctx, size_t bytes);
-/* Pre-sizes the context's fp16 staging buffer (bytes), which two paths fill per call: prefill
- * over an int8 cache stages the layer's dequantised rows, 2 * batch * n_kv_heads * rows *
- * head_dim * 2 bytes with rows = max over the batch of past_len + n_tokens - kv_offset; non-
+/* Pre-sizes the context's fp16 staging buffer (bytes), which three paths fill per call:
+ * brk_attn_prefill_step over an fp16 cache (8+ tokens) stages the rotated q, 2 * batch *
+ * n_tokens * n_heads * head_dim bytes; prefill over an int8 cache stages the layer's
+ * dequantised rows, 2 * batch * n_kv_heads * rows * head_dim * 2 bytes with rows = max over
+ * the batch of past_len + n_tokens - kv_offset; non-
  * causal attention stages its K/V (and, for head dims other than 64 / 128 / 256, q and out):
  * 4 * batch * n_kv_heads * kv_len * Dp + 8 * batch * n_tokens * n_heads * Dp + 256 bytes with
  * Dp the head dim rounded up to 64 / 128 / 256 (the q term only when Dp != head_dim).  A call
@@ -222,12 +224,20 @@ int brk_attn_decode_static(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_
 int brk_attn_prefill(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p,
                      int batch, int n_tokens, const int32_t *past_len, const float *q, float *out,
                      void *stream);
+/* The same with q already rotated and rounded to fp16 (IEEE half bits, [B][T][Hq][D], 16-byte
+ * aligned), which the kernel loads with TMA instead of staging it (the form brk_attn_prefill_step
+ * uses for fp16 caches).  fp16 caches only. */
+int brk_attn_prefill_h(brk_ctx *ctx, const brk_kv *kv, int layer, const brk_attn_params *p,
+                       int batch, int n_tokens, const int32_t *past_len, const uint16_t *q16, float *out,
+                       void *stream);
 
 /* One prefill chunk of a layer's attention slice (recordLayerKV, kernels.ts:1707-1731, as the
  * chunked prefill of lfm2Model.ts:320-333): K/V appended as by brk_attn_append, then the
- * tensor-core kernel with the q prologue (QK-norm + RoPE in f32; q only feeds the fp16
- * tensor-core operand) fused into its q staging, so the rotated q never round-trips through HBM.
- * The cache rows equal brk_attn_append's bit for bit.  head_dim 64 or 128.
+ * tensor-core kernel.  q gets QK-norm + RoPE in f32 (q only feeds the fp16 tensor-core operand):
+ * for an fp16 cache and 8+ tokens in the append kernel, which leaves it as fp16 rows in the
+ * context's staging buffer for the tensor-core kernel's TMA loads; otherwise inside the
+ * tensor-core kernel's q staging.  The cache rows equal brk_attn_append's bit for bit.  head_dim
+ * 64 or 128.
  * q_in [B][T][Hq][D], k_in / v_in [B][T][Hkv][D] f32 projections; out [B][T][Hq][D] f32. */
 int brk_attn_prefill_step(brk_ctx *ctx, brk_kv *kv, int layer, const brk_attn_params *p,
                           int batch, int n_tokens, const int32_t *past_len, const float *q_in,

@@ -128,3 +128,63 @@ def test_prefill_step_fused_prologue_matches(eng, D, norm, one_plus):
         assert torch.equal(ka.view(torch.int16), kb.view(torch.int16))
         assert torch.equal(va.view(torch.int16), vb.view(torch.int16))
     kv_a.close(), kv_b.close(), rope.close()
+
+
+@pytest.mark.parametrize("name,Hq,Hkv,D,pasts,T,softcap,window", [
+    ("h_d128", 32, 8, 128, [0, 1000, 37], 300, 0.0, 0),
+    ("h_gqa7_d64", 14, 2, 64, [513, 0], 257, 0.0, 0),
+    ("h_win_cap", 16, 4, 128, [700], 384, 30.0, 200),
+])
+def test_prefill_half_q_matches_oracle(eng, name, Hq, Hkv, D, pasts, T, softcap, window):
+    """brk_attn_prefill_h: q given as fp16 rows and loaded by TMA (both streams' tiles, a lone
+    stream at an odd GQA group's last tile, tiles past the chunk's end) against attentionCpu on the
+    same fp16-rounded q and K/V."""
+    import torch
+    from brimkern_b200.engine import AttnConfig, KvCache
+    rng = np.random.default_rng(zlib.crc32(name.encode()))
+    B = len(pasts)
+    rows = max(pasts) + T
+    kv = KvCache(eng.ctx, 1, B, Hkv, D, rows)
+    ks, vs = [], []
+    for b in range(B):
+        k = normal(rng, rows, Hkv, D)
+        v = normal(rng, rows, Hkv, D)
+        kv.write_rows(0, b, 0, torch.from_numpy(k).to(eng.device), torch.from_numpy(v).to(eng.device))
+        ks.append(f16_round(k))
+        vs.append(f16_round(v))
+    q = f16_round(normal(rng, B, T, Hq, D))
+    q16 = torch.from_numpy(q).to(eng.device).half()
+    out = torch.full((B, T, Hq, D), float("nan"), dtype=torch.float32, device=eng.device)
+    cfg = AttnConfig(Hq, Hkv, D, softcap=softcap, window=window)
+    eng.prefillHalfQ(kv, 0, cfg, q16, out, pasts)
+    eng.ctx.check()
+    got = out.cpu().numpy()
+    kv.close()
+    refs, _ = O.attention_batch(q.ravel(), np.stack(ks).ravel(), np.stack(vs).ravel(), B, rows * Hkv * D, T, Hq, Hkv,
+                                D, pasts, None, softcap, window)
+    assert_close(got.ravel(), refs, what=name)
+
+
+def test_prefill_step_short_chunk_uses_fused_prologue(eng):
+    """brk_attn_prefill_step with fewer than 8 tokens (the q prologue inside the prefill kernel)
+    against append + prefill on the append's rotated q."""
+    import torch
+    from brimkern_b200.engine import AttnConfig, KvCache, RopeTable
+    rng = np.random.default_rng(5)
+    Hq, Hkv, D, T, pasts = 8, 2, 128, 5, [40, 0]
+    dev = eng.device
+    qn = torch.from_numpy((1 + 0.02 * rng.standard_normal(D)).astype(np.float32)).to(dev)
+    rope = RopeTable(eng.ctx, D, 1e6, None, max(pasts) + T)
+    cfg = AttnConfig(Hq, Hkv, D, q_norm=qn, k_norm=qn, rope=rope)
+    q = torch.from_numpy(normal(rng, 2, T, Hq, D)).to(dev)
+    k = torch.from_numpy(normal(rng, 2, T, Hkv, D)).to(dev)
+    v = torch.from_numpy(normal(rng, 2, T, Hkv, D)).to(dev)
+    kv_a = KvCache(eng.ctx, 1, 2, Hkv, D, max(pasts) + T)
+    kv_b = KvCache(eng.ctx, 1, 2, Hkv, D, max(pasts) + T)
+    q_rot, out_a, out_b = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
+    eng.appendKv(kv_a, 0, cfg, q, k, v, q_rot, pasts)
+    eng.recAttention(kv_a, 0, cfg, q_rot, out_a, pasts, kernel="prefill")
+    eng.prefillStep(kv_b, 0, cfg, q, k, v, out_b, pasts)
+    eng.ctx.check()
+    assert_close(out_b.cpu().numpy(), out_a.cpu().numpy(), what="short chunk")
+    kv_a.close(), kv_b.close(), rope.close()
