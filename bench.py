@@ -323,7 +323,8 @@ def run_prefill(args, c, workload, eng=None, emit=True):
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": sus, "unit": "TFLOP/s",
                          "frac": round(achieved / sus, 4), "frac_of_burst": round(achieved / burst, 4),
                          "traffic": None, "peak_kind": kind + " sustained bf16 (fp16 runs at the same rate)",
-                         "kernel": "prefill_attn_kernel", "timing": f"CUDA events around each prefill launch, {rsteps} steps",
+                         "kernel": "prefill_attn_kernel", "timing": (f"CUDA events around each prefill launch, {rsteps} steps; q given pre-rotated "
+                                    + ("as f32 rows it stages" if q8 else "as fp16 rows it loads with TMA, as in the step")),
                          "flops_per_step": step_flops, "kernel_ms_per_step": round(kern_ms, 4)},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
         }
