@@ -445,31 +445,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 const float mraw = max_tree(v);
                 const float mt = mraw == -CUDART_INF_F ? -CUDART_INF_F : score_log2<CAP>(mraw, a);
+                // The row's max is raised when a tile's max exceeds it by more than 2^8 (or on its
+                // first finite score); O_s (and l) of the row are then rescaled, except on that first
+                // raise.  Rows decide separately, but tcgen05.ld / st / wait are warp-collective
+                // (.sync.aligned), so the whole warp runs the rescale pass when any of its rows needs
+                // it, the other rows with factor 1.
+                const bool raise = mt > m_used + kRescaleLog2 || (m_used == -CUDART_INF_F && mt != -CUDART_INF_F);
+                const bool rescale = raise && m_used != -CUDART_INF_F && j >= 1;
                 bool waited_o = false;
-                if (mt > m_used + kRescaleLog2 || (m_used == -CUDART_INF_F && mt != -CUDART_INF_F)) {
-                    if (m_used != -CUDART_INF_F && j >= 1) {
-                        // Rescale O_s (and l) to the new max once PV_s(j-1) has landed.
-                        if (!mbar_wait(&bars[kBarODone + s], (j - 1) & 1, a.err, kErrMmaTimeout)) {
-                            ok = false;
-                            break;
-                        }
-                        waited_o = true;
-                        tc_fence_after();
-                        const float alpha = ex2_fast(m_used - mt);
-#pragma unroll 1
-                        for (int c = 0; c < D / 32; ++c) {
-                            uint32_t o[32];
-                            tc_ld32_nowait(tO + c * 32, o);
-                            tc_wait_ld();
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                            tc_st32(tO + c * 32, o);
-                        }
-                        tc_wait_st();
-                        l_run *= alpha;
+                if (__any_sync(0xffffffffu, rescale)) {
+                    // ... once PV_s(j-1) has landed (j >= 1 for the whole warp: j is uniform).
+                    const bool got = mbar_wait(&bars[kBarODone + s], (j - 1) & 1, a.err, kErrMmaTimeout);
+                    if (!__all_sync(0xffffffffu, got)) {
+                        ok = false;
+                        break;
                     }
-                    m_used = mt;
+                    waited_o = true;
+                    tc_fence_after();
+                    const float alpha = rescale ? ex2_fast(m_used - mt) : 1.f;
+#pragma unroll 1
+                    for (int c = 0; c < D / 32; ++c) {
+                        uint32_t o[32];
+                        tc_ld32_nowait(tO + c * 32, o);
+                        tc_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                        tc_st32(tO + c * 32, o);
+                    }
+                    tc_wait_st();
+                    l_run *= alpha;
                 }
+                if (raise) m_used = mt;
                 const float m_eff = m_used == -CUDART_INF_F ? 0.f : m_used;
                 // P_s as packed fp16 in registers first, so that the exponentials overlap the
                 // tensor core's PV_s(j-1); only the stores wait for it to stop reading P_s.
@@ -510,26 +516,36 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_st32(tP, pk);
                 // Keys past the range end: zero their V rows so that 0 * (stale data) stays 0
                 // (stream 0's warpgroup does it; stream 1's PV of this tile also waits for P_0).
-                if (s == 0 && kbase + kTK > khi && r < kTK && kbase + r >= khi) {
-                    if (!mbar_wait(&bars[kBarKvFull + j % L::kStages], (j / L::kStages) & 1, a.err, kErrTmaTimeout)) {
+                // (Only some lanes zero a row; the warp leaves together on a timeout, since the
+                // warp-collective tcgen05 instructions below need every lane.)
+                if (s == 0 && kbase + kTK > khi) {
+                    bool zok = true;
+                    if (r < kTK && kbase + r >= khi) {
+                        zok = mbar_wait(&bars[kBarKvFull + j % L::kStages], (j / L::kStages) & 1, a.err, kErrTmaTimeout);
+                        if (zok) {
+#pragma unroll
+                            for (int blk = 0; blk < L::kBlocks; ++blk)
+#pragma unroll
+                                for (int c = 0; c < 8; ++c)
+                                    *reinterpret_cast<uint4 *>(sV(j % L::kStages) + blk * L::kKVBlock + sw128(r, c)) =
+                                        make_uint4(0u, 0u, 0u, 0u);
+                        }
+                    }
+                    if (!__all_sync(0xffffffffu, zok)) {
                         ok = false;
                         break;
                     }
-#pragma unroll
-                    for (int blk = 0; blk < L::kBlocks; ++blk)
-#pragma unroll
-                        for (int c = 0; c < 8; ++c)
-                            *reinterpret_cast<uint4 *>(sV(j % L::kStages) + blk * L::kKVBlock + sw128(r, c)) =
-                                make_uint4(0u, 0u, 0u, 0u);
+                    fence_proxy_async_smem();  // the zeroed V rows
                 }
-                if (s == 0 && kbase + kTK > khi) fence_proxy_async_smem();  // the zeroed V rows
                 tc_wait_st();
                 tc_fence_before();
                 mbar_arrive(&bars[kBarPFull + s]);
                 if (s == 0 && j == 0) mbar_arrive(&bars[kBarStagger]);
                 l_run += rsum;
             }
-            if (ok && nk > 0 && mbar_wait(&bars[kBarODone + s], (nk - 1) & 1, a.err, kErrMmaTimeout)) {
+            bool fin = ok && nk > 0;
+            if (fin) fin = mbar_wait(&bars[kBarODone + s], (nk - 1) & 1, a.err, kErrMmaTimeout);
+            if (__all_sync(0xffffffffu, fin)) {
                 tc_fence_after();
                 const float inv = 1.f / l_run;
                 float *dst = a.out + (((size_t)b * T + (row_ok ? t : 0)) * a.Hq + h) * D;

@@ -188,3 +188,82 @@ def test_prefill_step_short_chunk_uses_fused_prologue(eng):
     eng.ctx.check()
     assert_close(out_b.cpu().numpy(), out_a.cpu().numpy(), what="short chunk")
     kv_a.close(), kv_b.close(), rope.close()
+
+
+def _mixed_rescale_warps(q, ks, pasts, Hq, Hkv, D, scale=None):
+    """How many (sequence, head, warp of 32 query rows, 64-key tile) have rows that disagree on
+    rescaling O at that tile, replaying the kernel's per-row rule on the CPU: a row's max (log2
+    units) is raised when a tile's max exceeds it by more than 8, or on its first finite score,
+    and O is rescaled on every raise but that first one.  Query tiles start at multiples of 128
+    rows, so 32-row warps never straddle two tiles."""
+    B, T = q.shape[0], q.shape[1]
+    G = Hq // Hkv
+    sc = (scale if scale is not None else 1.0 / np.sqrt(D)) * 1.4426950408889634
+    mixed = 0
+    for b in range(B):
+        nkeys = pasts[b] + T
+        ntiles = (nkeys + 63) // 64
+        t = np.arange(T)
+        keys = np.arange(ntiles * 64)
+        valid = keys[None, :] <= pasts[b] + t[:, None]
+        for h in range(Hq):
+            s = q[b, :, h, :].astype(np.float64) @ ks[b][:nkeys, h // G, :].astype(np.float64).T * sc
+            s = np.pad(s, ((0, 0), (0, ntiles * 64 - nkeys)), constant_values=-np.inf)
+            s = np.where(valid, s, -np.inf).reshape(T, ntiles, 64).max(axis=2)
+            m = np.full(T, -np.inf)
+            for j in range(ntiles):
+                mt = s[:, j]
+                first = np.isneginf(m) & ~np.isneginf(mt)
+                raise_ = (mt > m + 8) | first
+                resc = raise_ & ~np.isneginf(m) & (j >= 1)
+                m = np.where(raise_, mt, m)
+                pad = (-T) % 32
+                w = np.pad(resc, (0, pad)).reshape(-1, 32)
+                mixed += int(np.sum(w.any(axis=1) & ~w.all(axis=1)))
+    return mixed
+
+
+@pytest.mark.parametrize("name,Hq,Hkv,D,pasts,T,qscale,half_q", [
+    ("sharp_d128", 8, 2, 128, [0, 300], 256, 4.0, False),
+    ("sharp_d128_h", 8, 2, 128, [0, 300], 256, 4.0, True),
+    ("sharp_gqa7_d64", 14, 2, 64, [0, 129], 200, 4.0, False),
+])
+def test_prefill_sharp_scores_mixed_rescale(eng, name, Hq, Hkv, D, pasts, T, qscale, half_q):
+    """Scores with a wide range (q four times N(0,1), no QK-norm): later key tiles raise some
+    rows' running max by more than 2^8 but not their warp neighbours', so the rows of one warp
+    disagree on rescaling O in TMEM.  The rescale pass uses warp-collective TMEM loads and stores,
+    which the kernel must run with the whole warp (rows that need no rescale take factor 1).  The
+    inputs are checked on the CPU to cause such mixed warps before the GPU result is compared with
+    attentionCpu.  attentionCpu gets q rounded to fp16, the tensor core's operand: at these score
+    ranges that rounding alone moves a few outputs by up to ~4e-3 (a CPU emulation of the kernel's
+    arithmetic gives the same errors), which is not what this test is about."""
+    import torch
+    from brimkern_b200.engine import AttnConfig, KvCache
+    rng = np.random.default_rng(zlib.crc32(name.encode()))
+    B = len(pasts)
+    rows = max(pasts) + T
+    kv = KvCache(eng.ctx, 1, B, Hkv, D, rows)
+    ks, vs = [], []
+    for b in range(B):
+        k = normal(rng, rows, Hkv, D)
+        v = normal(rng, rows, Hkv, D)
+        kv.write_rows(0, b, 0, torch.from_numpy(k).to(eng.device), torch.from_numpy(v).to(eng.device))
+        ks.append(f16_round(k))
+        vs.append(f16_round(v))
+    q = normal(rng, B, T, Hq, D) * np.float32(qscale)
+    if half_q:
+        q = f16_round(q)
+    q_ref = f16_round(q)
+    assert _mixed_rescale_warps(q_ref, ks, pasts, Hq, Hkv, D) > 0, "inputs cause no mixed-rescale warp"
+    out = torch.full((B, T, Hq, D), float("nan"), dtype=torch.float32, device=eng.device)
+    cfg = AttnConfig(Hq, Hkv, D)
+    if half_q:
+        eng.prefillHalfQ(kv, 0, cfg, torch.from_numpy(q).to(eng.device).half(), out, pasts)
+    else:
+        eng.recAttention(kv, 0, cfg, torch.from_numpy(q).to(eng.device), out, pasts, kernel="prefill")
+    eng.ctx.check()
+    got = out.cpu().numpy()
+    kv.close()
+    refs, _ = O.attention_batch(q_ref.ravel(), np.stack(ks).ravel(), np.stack(vs).ravel(), B, rows * Hkv * D, T, Hq,
+                                Hkv, D, pasts)
+    assert_close(got.ravel(), refs, what=name)
