@@ -827,9 +827,10 @@ def run_slice(args, c, workload):
     return 0
 
 
-def decode_config(c, workload, B, world, scaling, launch=None):
+def decode_config(c, workload, B, world, scaling):
     """The `config` object of a decode line, shared by this build's arm and the reference arm so
-    that both name the same workload."""
+    that both name the same workload with the same keys (how the GPU arm launches its kernels is
+    a key of its line, not of the workload)."""
     bytes_step = kv_bytes_per_step(c, B)
     q8 = c.get("kv") == "q8"
     cfg = {"workload": workload, "kv_cache": "int8" if q8 else "fp16", "global_batch": B * world,
@@ -838,8 +839,6 @@ def decode_config(c, workload, B, world, scaling, launch=None):
            "parallelism": (f"batch-sharded x{world}: {B} of {B * world} sequences per GPU, no communication "
                            f"({scaling} scaling)"),
            "l2": f"no flush: each step streams {bytes_step / 1e9:.1f} GB of KV per GPU > 126 MB L2"}
-    if launch:
-        cfg["launch"] = launch
     return cfg
 
 
@@ -1177,8 +1176,8 @@ def main():
             "scaling": args.scaling, "vs_baseline": None,
             "dtype": "int8 KV + f32 row scales / f32 accumulate" if q8 else "f16 KV / f32 accumulate",
             "data": "synthetic",
-            "config": decode_config(c, workload, B, world, args.scaling,
-                                    "host launches" if args.eager else "CUDA-graph replay of the step"),
+            "config": decode_config(c, workload, B, world, args.scaling),
+            "launch": "host launches" if args.eager else "CUDA-graph replay of the step",
             "tokens_per_s": round(tok_s, 1),
             "frac_of_measured_hbm": round(value / world / peak, 4),
             "decode_splits": nsplit,
